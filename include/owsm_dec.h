@@ -1,0 +1,136 @@
+/* C ABI of libowsmdec.so: the OWSM Transformer decoder call (embedding -> L pre-LN layers of masked
+ * self-attention over a per-row KV cache, cross-attention over precomputed encoder K/V and a ReLU FFN ->
+ * final LayerNorm -> vocabulary projection -> argmax, or log-softmax + top-K with a KV-cache reorder)
+ * as one persistent CUDA kernel for sm_100a (B200).
+ *
+ * Plain C types only: device pointers as void*, sizes as int / int64_t, the CUDA stream as void*.
+ * Every function returns OWSM_DEC_OK (0) or a negative error code; no exception crosses the ABI.
+ *
+ * Correspondence with owsm-trt (the Python interface this library replaces):
+ *   owsm_dec_create      <- MegaDecoder.__init__        src/owsm_trt/megakernel.py:548-614
+ *                           (LayerNorm folding :564-570, per-layer weight stacks :577-599)
+ *   owsm_dec_plan        <- MegaDecoder.step_fn scratch src/owsm_trt/megakernel.py:624-650,
+ *                           RingDecoder.step_fn         src/owsm_trt/megakernel_ring.py:794-830
+ *   owsm_dec_step        <- the returned run()          src/owsm_trt/megakernel.py:667-672,
+ *                           megakernel_ring.py:852-853 (pred / notime: :794-799)
+ *   owsm_dec_beam_step   <- run() followed by BeamSession._select step 1 and the cache reorder
+ *                           src/owsm_trt/runtime.py:1399-1413
+ *   owsm_dec_get_error   <- MegaDecoder.check           src/owsm_trt/megakernel.py:616-622
+ */
+#ifndef OWSM_DEC_H
+#define OWSM_DEC_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OWSM_DEC_OK 0
+#define OWSM_DEC_ERR_ARG (-1)      /* invalid argument (shape, pointer, alignment) */
+#define OWSM_DEC_ERR_CUDA (-2)     /* a CUDA runtime call failed */
+#define OWSM_DEC_ERR_TIMEOUT (-3)  /* a bounded in-kernel wait gave up (results of that call are garbage) */
+#define OWSM_DEC_ERR_LIMIT (-4)    /* the call exceeds a supported maximum (rows x window, head size, ...) */
+
+#define OWSM_DEC_F32 0 /* weight element type given to owsm_dec_create */
+#define OWSM_DEC_F16 1
+
+/* Model shapes (OWSMConfig dec_layers, d_model, dec_heads, dec_ffn, vocab_size; src/owsm_trt/config.py:15-30). */
+typedef struct OwsmDecDims {
+  int L, D, H, F, V;
+  int max_pos;  /* rows of the positional table */
+  float eps;    /* LayerNorm eps (1e-12, src/owsm_trt/modeling.py:25) */
+  float xscale; /* embedding scale sqrt(D) (modeling.py:481) */
+} OwsmDecDims;
+
+/* One layer's parameters, device pointers, row-major [out, in] as torch.nn.Linear stores them
+ * (element type = weight_dtype; vectors always fp32). wq/wk/wv are the self-attention projections
+ * (DecoderLayer.self_attn, modeling.py:461-469); if wk == NULL, wq is the fused [3D, D] matrix
+ * (MultiHeadedAttention.fuse_qkv, modeling.py:153-161) and bq the fused bias. */
+typedef struct OwsmDecLayer {
+  const void *wq, *wk, *wv;
+  const float *bq, *bk, *bv;
+  const void* wo;
+  const float* bo;
+  const void* wcq; /* src_attn.linear_q */
+  const float* bcq;
+  const void* wco; /* src_attn.linear_out */
+  const float* bco;
+  const void* w1; /* feed_forward.w_1 [F, D] */
+  const float* b1;
+  const void* w2; /* feed_forward.w_2 [D, F] */
+  const float* b2;
+  const float *ln1_g, *ln1_b, *ln2_g, *ln2_b, *ln3_g, *ln3_b;
+} OwsmDecLayer;
+
+typedef struct OwsmDecWeights {
+  int weight_dtype;         /* OWSM_DEC_F32 or OWSM_DEC_F16 */
+  const void* emb;          /* [V, D] */
+  const float* pe;          /* [max_pos, D] positional table (fp32) */
+  const OwsmDecLayer* layers; /* host array of L */
+  const float *lnf_g, *lnf_b; /* after_norm */
+  const void* wout;         /* output_layer [V, D] */
+  const float* bout;
+} OwsmDecWeights;
+
+typedef struct OwsmDec OwsmDec;         /* packed weights on one device */
+typedef struct OwsmDecPlan OwsmDecPlan; /* scratch + schedule for one call shape */
+
+/* Pack the weights (LayerNorms folded into the following GEMMs, fp16, tensor-core fragment order) on
+ * `device`. The given buffers may be freed afterwards. `programs` = CTAs of the persistent kernel
+ * (0: one per SM). */
+int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device, int programs, OwsmDec** out);
+void owsm_dec_destroy(OwsmDec* h);
+
+/* Shapes of a call: R rows x S new tokens, self-KV cache capacity C, T encoder frames; cross K/V hold
+ * R / rows_per_utt utterances (rows_per_utt = 1: one per row, owsm-trt's layout; = beam: the beam
+ * hypotheses of an utterance read its K/V once). beam > 0 prepares owsm_dec_beam_step with that beam
+ * (R = batch * beam, utterance-major). Allocates the call's scratch on the handle's device. */
+int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out);
+void owsm_dec_plan_destroy(OwsmDecPlan* p);
+
+/* One decoder call on `stream` (cudaStream_t; NULL = legacy default). Device pointers:
+ *   tokens  int64 [R, S], row stride tok_stride (elements)      offset int64 [R], stride off_stride
+ *   self_k, self_v fp16 [L, R, H, C, dk]: read at slots < offset[r], written at offset[r] .. +S-1
+ *   cross_k, cross_v fp16 [L, R / rows_per_utt, H, T, dk]
+ *   enc_len int32 [R / rows_per_utt] or NULL: frames of each utterance (key-padding mask), clamped to [1, T]
+ *   logits fp32 [R, S, V] (written)    new_kv fp16 [L, 2, R, H, S, dk] (written)
+ *   pred int64 [R, S] or NULL: argmax of the logits (first index on ties)
+ *   notime uint8 [R] or NULL: rows whose argmax leaves out ids first_time..last_time
+ * No host synchronisation; capturable in a CUDA graph (all pointers are fixed in the graph). */
+int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride, const int64_t* offset,
+                  int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
+                  const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
+                  int first_time, int last_time);
+
+/* owsm_dec_step (S = 1) followed by the beam selection of BeamSession._select step 1 over the plan's
+ * batch x beam rows: logp = log_softmax(logits) (fp32), cand = score[r] + logp, inactive rows LOG_ZERO,
+ * top-`beam` of beam x V per utterance (ties: lower flat index) ->
+ *   score fp32 [R] (overwritten with the new scores), parent int64 [R] (row each slot came from),
+ *   token int64 [R]; then self_k / self_v rows are replaced by their parent's rows (slots 0 .. offset+S-1).
+ * active uint8 [R]. */
+int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride,
+                       const int64_t* offset, int64_t off_stride, void* self_k, void* self_v, const void* cross_k,
+                       const void* cross_v, const int32_t* enc_len, float* logits, void* new_kv, float* score,
+                       const uint8_t* active, int64_t* parent, int64_t* token);
+
+/* Read and clear the device error word of the handle's calls (synchronises the device).
+ * Returns OWSM_DEC_OK, OWSM_DEC_ERR_TIMEOUT (a bounded wait gave up) or OWSM_DEC_ERR_CUDA. */
+int owsm_dec_get_error(OwsmDec* h);
+
+/* Reset a plan's inter-CTA counters after a failed call (synchronises the device). */
+int owsm_dec_plan_reset(OwsmDecPlan* p);
+
+/* Plan facts for callers and tests: programs (CTAs), ring slots, bytes of scratch. */
+int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int64_t* scratch_bytes);
+
+/* Testing hook: the in-kernel wait limit (polls) of later calls on this handle; 0 restores the default. */
+int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
+
+/* Last CUDA / argument error message of this thread ("" if none). */
+const char* owsm_dec_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* OWSM_DEC_H */

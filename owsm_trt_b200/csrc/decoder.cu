@@ -1,0 +1,1591 @@
+// The OWSM decoder call as one persistent kernel for sm_100a, and the C ABI around it (include/owsm_dec.h).
+//
+// Semantics: owsm-trt's Decoder.step (src/owsm_trt/modeling.py:501-560) with the megakernel's in-kernel
+// cache write (src/owsm_trt/megakernel.py:321-326), fused argmax (src/owsm_trt/megakernel_ring.py:437-500)
+// and BeamSession._select step 1 + cache reorder (src/owsm_trt/runtime.py:1399-1413).
+//
+// Execution model (one CTA per SM, all co-resident: cooperative launch):
+//   * warp 8 of every CTA is the producer: lane 0 walks the CTA's whole sequence of input byte ranges for
+//     the call (its GEMM weight row blocks, the KV-cache rows of its self-attention units, the encoder K/V
+//     frames of its cross-attention pieces) and copies them with cp.async.bulk into a ring of 32 KB
+//     shared-memory slots, running ahead of the computation across the stage boundaries, so HBM streams
+//     while the CTAs wait for each other.
+//   * warps 0-7 consume the slots stage by stage; between stages a bounded grid barrier.
+//   * stages: embedding; per layer LN1+QKV, self-attention, out-proj+residual, LN2+cross-Q,
+//     cross-attention, cross-out+residual, LN3+FFN1+ReLU, FFN2+residual; final LN + vocabulary projection
+//     (+ argmax or per-CTA log-softmax / top-K partials); for beam calls: selection, cache reorder (2 stages).
+//   * GEMMs: y[token, n] = sum_k W[n, k] x[token, k] with mma.sync m16n8k16 (fp16 in, fp32 accumulate),
+//     weights as the 16-row A operand, prepacked in fragment order so each lane loads 16 contiguous bytes;
+//     LayerNorm folded into the weights (W*gamma, b + W beta) and the normalised activations computed by
+//     every CTA that needs them from the fp32 residual stream.
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/owsm_dec.h"
+#include "ptx.cuh"
+
+namespace owsm {
+
+constexpr int DK = 64;                 // head size (every OWSM model)
+constexpr int NWARP = 8;               // consumer warps
+constexpr int NTHR = NWARP * 32;       // consumer threads
+constexpr int BLOCK = NTHR + 32;       // + producer warp
+constexpr int SLOT = 32768;            // ring slot bytes
+constexpr int MAXSLOT = 8;
+constexpr int MAXNT = 8;               // n-tiles of 8 tokens: M <= 64 tokens per call
+constexpr int MAXQ = 16;               // queries of one attention unit
+constexpr int KTOP = 8;                // largest beam
+constexpr int APOS = SLOT / (DK * 2);  // attention positions per chunk (256)
+constexpr uint32_t DEFAULT_SPIN = 1u << 22;
+
+enum Gemm { G_QKV = 0, G_WO, G_CQ, G_WCO, G_F1, G_F2, G_OUT, NGEMM };
+enum { E_ERR_TIMEOUT = 1 };
+
+struct GemmW {
+  const uint4* w;   // packed fragments: [layer][block][kblock][lane] of 16 bytes
+  const float* b;   // [layer][N]
+  int N, K, NB;     // output rows, input features, 16-row blocks
+  long long lstride;  // uint4 elements per layer
+};
+
+struct PlanDev {
+  int L, D, H, F, V, max_pos;
+  float eps, xscale;
+  int R, S, M, NT, C, T, G, U, beam, P, nslot;
+  uint32_t max_spin;
+  const __half* emb;
+  const float* pe;
+  GemmW g[NGEMM];
+  const int* goff[NGEMM];  // [P + 1]
+  const int* gblk[NGEMM];
+  float* x;       // [M][D] residual stream
+  __half* qkv;    // [M][3D]
+  __half* q2;     // [M][D]
+  __half* oB;     // attention outputs, B-fragment order [D/16][NT][32][4]
+  __half* hB;     // FFN hidden, B-fragment order [F/16][NT][32][4]
+  float* xpart;   // cross-attention partials [U*H][P][Q][66]
+  uint32_t* xcnt; // [U*H]
+  float* amax;    // [P][M]
+  int* aidx;      // [P][M]
+  float* lmax;    // [P][M]
+  float* lsum;    // [P][M]
+  float* topv;    // [P][M][KTOP]
+  int* topi;      // [P][M][KTOP]
+  uint32_t* ctr;  // [0] grid barrier, [1] exits, [2] argmax arrivals
+  int* err;
+  __half* tmpk;   // reorder staging [L][R][H][C][DK]
+  __half* tmpv;
+  int Qmax;           // queries of the largest attention unit
+  int off_pre, off_out, off_ring, off_work;  // shared-memory layout (bytes)
+};
+
+struct CallArgs {
+  const int64_t* tok;
+  int64_t tok_stride;
+  const int64_t* off;
+  int64_t off_stride;
+  __half* kc;
+  __half* vc;
+  const __half* ck;
+  const __half* cv;
+  const int32_t* enc_len;
+  float* logits;
+  __half* new_kv;
+  int64_t* pred;
+  const uint8_t* notime;
+  int ft, lt;
+  float* score;
+  const uint8_t* active;
+  int64_t* parent;
+  int64_t* token;
+  int beam_mode;
+};
+
+// ------------------------------------------------------------------------------------------------ helpers
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NTHR) : "memory"); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ int row_off(const PlanDev& pd, const CallArgs& a, int r) {
+  long long o = a.off[(long long)r * a.off_stride];
+  long long hi = pd.C - pd.S;
+  return (int)(o < 0 ? 0 : (o > hi ? hi : o));
+}
+
+__device__ __forceinline__ int utt_len(const PlanDev& pd, const CallArgs& a, int u) {
+  int t = a.enc_len ? a.enc_len[u] : pd.T;
+  return t < 1 ? 1 : (t > pd.T ? pd.T : t);
+}
+
+// Half index of element (token m, feature k) in B-fragment order with NT n-tiles.
+__device__ __forceinline__ long long bfrag_idx(int m, int k, int NT) {
+  int kb = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
+  int reg = kk >> 3, t = (kk & 7) >> 1, e = kk & 1;
+  return ((((long long)kb * NT + nt) * 32 + (g * 4 + t)) * 4) + reg * 2 + e;
+}
+
+// The frame-space partition of cross-attention: frames of all (utterance, head) segments in a row,
+// split in P contiguous ranges (P = min(CTAs, frames), so no range is empty).
+struct Frames {
+  long long total;
+  int U, H, P;
+  const int* pre;  // [U + 1] prefix sums of utterance lengths (shared memory)
+  __device__ long long bound(int c) const { return c >= P ? total : (long long)c * total / P; }
+  __device__ int owner(long long f) const {  // the CTA whose range holds frame f
+    int lo = 0, hi = P - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (bound(mid) <= f) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
+  __device__ int utt_of(long long f) const {  // utterance of flat frame f
+    int lo = 0, hi = U - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if ((long long)H * pre[mid] <= f) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+  }
+};
+
+// One piece of a CTA's cross-attention range: segment (u, h) frames [t0, t1).
+struct Piece {
+  int u, h, t0, t1;
+};
+
+__device__ __forceinline__ bool next_piece(const Frames& fr, long long& f, long long end, Piece& p) {
+  if (f >= end) return false;
+  int u = fr.utt_of(f);
+  int len = fr.pre[u + 1] - fr.pre[u];
+  long long base = (long long)fr.H * fr.pre[u];
+  int h = (int)((f - base) / len);
+  int t0 = (int)(f - base - (long long)h * len);
+  long long t1 = t0 + (end - f);
+  if (t1 > len) t1 = len;
+  p.u = u; p.h = h; p.t0 = t0; p.t1 = (int)t1;
+  f += t1 - t0;
+  return true;
+}
+
+// ------------------------------------------------------------------------------------------------ stages
+// Stage index g: 0 embed; 1 + 8 l + i for i in (QKV, SATT, WO, CQ, XATT, WCO, F1, F2); 8 L + 1 output;
+// beam calls: 8 L + 2 select, 8 L + 3 reorder A, 8 L + 4 reorder B.
+enum Kind { K_EMBED, K_QKV, K_SATT, K_WO, K_CQ, K_XATT, K_WCO, K_F1, K_F2, K_OUT, K_SELECT, K_REORD_A, K_REORD_B };
+
+__device__ __forceinline__ Kind stage_kind(const PlanDev& pd, int g, int& layer) {
+  layer = 0;
+  if (g == 0) return K_EMBED;
+  if (g <= 8 * pd.L) {
+    layer = (g - 1) >> 3;
+    return (Kind)(K_QKV + ((g - 1) & 7));
+  }
+  int i = g - 8 * pd.L - 1;
+  return (Kind)(K_OUT + i);
+}
+
+__device__ __forceinline__ int gemm_of(Kind k) {
+  switch (k) {
+    case K_QKV: return G_QKV;
+    case K_WO: return G_WO;
+    case K_CQ: return G_CQ;
+    case K_WCO: return G_WCO;
+    case K_F1: return G_F1;
+    case K_F2: return G_F2;
+    case K_OUT: return G_OUT;
+    default: return -1;
+  }
+}
+
+// Chunk enumeration shared by the producer (issues the copies) and the consumer (waits for them):
+// calls f(src, bytes) for every chunk of stage g on CTA c, in consumption order.
+template <class Fn>
+__device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& fr, int g, int c, Fn&& f) {
+  int layer;
+  Kind k = stage_kind(pd, g, layer);
+  int gi = gemm_of(k);
+  if (gi >= 0) {
+    const GemmW& gw = pd.g[gi];
+    int l = (k == K_OUT) ? 0 : layer;
+    int kbs = gw.K >> 4;
+    int kpc = kbs < (SLOT / 512) ? kbs : (SLOT / 512);  // k-blocks per chunk
+    for (int i = pd.goff[gi][c]; i < pd.goff[gi][c + 1]; ++i) {
+      int rb = pd.gblk[gi][i];
+      const uint4* base = gw.w + (long long)l * gw.lstride + (long long)rb * kbs * 32;
+      for (int kb0 = 0; kb0 < kbs; kb0 += kpc) {
+        int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
+        f((const void*)(base + (long long)kb0 * 32), (uint32_t)n * 512);
+      }
+    }
+    return;
+  }
+  if (k == K_SATT) {
+    for (int u = c; u < pd.R * pd.H; u += pd.P) {
+      int b = u / pd.H, h = u % pd.H;
+      int off = row_off(pd, a, b);
+      long long base = ((((long long)layer * pd.R + b) * pd.H + h) * pd.C) * DK;
+      for (int j0 = 0; j0 < off; j0 += APOS) {
+        int n = off - j0 < APOS ? off - j0 : APOS;
+        f((const void*)(a.kc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+        f((const void*)(a.vc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+      }
+    }
+    return;
+  }
+  if (k == K_XATT) {
+    long long f0 = fr.bound(c), f1 = fr.bound(c + 1);
+    Piece p;
+    while (next_piece(fr, f0, f1, p)) {
+      long long base = ((((long long)layer * pd.U + p.u) * pd.H + p.h) * pd.T) * DK;
+      for (int j0 = p.t0; j0 < p.t1; j0 += APOS) {
+        int n = p.t1 - j0 < APOS ? p.t1 - j0 : APOS;
+        f((const void*)(a.ck + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+        f((const void*)(a.cv + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+      }
+    }
+  }
+}
+
+struct Ring {
+  uint64_t* full;
+  uint64_t* empty;
+  uint8_t* data;
+  int ns;
+  uint32_t i;     // chunks consumed so far
+  uint32_t spin;
+  int* err;
+  bool dead;
+  __device__ uint8_t* wait() {
+    int s = i % ns;
+    if (!dead && !mbar_wait(&full[s], (i / ns) & 1, spin)) {
+      dead = true;
+      atomicExch(err, E_ERR_TIMEOUT);
+    }
+    return data + (size_t)s * SLOT;
+  }
+  __device__ void release() {  // by every consumer warp after its last read of the slot
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[i % ns]);
+    ++i;
+  }
+};
+
+// Grid barrier: all P CTAs arrive after their stage; bounded wait; the counter resets at kernel exit.
+__device__ void grid_sync(const PlanDev& pd, uint32_t target, bool& dead) {
+  csync();
+  if (threadIdx.x == 0) {
+    red_release_add(&pd.ctr[0], 1);
+    if (!dead && !*(volatile int*)pd.err) {
+      uint32_t n = 0;
+      while ((int)(ld_acquire(&pd.ctr[0]) - target) < 0) {
+        if (++n > pd.max_spin) {
+          atomicExch(pd.err, E_ERR_TIMEOUT);
+          dead = true;
+          break;
+        }
+      }
+    }
+  }
+  csync();
+}
+
+// ------------------------------------------------------------------------------------------------ GEMM
+struct Work {  // shared-memory work area, carved per stage
+  uint8_t* p;
+};
+
+// LayerNorm of the residual stream x [M][D] (eps) into B-fragment order (fp16) in shared memory.
+__device__ void ln_to_frag(const PlanDev& pd, __half* bbuf) {
+  const int D = pd.D, M = pd.M, NT = pd.NT;
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // zero the padding tokens' fragments
+  for (int m = M + warp; m < NT * 8; m += NWARP)
+    for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
+  for (int m = warp; m < M; m += NWARP) {
+    const float* xr = pd.x + (long long)m * D;
+    float s = 0.f;
+    for (int k = lane; k < D; k += 32) s += __ldcg(xr + k);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    float mean = s / D;
+    float v = 0.f;
+    for (int k = lane; k < D; k += 32) {
+      float d = __ldcg(xr + k) - mean;
+      v += d * d;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    float rstd = rsqrtf(v / D + pd.eps);
+    for (int k = lane * 2; k < D; k += 64) {
+      float2 xv = __ldcg(reinterpret_cast<const float2*>(xr + k));
+      __half2 hv = __floats2half2_rn((xv.x - mean) * rstd, (xv.y - mean) * rstd);
+      *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) = hv;
+    }
+  }
+}
+
+struct OutState {  // per-token running results of the output stage (shared memory)
+  float* amax;
+  int* aidx;
+  float* rmax;
+  float* rsum;
+  float* topv;  // [M][KTOP]
+  int* topi;
+  float* tile;  // [16][M] values of the current row block
+};
+
+__device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, Kind kind, int layer, int c,
+                           uint8_t* work, OutState& os) {
+  const int gi = gemm_of(kind);
+  const GemmW& gw = pd.g[gi];
+  const int nb0 = pd.goff[gi][c], nb1 = pd.goff[gi][c + 1];
+  if (nb0 == nb1) return;
+  const int NT = pd.NT, M = pd.M;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool ln = (kind == K_QKV || kind == K_CQ || kind == K_F1 || kind == K_OUT);
+  const int l = (kind == K_OUT) ? 0 : layer;
+  __half* bbuf = reinterpret_cast<__half*>(work);
+  float* red = reinterpret_cast<float*>(work + (ln ? (size_t)NT * (pd.D / 16) * 256 : 0));
+  const __half* gsrc = (kind == K_F2) ? pd.hB : pd.oB;
+  if (ln) {
+    ln_to_frag(pd, bbuf);
+    csync();
+  }
+  const int kbs = gw.K >> 4;
+  const int kpc = kbs < (SLOT / 512) ? kbs : (SLOT / 512);
+  const float* bias = gw.b + (long long)l * gw.N;
+  for (int i = nb0; i < nb1; ++i) {
+    const int rb = pd.gblk[gi][i];
+    float acc[MAXNT][4];
+#pragma unroll
+    for (int nt = 0; nt < MAXNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    for (int kb0 = 0; kb0 < kbs; kb0 += kpc) {
+      const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
+      const uint4* slot = reinterpret_cast<const uint4*>(ring.wait());
+      for (int kb = warp; kb < n; kb += NWARP) {
+        uint4 af = slot[kb * 32 + lane];
+        const int kg = kb0 + kb;
+#pragma unroll
+        for (int nt = 0; nt < MAXNT; ++nt) {
+          if (nt < NT) {
+            uint2 bf;
+            long long bi = (((long long)kg * NT + nt) * 32 + lane) * 4;
+            if (ln) bf = *reinterpret_cast<const uint2*>(bbuf + bi);
+            else bf = __ldcg(reinterpret_cast<const uint2*>(gsrc + bi));
+            mma16816(acc[nt], af, bf.x, bf.y);
+          }
+        }
+      }
+      ring.release();
+    }
+    // reduce over warps
+#pragma unroll
+    for (int nt = 0; nt < MAXNT; ++nt)
+      if (nt < NT)
+        *reinterpret_cast<float4*>(&red[((warp * NT + nt) * 32 + lane) * 4]) =
+            make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+    csync();
+    const int tid = threadIdx.x;
+    if (kind == K_OUT && a.beam_mode) {
+      // values of the block to the tile [16][M], then one thread per token merges them
+      if (tid < NT * 32) {
+        int nt = tid >> 5, ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int w = 0; w < NWARP; ++w) {
+          float4 q = *reinterpret_cast<const float4*>(&red[((w * NT + nt) * 32 + ln2) * 4]);
+          v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+        }
+        for (int e = 0; e < 4; ++e) {
+          int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+          if (m < M) {
+            float y = v[e] + (n < gw.N ? bias[n] : 0.f);
+            if (n < pd.V) a.logits[(long long)m * pd.V + n] = y;
+            os.tile[row * M + m] = (n < pd.V) ? y : -INFINITY;
+          }
+        }
+      }
+      csync();
+      if (tid < M) {
+        int m = tid;
+        float mx = os.rmax[m], sm = os.rsum[m];
+        float bmx = mx;
+        for (int row = 0; row < 16; ++row) bmx = fmaxf(bmx, os.tile[row * M + m]);
+        if (bmx > -INFINITY) {
+          sm = (mx > -INFINITY ? sm * expf(mx - bmx) : 0.f);
+          for (int row = 0; row < 16; ++row) {
+            float y = os.tile[row * M + m];
+            if (y > -INFINITY) sm += expf(y - bmx);
+          }
+          os.rmax[m] = bmx;
+          os.rsum[m] = sm;
+        }
+        float* tv = os.topv + m * KTOP;
+        int* ti = os.topi + m * KTOP;
+        for (int row = 0; row < 16; ++row) {
+          float y = os.tile[row * M + m];
+          int n = rb * 16 + row;
+          if (!(y > tv[KTOP - 1])) continue;  // ties keep the earlier (lower) index
+          int j = KTOP - 1;
+          while (j > 0 && y > tv[j - 1]) { tv[j] = tv[j - 1]; ti[j] = ti[j - 1]; --j; }
+          tv[j] = y; ti[j] = n;
+        }
+      }
+      csync();
+      continue;
+    }
+    if (tid < NT * 32) {
+      const int nt = tid >> 5, ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w = 0; w < NWARP; ++w) {
+        float4 q = *reinterpret_cast<const float4*>(&red[((w * NT + nt) * 32 + ln2) * 4]);
+        v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+      }
+      float best[2] = {-INFINITY, -INFINITY};
+      int besti[2] = {0x7fffffff, 0x7fffffff};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+        if (m >= M || n >= gw.N) continue;
+        float y = v[e] + bias[n];
+        switch (kind) {
+          case K_QKV: pd.qkv[(long long)m * 3 * pd.D + n] = __float2half_rn(y); break;
+          case K_CQ: pd.q2[(long long)m * pd.D + n] = __float2half_rn(y); break;
+          case K_F1: pd.hB[bfrag_idx(m, n, NT)] = __float2half_rn(fmaxf(y, 0.f)); break;
+          case K_WO: case K_WCO: case K_F2: {
+            float* xp = pd.x + (long long)m * pd.D + n;
+            *xp = __ldcg(xp) + y;
+            break;
+          }
+          case K_OUT: {
+            a.logits[(long long)m * pd.V + n] = y;
+            float ya = y;
+            if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
+            int s = e & 1;
+            if (ya > best[s] || (ya == best[s] && n < besti[s])) { best[s] = ya; besti[s] = n; }
+            break;
+          }
+          default: break;
+        }
+      }
+      if (kind == K_OUT) {
+        // reduce over the 8 row groups (lanes with the same t), then merge into the running best
+#pragma unroll
+        for (int s = 0; s < 2; ++s) {
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, best[s], o);
+            int oi = __shfl_xor_sync(0xffffffffu, besti[s], o);
+            if (ov > best[s] || (ov == best[s] && oi < besti[s])) { best[s] = ov; besti[s] = oi; }
+          }
+          const int m = nt * 8 + 2 * t + s;
+          if (g == 0 && m < M) {
+            float cur = os.amax[m];
+            int ci = os.aidx[m];
+            if (best[s] > cur || (best[s] == cur && besti[s] < ci)) { os.amax[m] = best[s]; os.aidx[m] = besti[s]; }
+          }
+        }
+      }
+    }
+    csync();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+// Online-softmax attention of Q queries (q_s [Q][64], scaled) over chunks of keys/values; each warp keeps
+// partial outputs for positions j = warp (mod 8) in registers: lane owns dims 2*lane, 2*lane + 1.
+struct AttnAcc {
+  float o[MAXQ][2];
+};
+
+// scores[q][j] = q . K[j] for j < npos (K rows in shared memory, 128 bytes each).
+__device__ __forceinline__ void attn_scores(const float* qs, const __half* kt, int npos, int Q, float* sc) {
+  for (int idx = threadIdx.x; idx < Q * npos; idx += NTHR) {
+    int q = idx / npos, j = idx - q * npos;
+    const uint4* kr = reinterpret_cast<const uint4*>(kt + (long long)j * DK);
+    const float* qq = qs + q * DK;
+    float s = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      int ch = (cc + j) & 7;  // rotate the 16-byte chunk per position: fewer bank conflicts
+      uint4 kv = kr[ch];
+      const __half2* h2 = reinterpret_cast<const __half2*>(&kv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __half22float2(h2[e]);
+        s += f.x * qq[ch * 8 + 2 * e] + f.y * qq[ch * 8 + 2 * e + 1];
+      }
+    }
+    sc[q * APOS + j] = s;
+  }
+}
+
+// Softmax bookkeeping of a chunk: new running max per query, p = exp(s - max) in place, alpha (rescale of
+// the old sums), running sum. `valid(q, j)` masks positions.
+template <class Valid>
+__device__ __forceinline__ void attn_softmax(float* sc, int npos, int Q, float* mrun, float* lrun, float* alpha,
+                                             Valid valid) {
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int q = warp; q < Q; q += NWARP) {
+    float mx = -INFINITY;
+    for (int j = lane; j < npos; j += 32)
+      if (valid(q, j)) mx = fmaxf(mx, sc[q * APOS + j]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float mold = mrun[q];
+    float mnew = fmaxf(mold, mx);
+    float sum = 0.f;
+    for (int j = lane; j < npos; j += 32) {
+      float p = (valid(q, j) && mnew > -INFINITY) ? expf(sc[q * APOS + j] - mnew) : 0.f;
+      sc[q * APOS + j] = p;
+      sum += p;
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      float al = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
+      alpha[q] = al;
+      lrun[q] = lrun[q] * al + sum;
+      mrun[q] = mnew;
+    }
+  }
+}
+
+__device__ __forceinline__ void attn_accum(AttnAcc& acc, const float* sc, const float* alpha, const __half* vt,
+                                           int npos, int Q) {
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < MAXQ; ++q)
+    if (q < Q) { acc.o[q][0] *= alpha[q]; acc.o[q][1] *= alpha[q]; }
+  for (int j = warp; j < npos; j += NWARP) {
+    float2 v = __half22float2(reinterpret_cast<const __half2*>(vt + (long long)j * DK)[lane]);
+#pragma unroll
+    for (int q = 0; q < MAXQ; ++q)
+      if (q < Q) {
+        float p = sc[q * APOS + j];
+        acc.o[q][0] += p * v.x;
+        acc.o[q][1] += p * v.y;
+      }
+  }
+}
+
+// Sum the warps' partial outputs into out[q][64] (shared memory).
+__device__ __forceinline__ void attn_reduce(const AttnAcc& acc, int Q, float* scratch, float* out) {
+  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int q = 0; q < MAXQ; ++q)
+    if (q < Q) {
+      scratch[(warp * Q + q) * DK + 2 * lane] = acc.o[q][0];
+      scratch[(warp * Q + q) * DK + 2 * lane + 1] = acc.o[q][1];
+    }
+  csync();
+  for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
+    int q = idx / DK, d = idx % DK;
+    float s = 0.f;
+    for (int w = 0; w < NWARP; ++w) s += scratch[(w * Q + q) * DK + d];
+    out[q * DK + d] = s;
+  }
+  csync();
+}
+
+struct AttnSmem {
+  float* q;      // [MAXQ][64]
+  float* sc;     // [MAXQ][APOS]
+  float* mrun;   // [MAXQ]
+  float* lrun;
+  float* alpha;
+  float* knew;   // [MAXQ][64] (self-attention: the new keys, fp32)
+  float* out;    // [MAXQ][64]
+  float* scratch;  // [NWARP][MAXQ][64]
+  int* flag;
+};
+
+__device__ AttnSmem carve_attn(uint8_t* work, int Q) {
+  AttnSmem s;
+  float* p = reinterpret_cast<float*>(work);
+  s.q = p; p += Q * DK;
+  s.sc = p; p += Q * APOS;
+  s.mrun = p; p += MAXQ;
+  s.lrun = p; p += MAXQ;
+  s.alpha = p; p += MAXQ;
+  s.knew = p; p += Q * DK;
+  s.out = p; p += Q * DK;
+  s.scratch = p; p += NWARP * Q * DK;
+  s.flag = reinterpret_cast<int*>(p);
+  return s;
+}
+
+// Bytes of carve_attn(Q).
+__host__ __device__ constexpr size_t attn_smem(int Q) {
+  return sizeof(float) * ((size_t)Q * DK * 3 + (size_t)Q * APOS + 3 * MAXQ + (size_t)NWARP * Q * DK) + 16;
+}
+
+__device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, int layer, int c, uint8_t* work) {
+  AttnSmem s = carve_attn(work, pd.Qmax);
+  const int S = pd.S, D = pd.D, H = pd.H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int u = c; u < pd.R * H; u += pd.P) {
+    const int b = u / H, h = u % H;
+    const int off = row_off(pd, a, b);
+    for (int idx = threadIdx.x; idx < S * DK; idx += NTHR) {
+      int q = idx / DK, d = idx % DK;
+      const __half* row = pd.qkv + (long long)(b * S + q) * 3 * D + h * DK + d;
+      s.q[q * DK + d] = __half2float(__ldcg(row)) * 0.125f;
+      s.knew[q * DK + d] = __half2float(__ldcg(row + D));
+    }
+    if (threadIdx.x < S) { s.mrun[threadIdx.x] = -INFINITY; s.lrun[threadIdx.x] = 0.f; }
+    AttnAcc acc;
+#pragma unroll
+    for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
+    csync();
+    for (int j0 = 0; j0 < off; j0 += APOS) {
+      const int npos = off - j0 < APOS ? off - j0 : APOS;
+      const __half* kt = reinterpret_cast<const __half*>(ring.wait());
+      attn_scores(s.q, kt, npos, S, s.sc);
+      ring.release();
+      csync();
+      attn_softmax(s.sc, npos, S, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
+      csync();
+      const __half* vt = reinterpret_cast<const __half*>(ring.wait());
+      attn_accum(acc, s.sc, s.alpha, vt, npos, S);
+      ring.release();
+      csync();
+    }
+    // the new tokens, causally (keys/values from the QKV projection)
+    for (int idx = threadIdx.x; idx < S * S; idx += NTHR) {
+      int q = idx / S, j = idx % S;
+      float sum = 0.f;
+      for (int d = 0; d < DK; ++d) sum += s.q[q * DK + d] * s.knew[j * DK + d];
+      s.sc[q * APOS + j] = sum;
+    }
+    csync();
+    attn_softmax(s.sc, S, S, s.mrun, s.lrun, s.alpha, [](int q, int j) { return j <= q; });
+    csync();
+    {
+#pragma unroll
+      for (int q = 0; q < MAXQ; ++q)
+        if (q < S) { acc.o[q][0] *= s.alpha[q]; acc.o[q][1] *= s.alpha[q]; }
+      for (int j = warp; j < S; j += NWARP) {
+        const __half* vr = pd.qkv + (long long)(b * S + j) * 3 * D + 2 * D + h * DK;
+        float2 v = __half22float2(__ldcg(reinterpret_cast<const __half2*>(vr) + lane));
+#pragma unroll
+        for (int q = 0; q < MAXQ; ++q)
+          if (q < S) {
+            float p = s.sc[q * APOS + j];
+            acc.o[q][0] += p * v.x;
+            acc.o[q][1] += p * v.y;
+          }
+      }
+    }
+    attn_reduce(acc, S, s.scratch, s.out);
+    // outputs: o (B-fragment order for the out-projection), the cache slots, new_kv
+    for (int idx = threadIdx.x; idx < S * (DK / 2); idx += NTHR) {
+      int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
+      float inv = 1.f / s.lrun[q];
+      int m = b * S + q;
+      *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
+          __floats2half2_rn(s.out[q * DK + d] * inv, s.out[q * DK + d + 1] * inv);
+      const __half* row = pd.qkv + (long long)m * 3 * D + h * DK + d;
+      __half2 kn = __ldcg(reinterpret_cast<const __half2*>(row + D));
+      __half2 vn = __ldcg(reinterpret_cast<const __half2*>(row + 2 * D));
+      long long cslot = ((((long long)layer * pd.R + b) * H + h) * pd.C + off + q) * DK + d;
+      *reinterpret_cast<__half2*>(a.kc + cslot) = kn;
+      *reinterpret_cast<__half2*>(a.vc + cslot) = vn;
+      long long nk = ((((long long)layer * 2 * pd.R + b) * H + h) * S + q) * DK + d;
+      long long nv = nk + (long long)pd.R * H * S * DK;
+      *reinterpret_cast<__half2*>(a.new_kv + nk) = kn;
+      *reinterpret_cast<__half2*>(a.new_kv + nv) = vn;
+    }
+    csync();
+  }
+}
+
+__device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, int layer, int c, uint8_t* work,
+                                 const Frames& fr) {
+  AttnSmem s = carve_attn(work, pd.Qmax);
+  const int S = pd.S, D = pd.D, H = pd.H, G = pd.G, Q = G * S;
+  long long f0 = fr.bound(c), f1 = fr.bound(c + 1);
+  Piece p;
+  while (next_piece(fr, f0, f1, p)) {
+    const int u = p.u, h = p.h;
+    for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
+      int q = idx / DK, d = idx % DK;
+      int m = u * Q + q;  // rows u*G .. u*G+G-1, tokens s: token index (u*G + q/S)*S + q%S = u*Q + q
+      s.q[q * DK + d] = __half2float(__ldcg(pd.q2 + (long long)m * D + h * DK + d)) * 0.125f;
+    }
+    if (threadIdx.x < Q) { s.mrun[threadIdx.x] = -INFINITY; s.lrun[threadIdx.x] = 0.f; }
+    AttnAcc acc;
+#pragma unroll
+    for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
+    csync();
+    for (int j0 = p.t0; j0 < p.t1; j0 += APOS) {
+      const int npos = p.t1 - j0 < APOS ? p.t1 - j0 : APOS;
+      const __half* kt = reinterpret_cast<const __half*>(ring.wait());
+      attn_scores(s.q, kt, npos, Q, s.sc);
+      ring.release();
+      csync();
+      attn_softmax(s.sc, npos, Q, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
+      csync();
+      const __half* vt = reinterpret_cast<const __half*>(ring.wait());
+      attn_accum(acc, s.sc, s.alpha, vt, npos, Q);
+      ring.release();
+      csync();
+    }
+    attn_reduce(acc, Q, s.scratch, s.out);
+    // partial -> xpart[seg][rank]; the last contributor of the segment combines in rank order
+    const int seg = u * H + h;
+    const int len = fr.pre[u + 1] - fr.pre[u];
+    const long long sbeg = (long long)H * fr.pre[u] + (long long)h * len;
+    const int first = fr.owner(sbeg), last = fr.owner(sbeg + len - 1);
+    const int ncontrib = last - first + 1, rank = c - first;
+    float* part = pd.xpart + (((long long)seg * pd.P + rank) * Q) * (DK + 2);
+    for (int idx = threadIdx.x; idx < Q * (DK + 2); idx += NTHR) {
+      int q = idx / (DK + 2), d = idx % (DK + 2);
+      float v = d < DK ? s.out[q * DK + d] : (d == DK ? s.mrun[q] : s.lrun[q]);
+      __stcg(part + idx, v);
+    }
+    __threadfence();
+    csync();
+    if (threadIdx.x == 0) {
+      uint32_t old = atom_acq_rel_add(&pd.xcnt[seg], 1);
+      *s.flag = (old == (uint32_t)(ncontrib - 1));
+    }
+    csync();
+    if (*s.flag) {
+      const float* base = pd.xpart + ((long long)seg * pd.P * Q) * (DK + 2);
+      for (int idx = threadIdx.x; idx < Q * (DK / 2); idx += NTHR) {
+        int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
+        float mx = -INFINITY;
+        for (int r = 0; r < ncontrib; ++r) mx = fmaxf(mx, __ldcg(base + ((long long)r * Q + q) * (DK + 2) + DK));
+        float num0 = 0.f, num1 = 0.f, den = 0.f;
+        for (int r = 0; r < ncontrib; ++r) {
+          const float* pr = base + ((long long)r * Q + q) * (DK + 2);
+          float mr = __ldcg(pr + DK);
+          float w = mr > -INFINITY ? expf(mr - mx) : 0.f;
+          den += w * __ldcg(pr + DK + 1);
+          num0 += w * __ldcg(pr + d);
+          num1 += w * __ldcg(pr + d + 1);
+        }
+        int m = u * Q + q;
+        *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
+            __floats2half2_rn(num0 / den, num1 / den);
+      }
+      if (threadIdx.x == 0) atomicExch(&pd.xcnt[seg], 0u);
+    }
+    csync();
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ other stages
+__device__ void embed_stage(const PlanDev& pd, const CallArgs& a, int c) {
+  const long long total = (long long)pd.M * pd.D;
+  const long long lo = total * c / pd.P, hi = total * (c + 1) / pd.P;
+  for (long long i = lo + threadIdx.x; i < hi; i += NTHR) {
+    int m = (int)(i / pd.D), n = (int)(i % pd.D);
+    int r = m / pd.S, s = m % pd.S;
+    long long t = a.tok[(long long)r * a.tok_stride + s];
+    t = t < 0 ? 0 : (t >= pd.V ? pd.V - 1 : t);
+    long long pos = (long long)row_off(pd, a, r) + s;
+    pos = pos >= pd.max_pos ? pd.max_pos - 1 : pos;
+    pd.x[i] = __half2float(pd.emb[t * pd.D + n]) * pd.xscale + pd.pe[pos * pd.D + n];
+  }
+}
+
+// After the output stage: per-CTA argmax partials -> global; the last CTA to arrive reduces them.
+__device__ void argmax_finish(const PlanDev& pd, const CallArgs& a, int c, OutState& os, int* flag) {
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    __stcg(pd.amax + (long long)c * pd.M + m, os.amax[m]);
+    __stcg(pd.aidx + (long long)c * pd.M + m, os.aidx[m]);
+  }
+  __threadfence();
+  csync();
+  if (threadIdx.x == 0) *flag = (atom_acq_rel_add(&pd.ctr[2], 1) == (uint32_t)(pd.P - 1));
+  csync();
+  if (!*flag) return;
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int q = 0; q < pd.P; ++q) {
+      float v = __ldcg(pd.amax + (long long)q * pd.M + m);
+      int i = __ldcg(pd.aidx + (long long)q * pd.M + m);
+      if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+    }
+    if (bi == 0x7fffffff) bi = 0;
+    a.pred[(long long)(m / pd.S) * pd.S + (m % pd.S)] = bi;
+  }
+  if (threadIdx.x == 0) atomicExch(&pd.ctr[2], 0u);
+}
+
+__device__ void beam_partials(const PlanDev& pd, int c, OutState& os) {
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    __stcg(pd.lmax + (long long)c * pd.M + m, os.rmax[m]);
+    __stcg(pd.lsum + (long long)c * pd.M + m, os.rsum[m]);
+    for (int j = 0; j < KTOP; ++j) {
+      __stcg(pd.topv + ((long long)c * pd.M + m) * KTOP + j, os.topv[m * KTOP + j]);
+      __stcg(pd.topi + ((long long)c * pd.M + m) * KTOP + j, os.topi[m * KTOP + j]);
+    }
+  }
+}
+
+constexpr float LOG_ZERO = -1.0e10f;
+
+// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials, candidates
+// score + (logit - lse) from every CTA's per-row top-K (LOG_ZERO for inactive rows), top-`beam` by
+// (value desc, flat index asc); candidates are scanned in place, the picks kept in shared memory.
+__device__ void select_stage(const PlanDev& pd, const CallArgs& a, int c, uint8_t* work) {
+  const int K = pd.beam, V = pd.V, P = pd.P;
+  const int B = pd.R / K;
+  float* lmx = reinterpret_cast<float*>(work);  // [KTOP] row max of the logits
+  float* lse = lmx + KTOP;                      // [KTOP] log of the row's sum of exp(logit - max)
+  float* pickv = lse + KTOP;                    // [KTOP]
+  float* rv = pickv + KTOP;                     // [NTHR]
+  int* ri = reinterpret_cast<int*>(rv + NTHR);  // [NTHR]
+  int* picked = ri + NTHR;                      // [KTOP]
+  const int per_row = P * K + K;
+  const int ncand = K * per_row;
+  for (int u = c; u < B; u += P) {
+    for (int k = threadIdx.x; k < K; k += NTHR) {
+      const int r = u * K + k;
+      float mx = -INFINITY;
+      for (int q = 0; q < P; ++q) mx = fmaxf(mx, __ldcg(pd.lmax + (long long)q * pd.M + r));
+      float sm = 0.f;
+      for (int q = 0; q < P; ++q) {
+        float mq = __ldcg(pd.lmax + (long long)q * pd.M + r);
+        if (mq > -INFINITY) sm += __ldcg(pd.lsum + (long long)q * pd.M + r) * expf(mq - mx);
+      }
+      lmx[k] = mx;
+      lse[k] = logf(sm);
+    }
+    csync();
+    for (int sel = 0; sel < K; ++sel) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+      for (int idx = threadIdx.x; idx < ncand; idx += NTHR) {
+        const int k = idx / per_row, j = idx % per_row;
+        const int r = u * K + k;
+        const bool act = a.active[r] != 0;
+        float v;
+        int fi;
+        if (j < P * K) {
+          if (!act) continue;
+          const int q = j / K, e = j % K;
+          const float lv = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
+          if (!(lv > -INFINITY)) continue;
+          v = a.score[r] + ((lv - lmx[k]) - lse[k]);  // log_softmax = (x - max) - log(sum)
+          fi = k * V + __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
+        } else {
+          if (act) continue;
+          v = LOG_ZERO;
+          fi = k * V + (j - P * K);
+        }
+        bool taken = false;
+        for (int t = 0; t < sel; ++t) taken |= (picked[t] == fi);
+        if (taken) continue;
+        if (v > bv || (v == bv && fi < bi)) { bv = v; bi = fi; }
+      }
+      rv[threadIdx.x] = bv;
+      ri[threadIdx.x] = bi;
+      csync();
+      for (int st = NTHR / 2; st > 0; st >>= 1) {
+        if (threadIdx.x < st) {
+          const float ov = rv[threadIdx.x + st];
+          const int oi = ri[threadIdx.x + st];
+          if (ov > rv[threadIdx.x] || (ov == rv[threadIdx.x] && oi < ri[threadIdx.x])) {
+            rv[threadIdx.x] = ov;
+            ri[threadIdx.x] = oi;
+          }
+        }
+        csync();
+      }
+      if (threadIdx.x == 0) {
+        picked[sel] = ri[0];
+        pickv[sel] = rv[0];
+      }
+      csync();
+    }
+    // the scores of the (old) rows are read above: write the new ones only after all rounds
+    if (threadIdx.x < K) {
+      const int sel = threadIdx.x;
+      const int fi = picked[sel] == 0x7fffffff ? 0 : picked[sel];
+      a.score[u * K + sel] = pickv[sel];
+      a.parent[u * K + sel] = (long long)u * K + fi / V;
+      a.token[u * K + sel] = fi % V;
+    }
+    csync();
+  }
+}
+
+// Cache reorder (BeamSession._select: buf.index_select(1, parent)), in two stages through a staging copy.
+__device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, int c, bool to_tmp) {
+  const int N = pd.R, H = pd.H;
+  const long long units = (long long)pd.L * N * H;
+  for (long long uidx = c; uidx < units; uidx += pd.P) {
+    int h = (int)(uidx % H);
+    int r = (int)((uidx / H) % N);
+    int l = (int)(uidx / ((long long)H * N));
+    int par = (int)__ldcg(reinterpret_cast<const long long*>(a.parent) + r);
+    if (par == r || par < 0 || par >= N) continue;
+    int len = row_off(pd, a, par) + pd.S;
+    long long src = ((((long long)l * N + par) * H + h) * pd.C) * DK;
+    long long dst = ((((long long)l * N + r) * H + h) * pd.C) * DK;
+    long long n16 = (long long)len * DK * 2 / 16;
+    for (int kv = 0; kv < 2; ++kv) {
+      __half* cache = kv ? a.vc : a.kc;
+      __half* tmp = kv ? pd.tmpv : pd.tmpk;
+      const uint4* s = reinterpret_cast<const uint4*>(to_tmp ? cache + src : tmp + dst);
+      uint4* d = reinterpret_cast<uint4*>(to_tmp ? tmp + dst : cache + dst);
+      for (long long i = threadIdx.x; i < n16; i += NTHR) d[i] = __ldcg(s + i);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ kernel
+__device__ OutState carve_out(uint8_t* p, int M) {
+  OutState os;
+  float* f = reinterpret_cast<float*>(p);
+  os.amax = f; f += M;
+  os.aidx = reinterpret_cast<int*>(f); f += M;
+  os.rmax = f; f += M;
+  os.rsum = f; f += M;
+  os.topv = f; f += M * KTOP;
+  os.topi = reinterpret_cast<int*>(f); f += M * KTOP;
+  os.tile = f;
+  return os;
+}
+
+__host__ __device__ constexpr size_t out_smem(int M) { return sizeof(float) * ((size_t)M * (4 + 2 * KTOP) + 16 * M); }
+
+__global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __restrict__ pdp, CallArgs a) {
+  const PlanDev& pd = *pdp;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + MAXSLOT;
+  int* pre = reinterpret_cast<int*>(smem + pd.off_pre);
+  uint8_t* ringdata = smem + pd.off_ring;
+  uint8_t* work = smem + pd.off_work;
+  const int c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_stages = 8 * pd.L + 2 + (a.beam_mode ? 3 : 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < pd.nslot; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NWARP);
+    }
+    fence_barrier_init();
+    pre[0] = 0;
+    for (int u = 0; u < pd.U; ++u) pre[u + 1] = pre[u] + utt_len(pd, a, u);
+  }
+  __syncthreads();
+  Frames fr;
+  fr.total = (long long)pd.H * pre[pd.U];
+  fr.U = pd.U;
+  fr.H = pd.H;
+  fr.P = (int)(fr.total < pd.P ? fr.total : pd.P);
+  fr.pre = pre;
+
+  if (warp == NWARP) {  // producer
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      uint32_t i = 0;
+      bool dead = false;
+      for (int g = 0; g < n_stages && !dead; ++g) {
+        for_chunks(pd, a, fr, g, c, [&](const void* src, uint32_t bytes) {
+          if (dead) return;
+          const int s = i % pd.nslot;
+          if (!mbar_wait(&empty[s], ((i / pd.nslot) & 1) ^ 1, pd.max_spin)) {
+            dead = true;
+            atomicExch(pd.err, E_ERR_TIMEOUT);
+            return;
+          }
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(ringdata + (size_t)s * SLOT, src, bytes, &full[s], pol);
+          ++i;
+        });
+      }
+      // Wait for the copies still in flight (the consumers may have stopped waiting for them): the CTA
+      // must not exit while the copy engine writes its shared memory. Copies always complete, so this
+      // uses the default limit, not the (testable) call limit.
+      const uint32_t first = i > (uint32_t)pd.nslot ? i - pd.nslot : 0;
+      for (uint32_t j = first; j < i; ++j) mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, DEFAULT_SPIN);
+    }
+    return;
+  }
+
+  Ring ring{full, empty, ringdata, pd.nslot, 0, pd.max_spin, pd.err, false};
+  OutState os = carve_out(smem + pd.off_out, pd.M);
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    os.amax[m] = -INFINITY;
+    os.aidx[m] = 0x7fffffff;
+    os.rmax[m] = -INFINITY;
+    os.rsum[m] = 0.f;
+    for (int j = 0; j < KTOP; ++j) {
+      os.topv[m * KTOP + j] = -INFINITY;
+      os.topi[m * KTOP + j] = 0x7fffffff;
+    }
+  }
+  int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;  // after pre[]
+  bool dead = false;
+  for (int g = 0; g < n_stages; ++g) {
+    int layer;
+    const Kind k = stage_kind(pd, g, layer);
+    switch (k) {
+      case K_EMBED: embed_stage(pd, a, c); break;
+      case K_SATT: self_attn_stage(pd, a, ring, layer, c, work); break;
+      case K_XATT: cross_attn_stage(pd, a, ring, layer, c, work, fr); break;
+      case K_SELECT: select_stage(pd, a, c, work); break;
+      case K_REORD_A: reorder_stage(pd, a, c, true); break;
+      case K_REORD_B: reorder_stage(pd, a, c, false); break;
+      default: gemm_stage(pd, a, ring, k, layer, c, work, os); break;
+    }
+    if (k == K_OUT) {
+      csync();
+      if (a.beam_mode) beam_partials(pd, c, os);
+      else if (a.pred) argmax_finish(pd, a, c, os, flag);
+    }
+    if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead);
+  }
+  // the last CTA out resets the barrier counter for the next call
+  csync();
+  if (threadIdx.x == 0) {
+    if (atom_acq_rel_add(&pd.ctr[1], 1) == (uint32_t)(pd.P - 1)) {
+      atomicExch(&pd.ctr[1], 0u);
+      atomicExch(&pd.ctr[0], 0u);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ packing
+// Weights [N, K] (fp32 or fp16, row-major) -> fragment order of rows [row0, row0 + N) of the destination;
+// optional column scale (LayerNorm gamma). One thread per (row block, k block, lane).
+__global__ void pack_kernel(const void* __restrict__ w, int dtype, int N, int K, const float* __restrict__ gamma,
+                            uint4* __restrict__ out, int row0) {
+  const long long kbs = K >> 4;
+  const long long total = (long long)((N + 15) >> 4) * kbs * 32;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int lane = (int)(i & 31);
+    const long long kb = (i >> 5) % kbs;
+    const long long rb = (i >> 5) / kbs;
+    const int g = lane >> 2, t = lane & 3;
+    uint32_t regs[4];
+    for (int r = 0; r < 4; ++r) {
+      const int row = (int)(rb * 16) + g + (r & 1) * 8;
+      const int col = (int)(kb * 16) + 2 * t + (r >> 1) * 8;
+      float v0 = 0.f, v1 = 0.f;
+      if (row < N) {
+        const long long o = (long long)row * K + col;
+        if (dtype == OWSM_DEC_F32) {
+          v0 = reinterpret_cast<const float*>(w)[o];
+          v1 = reinterpret_cast<const float*>(w)[o + 1];
+        } else {
+          v0 = __half2float(reinterpret_cast<const __half*>(w)[o]);
+          v1 = __half2float(reinterpret_cast<const __half*>(w)[o + 1]);
+        }
+        if (gamma) {
+          v0 *= gamma[col];
+          v1 *= gamma[col + 1];
+        }
+      }
+      __half2 h = __floats2half2_rn(v0, v1);
+      regs[r] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    const long long dst = ((long long)((row0 >> 4) + rb) * kbs + kb) * 32 + lane;
+    out[dst] = make_uint4(regs[0], regs[1], regs[2], regs[3]);
+  }
+}
+
+// out[n] = b[n] + sum_k W[n, k] beta[k] (beta may be NULL): the bias after a folded LayerNorm. Warp per row.
+__global__ void fold_bias_kernel(const void* __restrict__ w, int dtype, int N, int K, const float* __restrict__ beta,
+                                 const float* __restrict__ b, float* __restrict__ out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= N) return;
+  float s = 0.f;
+  if (beta) {
+    for (int k = lane; k < K; k += 32) {
+      const long long o = (long long)warp * K + k;
+      const float wv = dtype == OWSM_DEC_F32 ? reinterpret_cast<const float*>(w)[o]
+                                             : __half2float(reinterpret_cast<const __half*>(w)[o]);
+      s += wv * beta[k];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  }
+  if (lane == 0) out[warp] = (b ? b[warp] : 0.f) + s;
+}
+
+__global__ void to_half_kernel(const void* __restrict__ src, int dtype, long long n, __half* __restrict__ dst) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+    dst[i] = dtype == OWSM_DEC_F32 ? __float2half_rn(reinterpret_cast<const float*>(src)[i])
+                                   : reinterpret_cast<const __half*>(src)[i];
+}
+
+}  // namespace owsm
+
+// ================================================================================================ host / C ABI
+using namespace owsm;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define CUDA_TRY(x)                                                                              \
+  do {                                                                                           \
+    cudaError_t e_ = (x);                                                                        \
+    if (e_ != cudaSuccess) return fail(OWSM_DEC_ERR_CUDA, std::string(#x ": ") + cudaGetErrorString(e_)); \
+  } while (0)
+
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+
+}  // namespace
+
+struct OwsmDec {
+  int device = 0;
+  int programs = 0;
+  int sms = 0;
+  OwsmDecDims dims{};
+  std::vector<void*> allocs;  // packed weights, biases, tables
+  GemmW g[NGEMM]{};
+  __half* emb = nullptr;
+  float* pe = nullptr;
+  int* err = nullptr;  // device error word
+  uint32_t max_spin = DEFAULT_SPIN;
+  ~OwsmDec() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(device);
+    for (void* p : allocs) cudaFree(p);
+    cudaSetDevice(cur);
+  }
+};
+
+struct OwsmDecPlan {
+  OwsmDec* h = nullptr;
+  PlanDev pd{};
+  PlanDev* pd_dev = nullptr;
+  std::vector<void*> allocs;
+  size_t smem = 0;
+  int64_t scratch_bytes = 0;
+  int beam = 0;
+  ~OwsmDecPlan() {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    cudaSetDevice(h->device);
+    for (void* p : allocs) cudaFree(p);
+    cudaSetDevice(cur);
+  }
+};
+
+namespace {
+
+struct DeviceGuard {
+  int prev = 0;
+  explicit DeviceGuard(int d) {
+    cudaGetDevice(&prev);
+    cudaSetDevice(d);
+  }
+  ~DeviceGuard() { cudaSetDevice(prev); }
+};
+
+template <class T>
+int dev_alloc(std::vector<void*>& list, T** out, size_t count, int64_t* total = nullptr) {
+  void* p = nullptr;
+  size_t bytes = count * sizeof(T);
+  if (bytes == 0) bytes = 16;
+  CUDA_TRY(cudaMalloc(&p, bytes));
+  CUDA_TRY(cudaMemset(p, 0, bytes));
+  list.push_back(p);
+  *out = reinterpret_cast<T*>(p);
+  if (total) *total += (int64_t)bytes;
+  return OWSM_DEC_OK;
+}
+
+int launch_pack(const void* w, int dtype, int N, int K, const float* gamma, uint4* out, int row0) {
+  if (!w) return fail(OWSM_DEC_ERR_ARG, "missing weight pointer");
+  long long total = (long long)((N + 15) / 16) * (K / 16) * 32;
+  int blocks = (int)std::min<long long>((total + 255) / 256, 65535);
+  pack_kernel<<<blocks, 256>>>(w, dtype, N, K, gamma, out, row0);
+  CUDA_TRY(cudaGetLastError());
+  return OWSM_DEC_OK;
+}
+
+int launch_fold(const void* w, int dtype, int N, int K, const float* beta, const float* b, float* out) {
+  if (!w) return fail(OWSM_DEC_ERR_ARG, "missing weight pointer");
+  int blocks = (N * 32 + 255) / 256;
+  fold_bias_kernel<<<blocks, 256>>>(w, dtype, N, K, beta, b, out);
+  CUDA_TRY(cudaGetLastError());
+  return OWSM_DEC_OK;
+}
+
+}  // namespace
+
+namespace {
+
+// Greedy assignment of every 16-row block of the six layer GEMMs to the CTAs (largest blocks first, to the
+// CTA with the fewest bytes so far): balanced bytes per CTA over a layer, which is what the streaming
+// producers see. The output layer is split in contiguous ranges.
+void assign_blocks(const GemmW* g, int P, std::vector<int> off[NGEMM], std::vector<int> blk[NGEMM]) {
+  struct Item {
+    long long bytes;
+    int gi, rb;
+  };
+  std::vector<Item> items;
+  for (int gi = 0; gi < G_OUT; ++gi)
+    for (int rb = 0; rb < g[gi].NB; ++rb) items.push_back({(long long)g[gi].K * 32, gi, rb});
+  std::stable_sort(items.begin(), items.end(), [](const Item& x, const Item& y) { return x.bytes > y.bytes; });
+  std::vector<long long> load(P, 0);
+  std::vector<std::vector<int>> per[NGEMM];
+  for (int gi = 0; gi < NGEMM; ++gi) per[gi].assign(P, {});
+  for (const Item& it : items) {
+    int best = 0;
+    for (int c = 1; c < P; ++c)
+      if (load[c] < load[best]) best = c;
+    load[best] += it.bytes;
+    per[it.gi][best].push_back(it.rb);
+  }
+  for (int c = 0; c < P; ++c) {
+    long long lo = (long long)g[G_OUT].NB * c / P, hi = (long long)g[G_OUT].NB * (c + 1) / P;
+    for (long long rb = lo; rb < hi; ++rb) per[G_OUT][c].push_back((int)rb);
+  }
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    off[gi].assign(P + 1, 0);
+    blk[gi].clear();
+    for (int c = 0; c < P; ++c) {
+      std::sort(per[gi][c].begin(), per[gi][c].end());
+      off[gi][c + 1] = off[gi][c] + (int)per[gi][c].size();
+      blk[gi].insert(blk[gi].end(), per[gi][c].begin(), per[gi][c].end());
+    }
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* owsm_dec_last_error(void) { return g_last_error.c_str(); }
+
+int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device, int programs, OwsmDec** out) {
+  if (!dims || !w || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  *out = nullptr;
+  const OwsmDecDims d = *dims;
+  if (d.L < 1 || d.H < 1 || d.D != d.H * DK) return fail(OWSM_DEC_ERR_LIMIT, "the head size must be 64 (D = 64 * H)");
+  if (d.D % 16 || d.F % 16 || d.F < 16 || d.V < 1 || d.max_pos < 1)
+    return fail(OWSM_DEC_ERR_LIMIT, "D and F must be multiples of 16");
+  if (w->weight_dtype != OWSM_DEC_F32 && w->weight_dtype != OWSM_DEC_F16)
+    return fail(OWSM_DEC_ERR_ARG, "weight_dtype must be OWSM_DEC_F32 or OWSM_DEC_F16");
+  if (!w->layers || !w->emb || !w->pe || !w->wout) return fail(OWSM_DEC_ERR_ARG, "missing weights");
+  DeviceGuard guard(device);
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+  if (prop.major < 10) return fail(OWSM_DEC_ERR_LIMIT, "libowsmdec needs an sm_100 GPU (B200)");
+  OwsmDec* h = new OwsmDec();
+  h->device = device;
+  h->dims = d;
+  h->sms = prop.multiProcessorCount;
+  h->programs = (programs > 0 && programs < h->sms) ? programs : h->sms;
+  const int dt = w->weight_dtype;
+  const int D = d.D, F = d.F, L = d.L, V = d.V;
+  struct Spec {
+    int N, K, layers;
+  } spec[NGEMM] = {{3 * D, D, L}, {D, D, L}, {D, D, L}, {D, D, L}, {F, D, L}, {D, F, L}, {V, D, 1}};
+  int rc = OWSM_DEC_OK;
+  auto bail = [&](int code) {
+    delete h;
+    return code;
+  };
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    GemmW& gw = h->g[gi];
+    gw.N = spec[gi].N;
+    gw.K = spec[gi].K;
+    gw.NB = (gw.N + 15) / 16;
+    gw.lstride = (long long)gw.NB * (gw.K / 16) * 32;
+    uint4* wp;
+    float* bp;
+    if ((rc = dev_alloc(h->allocs, &wp, (size_t)gw.lstride * spec[gi].layers))) return bail(rc);
+    if ((rc = dev_alloc(h->allocs, &bp, (size_t)gw.N * spec[gi].layers))) return bail(rc);
+    gw.w = wp;
+    gw.b = bp;
+  }
+  for (int l = 0; l < L; ++l) {
+    const OwsmDecLayer& ly = w->layers[l];
+    uint4* wq = const_cast<uint4*>(h->g[G_QKV].w) + (long long)l * h->g[G_QKV].lstride;
+    float* bq = const_cast<float*>(h->g[G_QKV].b) + (long long)l * 3 * D;
+    if (ly.wk) {
+      const void* ws[3] = {ly.wq, ly.wk, ly.wv};
+      const float* bs[3] = {ly.bq, ly.bk, ly.bv};
+      for (int i = 0; i < 3; ++i) {
+        if ((rc = launch_pack(ws[i], dt, D, D, ly.ln1_g, wq, i * D))) return bail(rc);
+        if ((rc = launch_fold(ws[i], dt, D, D, ly.ln1_b, bs[i], bq + i * D))) return bail(rc);
+      }
+    } else {
+      if ((rc = launch_pack(ly.wq, dt, 3 * D, D, ly.ln1_g, wq, 0))) return bail(rc);
+      if ((rc = launch_fold(ly.wq, dt, 3 * D, D, ly.ln1_b, ly.bq, bq))) return bail(rc);
+    }
+    struct One {
+      int gi;
+      const void* w;
+      const float* b;
+      const float* g;
+      const float* beta;
+    } ones[5] = {{G_WO, ly.wo, ly.bo, nullptr, nullptr},
+                 {G_CQ, ly.wcq, ly.bcq, ly.ln2_g, ly.ln2_b},
+                 {G_WCO, ly.wco, ly.bco, nullptr, nullptr},
+                 {G_F1, ly.w1, ly.b1, ly.ln3_g, ly.ln3_b},
+                 {G_F2, ly.w2, ly.b2, nullptr, nullptr}};
+    for (const One& o : ones) {
+      GemmW& gw = h->g[o.gi];
+      uint4* wp = const_cast<uint4*>(gw.w) + (long long)l * gw.lstride;
+      float* bp = const_cast<float*>(gw.b) + (long long)l * gw.N;
+      if ((rc = launch_pack(o.w, dt, gw.N, gw.K, o.g, wp, 0))) return bail(rc);
+      if ((rc = launch_fold(o.w, dt, gw.N, gw.K, o.beta, o.b, bp))) return bail(rc);
+    }
+  }
+  {
+    GemmW& gw = h->g[G_OUT];
+    if ((rc = launch_pack(w->wout, dt, V, D, w->lnf_g, const_cast<uint4*>(gw.w), 0))) return bail(rc);
+    if ((rc = launch_fold(w->wout, dt, V, D, w->lnf_b, w->bout, const_cast<float*>(gw.b)))) return bail(rc);
+  }
+  if ((rc = dev_alloc(h->allocs, &h->emb, (size_t)V * D))) return bail(rc);
+  to_half_kernel<<<1024, 256>>>(w->emb, dt, (long long)V * D, h->emb);
+  if (cudaGetLastError() != cudaSuccess) return bail(fail(OWSM_DEC_ERR_CUDA, "embedding copy failed"));
+  if ((rc = dev_alloc(h->allocs, &h->pe, (size_t)d.max_pos * D))) return bail(rc);
+  if (cudaMemcpy(h->pe, w->pe, (size_t)d.max_pos * D * sizeof(float), cudaMemcpyDeviceToDevice) != cudaSuccess)
+    return bail(fail(OWSM_DEC_ERR_CUDA, "positional table copy failed"));
+  if ((rc = dev_alloc(h->allocs, &h->err, 4))) return bail(rc);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return bail(fail(OWSM_DEC_ERR_CUDA, std::string("packing: ") + cudaGetErrorString(e)));
+  *out = h;
+  return OWSM_DEC_OK;
+}
+
+void owsm_dec_destroy(OwsmDec* h) { delete h; }
+
+int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out) {
+  if (!h || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  *out = nullptr;
+  const OwsmDecDims& d = h->dims;
+  const int G = rows_per_utt < 1 ? 1 : rows_per_utt;
+  if (R < 1 || S < 1 || C < S || T < 1) return fail(OWSM_DEC_ERR_ARG, "bad call shape");
+  if (R % G) return fail(OWSM_DEC_ERR_ARG, "rows must be a multiple of rows_per_utt");
+  const int M = R * S;
+  if (M > MAXNT * 8) return fail(OWSM_DEC_ERR_LIMIT, "at most 64 tokens (rows x window) per call");
+  if (S > MAXQ || G * S > MAXQ) return fail(OWSM_DEC_ERR_LIMIT, "rows_per_utt x window must be <= 16");
+  if (beam) {
+    if (beam < 1 || beam > KTOP || S != 1 || R % beam || G != beam)
+      return fail(OWSM_DEC_ERR_LIMIT, "beam calls: S = 1, beam <= 8, rows = batch x beam, rows_per_utt = beam");
+  }
+  if (C + S > d.max_pos + C) return fail(OWSM_DEC_ERR_ARG, "bad cache");
+  const int U = R / G;
+  if (U > 1024) return fail(OWSM_DEC_ERR_LIMIT, "at most 1024 utterances");
+  DeviceGuard guard(h->device);
+  OwsmDecPlan* p = new OwsmDecPlan();
+  p->h = h;
+  p->beam = beam;
+  PlanDev& pd = p->pd;
+  pd.L = d.L; pd.D = d.D; pd.H = d.H; pd.F = d.F; pd.V = d.V; pd.max_pos = d.max_pos;
+  pd.eps = d.eps; pd.xscale = d.xscale;
+  pd.R = R; pd.S = S; pd.M = M; pd.NT = (M + 7) / 8; pd.C = C; pd.T = T; pd.G = G; pd.U = U; pd.beam = beam;
+  pd.P = h->programs;
+  pd.max_spin = h->max_spin;
+  pd.emb = h->emb;
+  pd.pe = h->pe;
+  for (int gi = 0; gi < NGEMM; ++gi) pd.g[gi] = h->g[gi];
+  pd.err = h->err;
+  pd.Qmax = std::max(S, G * S);
+  auto bail = [&](int code) {
+    delete p;
+    return code;
+  };
+  int rc;
+  int64_t* tot = &p->scratch_bytes;
+  // schedule
+  std::vector<int> off[NGEMM], blk[NGEMM];
+  assign_blocks(pd.g, pd.P, off, blk);
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    int *o, *b;
+    if ((rc = dev_alloc(p->allocs, &o, off[gi].size(), tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &b, std::max<size_t>(blk[gi].size(), 1), tot))) return bail(rc);
+    CUDA_TRY(cudaMemcpy(o, off[gi].data(), off[gi].size() * 4, cudaMemcpyHostToDevice));
+    if (!blk[gi].empty()) CUDA_TRY(cudaMemcpy(b, blk[gi].data(), blk[gi].size() * 4, cudaMemcpyHostToDevice));
+    pd.goff[gi] = o;
+    pd.gblk[gi] = b;
+  }
+  // scratch
+  const int NT = pd.NT, P = pd.P, D = d.D, F = d.F, Q = G * S;
+  if ((rc = dev_alloc(p->allocs, &pd.x, (size_t)M * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.qkv, (size_t)M * 3 * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.oB, (size_t)NT * 8 * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.hB, (size_t)NT * 8 * F, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * (DK + 2), tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);
+  if (beam) {
+    if ((rc = dev_alloc(p->allocs, &pd.lmax, (size_t)P * M, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.lsum, (size_t)P * M, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.topv, (size_t)P * M * KTOP, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.topi, (size_t)P * M * KTOP, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.tmpk, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.tmpv, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
+  }
+  // shared memory: barriers | utterance prefix sums + flag | output-stage state | ring | work area
+  size_t off_pre = 256;
+  size_t off_out = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  size_t off_ring = (off_out + out_smem(M) + 1023) & ~(size_t)1023;
+  size_t gemm_work = (size_t)NT * (D / 16) * 256 + (size_t)NWARP * NT * 32 * 16;
+  size_t work = std::max(gemm_work, attn_smem(pd.Qmax));
+  work = std::max(work, sizeof(float) * (3 * KTOP + 2 * NTHR + KTOP));
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
+  const size_t limit = prop.sharedMemPerBlockOptin;
+  if (off_ring + 2 * (size_t)SLOT + work > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
+  int nslot = (int)std::min<size_t>((limit - off_ring - work) / SLOT, 6);
+  pd.nslot = nslot;
+  pd.off_pre = (int)off_pre;
+  pd.off_out = (int)off_out;
+  pd.off_ring = (int)off_ring;
+  pd.off_work = (int)(off_ring + (size_t)nslot * SLOT);
+  p->smem = (size_t)pd.off_work + work;
+  // the attribute is per function: set it to the device maximum once, so plans of other sizes coexist
+  CUDA_TRY(cudaFuncSetAttribute(decoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decoder_kernel, BLOCK, p->smem));
+  if (per_sm < 1) return bail(fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM"));
+  if ((rc = dev_alloc(p->allocs, &p->pd_dev, 1, tot))) return bail(rc);
+  CUDA_TRY(cudaMemcpy(p->pd_dev, &pd, sizeof(PlanDev), cudaMemcpyHostToDevice));
+  *out = p;
+  return OWSM_DEC_OK;
+}
+
+void owsm_dec_plan_destroy(OwsmDecPlan* p) { delete p; }
+
+static int launch(OwsmDecPlan* p, void* stream, const CallArgs& a) {
+  DeviceGuard guard(p->h->device);
+  if (p->pd.max_spin != p->h->max_spin) {
+    p->pd.max_spin = p->h->max_spin;
+    CUDA_TRY(cudaMemcpy(p->pd_dev, &p->pd, sizeof(PlanDev), cudaMemcpyHostToDevice));
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3(p->pd.P);
+  cfg.blockDim = dim3(BLOCK);
+  cfg.dynamicSmemBytes = p->smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const PlanDev* pdp = p->pd_dev;
+  CUDA_TRY(cudaLaunchKernelEx(&cfg, decoder_kernel, pdp, a));
+  return OWSM_DEC_OK;
+}
+
+static int check_common(OwsmDecPlan* p, const int64_t* tokens, const int64_t* offset, void* self_k, void* self_v,
+                        const void* cross_k, const void* cross_v, float* logits, void* new_kv) {
+  if (!p || !tokens || !offset || !self_k || !self_v || !cross_k || !cross_v || !logits || !new_kv)
+    return fail(OWSM_DEC_ERR_ARG, "null buffer");
+  if (!aligned16(self_k) || !aligned16(self_v) || !aligned16(cross_k) || !aligned16(cross_v))
+    return fail(OWSM_DEC_ERR_ARG, "K/V buffers must be 16-byte aligned");
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride, const int64_t* offset,
+                  int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
+                  const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
+                  int first_time, int last_time) {
+  int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
+  if (rc) return rc;
+  CallArgs a{};
+  a.tok = tokens; a.tok_stride = tok_stride;
+  a.off = offset; a.off_stride = off_stride;
+  a.kc = reinterpret_cast<__half*>(self_k); a.vc = reinterpret_cast<__half*>(self_v);
+  a.ck = reinterpret_cast<const __half*>(cross_k); a.cv = reinterpret_cast<const __half*>(cross_v);
+  a.enc_len = enc_len;
+  a.logits = logits; a.new_kv = reinterpret_cast<__half*>(new_kv);
+  a.pred = pred; a.notime = notime; a.ft = first_time; a.lt = last_time;
+  a.beam_mode = 0;
+  return launch(p, stream, a);
+}
+
+int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride,
+                       const int64_t* offset, int64_t off_stride, void* self_k, void* self_v, const void* cross_k,
+                       const void* cross_v, const int32_t* enc_len, float* logits, void* new_kv, float* score,
+                       const uint8_t* active, int64_t* parent, int64_t* token) {
+  int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
+  if (rc) return rc;
+  if (!p->beam) return fail(OWSM_DEC_ERR_ARG, "the plan was not made for beam calls");
+  if (!score || !active || !parent || !token) return fail(OWSM_DEC_ERR_ARG, "null beam buffer");
+  CallArgs a{};
+  a.tok = tokens; a.tok_stride = tok_stride;
+  a.off = offset; a.off_stride = off_stride;
+  a.kc = reinterpret_cast<__half*>(self_k); a.vc = reinterpret_cast<__half*>(self_v);
+  a.ck = reinterpret_cast<const __half*>(cross_k); a.cv = reinterpret_cast<const __half*>(cross_v);
+  a.enc_len = enc_len;
+  a.logits = logits; a.new_kv = reinterpret_cast<__half*>(new_kv);
+  a.score = score; a.active = active; a.parent = parent; a.token = token;
+  a.beam_mode = 1;
+  return launch(p, stream, a);
+}
+
+int owsm_dec_get_error(OwsmDec* h) {
+  if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
+  DeviceGuard guard(h->device);
+  CUDA_TRY(cudaDeviceSynchronize());
+  int e = 0;
+  CUDA_TRY(cudaMemcpy(&e, h->err, 4, cudaMemcpyDeviceToHost));
+  if (e) {
+    CUDA_TRY(cudaMemset(h->err, 0, 4));
+    return fail(OWSM_DEC_ERR_TIMEOUT, "a bounded in-kernel wait gave up");
+  }
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_plan_reset(OwsmDecPlan* p) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  DeviceGuard guard(p->h->device);
+  CUDA_TRY(cudaDeviceSynchronize());
+  CUDA_TRY(cudaMemset(p->pd.ctr, 0, 8 * sizeof(uint32_t)));
+  CUDA_TRY(cudaMemset(p->pd.xcnt, 0, (size_t)p->pd.U * p->pd.H * sizeof(uint32_t)));
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int64_t* scratch_bytes) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  if (programs) *programs = p->pd.P;
+  if (ring_slots) *ring_slots = p->pd.nslot;
+  if (scratch_bytes) *scratch_bytes = p->scratch_bytes;
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls) {
+  if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
+  h->max_spin = polls ? polls : DEFAULT_SPIN;
+  return OWSM_DEC_OK;
+}
+
+}  // extern "C"

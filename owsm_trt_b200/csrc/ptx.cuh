@@ -1,0 +1,158 @@
+// Inline-PTX building blocks of the decoder-step kernel (sm_100a).
+//
+// * mbarrier + cp.async.bulk: the weight ring. A producer thread copies contiguous byte ranges from
+//   global memory into shared-memory slots with the bulk-copy engine (no registers, no tensor maps);
+//   each slot has a "full" barrier (transaction bytes) and an "empty" barrier (consumer warps).
+// * flag-in-data words ("LL" words): 8 bytes = 4 bytes of payload + a 4-byte epoch flag, written and
+//   read as one access, so a reader that sees the flag it expects also sees the payload written with
+//   it; one L2 round trip moves both the data and the signal between CTAs.
+// * release/acquire counters for the few places that need an arrival count (last-arriver combines).
+//
+// Every wait in this file is bounded: it gives up after a fixed number of polls and reports failure
+// to the caller, which records an error code and lets the kernel run to its end.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace owsm {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Make the initialised barriers visible to the bulk-copy (async) proxy.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete; false after `max_polls` failed polls.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_polls) {
+  for (uint32_t i = 0; i < max_polls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// ---------------------------------------------------------------- bulk copies
+// Global -> this CTA's shared memory; completion is counted in transaction bytes on `bar`.
+// dst, src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                         uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 policy for data read once per call (weights, encoder keys/values): evict first.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p));
+}
+
+// ---------------------------------------------------------------- flag-in-data words
+// One 16-byte store / load = two words (payload, flag, payload, flag).
+__device__ __forceinline__ void ll_store2(uint32_t* dst, uint32_t p0, uint32_t p1, uint32_t flag) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(p0), "r"(flag), "r"(p1),
+               "r"(flag)
+               : "memory");
+}
+
+__device__ __forceinline__ void ll_store1(uint32_t* dst, uint32_t p0, uint32_t flag) {
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(dst), "r"(p0), "r"(flag) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const uint32_t* src) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(src)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint2 ld_volatile_v2(const uint32_t* src) {
+  uint2 v;
+  asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(src) : "memory");
+  return v;
+}
+
+// Poll two words until both carry `flag`; false after `max_polls` polls.
+__device__ __forceinline__ bool ll_load2(const uint32_t* src, uint32_t flag, uint32_t max_polls, uint32_t& p0,
+                                         uint32_t& p1) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    uint4 v = ld_volatile_v4(src);
+    if (v.y == flag && v.w == flag) {
+      p0 = v.x;
+      p1 = v.z;
+      return true;
+    }
+  }
+  return false;
+}
+
+// ---------------------------------------------------------------- counters
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t atom_acq_rel_add(uint32_t* p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float2 unpack_half2(uint32_t u) {
+  __half2 h = *reinterpret_cast<__half2*>(&u);
+  return __half22float2(h);
+}
+
+}  // namespace owsm

@@ -1,0 +1,256 @@
+"""The decoder-step kernel behind owsm-trt's megakernel launcher interface.
+
+:class:`B200Decoder` has the contract of ``MegaDecoder`` / ``RingDecoder`` (src/owsm_trt/megakernel.py:537-685,
+src/owsm_trt/megakernel_ring.py:737-861): built from a ``Decoder`` module, ``step_fn(tokens, offset, self_k,
+self_v, cross_k, cross_v, logits, new_kv, kind="decode", pred=None, solo=False, notime=None)`` returns a
+graph-capturable ``run()`` that fills ``logits`` and ``new_kv``, writes the new keys/values into the cache
+(``run.writes_cache``) and, with ``pred``, the argmax (``run.writes_pred``). So ``MegaBackend``, the
+sessions and ``OWSM.from_pretrained(..., decoder_kernel=...)`` can use it unchanged.
+
+Additions (keyword-only, optional): ``enc_len`` (int32 [U] frames per utterance: a key-padding mask),
+``rows_per_utt`` (rows sharing one utterance's cross K/V, e.g. the beam), and :meth:`B200Decoder.beam_fn`
+(the call + BeamSession._select's top-K + the cache reorder in one launch).
+
+All compute runs in ``libowsmdec.so`` (CUDA, sm_100a), called through ctypes with raw device pointers.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import logging
+import math
+
+import torch
+
+from . import _lib
+from .synthetic import sinusoidal_positions
+
+log = logging.getLogger(__name__)
+
+
+def _state_of(decoder) -> tuple[dict, int, torch.Tensor | None, float]:
+    """(state dict in the reference naming, heads, positional table or None, LayerNorm eps)."""
+    if isinstance(decoder, dict):
+        raise TypeError("give (state_dict, heads) as B200Decoder.from_state_dict")
+    sd = {k: v for k, v in decoder.state_dict().items()}
+    heads = decoder.decoders[0].self_attn.h
+    pe = getattr(decoder, "pe", None)
+    eps = float(decoder.after_norm.eps)
+    return sd, heads, pe, eps
+
+
+class B200Decoder:
+    """The decoder of an encoder-decoder OWSM model as one persistent sm_100a kernel per call."""
+
+    name = "b200-megakernel"
+    argmax = True  # step_fn takes pred
+    solo_differs = False  # a single-row call is the same call with or without an encoder alongside
+
+    @torch.no_grad()
+    def __init__(self, decoder, device: torch.device | str = "cuda", programs: int | None = None, **opts):
+        sd, heads, pe, eps = _state_of(decoder)
+        self._init(sd, heads, torch.device(device), programs, pe=pe, eps=eps, **opts)
+
+    @classmethod
+    def from_state_dict(cls, sd: dict, heads: int, device="cuda", programs: int | None = None, pe=None,
+                        eps: float = 1e-12, **opts) -> "B200Decoder":  # fmt: skip
+        obj = cls.__new__(cls)
+        obj._init(sd, heads, torch.device(device), programs, pe=pe, eps=eps, **opts)
+        return obj
+
+    @torch.no_grad()
+    def _init(self, sd: dict, heads: int, device: torch.device, programs, pe=None, eps=1e-12, max_pos=5000,
+              weight_dtype=torch.float32):  # fmt: skip
+        if device.type != "cuda":
+            raise ValueError("B200Decoder needs a CUDA device")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        lib = _lib.lib()
+        self.device = device
+        V, D = sd["embed.0.weight"].shape
+        L = 1 + max(int(k.split(".")[1]) for k in sd if k.startswith("decoders."))
+        pre = "decoders.0."
+        F = sd[pre + "feed_forward.w_1.weight"].shape[0]
+        self.L, self.D, self.H, self.F, self.V = L, D, heads, F, V
+        if pe is None:
+            pe = sinusoidal_positions(max_pos, D)
+        fdt = weight_dtype
+        keep = []  # device copies alive during create
+
+        def dev(t, dt=torch.float32):
+            t = t.detach().to(device=device, dtype=dt).contiguous()
+            keep.append(t)
+            return t.data_ptr()
+
+        layers = (_lib.Layer * L)()
+        for i in range(L):
+            p = f"decoders.{i}."
+            ly = layers[i]
+            sa, xa, ff = p + "self_attn.", p + "src_attn.", p + "feed_forward."
+            if sa + "linear_qkv.weight" in sd:
+                ly.wq = dev(sd[sa + "linear_qkv.weight"], fdt)
+                ly.bq = dev(sd[sa + "linear_qkv.bias"])
+                ly.wk = ly.wv = ly.bk = ly.bv = None
+            else:
+                ly.wq, ly.wk, ly.wv = (dev(sd[sa + f"linear_{n}.weight"], fdt) for n in "qkv")
+                ly.bq, ly.bk, ly.bv = (dev(sd[sa + f"linear_{n}.bias"]) for n in "qkv")
+            ly.wo, ly.bo = dev(sd[sa + "linear_out.weight"], fdt), dev(sd[sa + "linear_out.bias"])
+            ly.wcq, ly.bcq = dev(sd[xa + "linear_q.weight"], fdt), dev(sd[xa + "linear_q.bias"])
+            ly.wco, ly.bco = dev(sd[xa + "linear_out.weight"], fdt), dev(sd[xa + "linear_out.bias"])
+            ly.w1, ly.b1 = dev(sd[ff + "w_1.weight"], fdt), dev(sd[ff + "w_1.bias"])
+            ly.w2, ly.b2 = dev(sd[ff + "w_2.weight"], fdt), dev(sd[ff + "w_2.bias"])
+            for n in (1, 2, 3):
+                setattr(ly, f"ln{n}_g", dev(sd[p + f"norm{n}.weight"]))
+                setattr(ly, f"ln{n}_b", dev(sd[p + f"norm{n}.bias"]))
+        w = _lib.Weights()
+        w.weight_dtype = _lib.F32 if fdt == torch.float32 else _lib.F16
+        w.emb = dev(sd["embed.0.weight"], fdt)
+        w.pe = dev(pe)
+        w.layers = C.cast(layers, C.POINTER(_lib.Layer))
+        w.lnf_g, w.lnf_b = dev(sd["after_norm.weight"]), dev(sd["after_norm.bias"])
+        w.wout, w.bout = dev(sd["output_layer.weight"], fdt), dev(sd["output_layer.bias"])
+        dims = _lib.Dims(L, D, heads, F, V, pe.shape[0], float(eps), float(math.sqrt(D)))
+        h = C.c_void_p()
+        with torch.cuda.device(device):
+            _lib.check(lib.owsm_dec_create(C.byref(dims), C.byref(w), device.index or 0, programs or 0, C.byref(h)),
+                       "owsm_dec_create")  # fmt: skip
+        del keep
+        self._h = h
+        self._plans: dict[tuple, C.c_void_p] = {}
+        self.programs = self._plan_info(self._plan(1, 1, 16, 16, 1, 0))[0]
+        self.max_pos = pe.shape[0]
+
+    # ------------------------------------------------------------------ plans
+    def _plan(self, R: int, S: int, Cc: int, T: int, G: int, beam: int) -> C.c_void_p:
+        key = (R, S, Cc, T, G, beam)
+        if key not in self._plans:
+            p = C.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.lib().owsm_dec_plan(self._h, R, S, Cc, T, G, beam, C.byref(p)), "owsm_dec_plan")
+            self._plans[key] = p
+        return self._plans[key]
+
+    @staticmethod
+    def _plan_info(p) -> tuple[int, int, int]:
+        a, b, c = C.c_int(), C.c_int(), C.c_int64()
+        _lib.check(_lib.lib().owsm_dec_plan_info(p, C.byref(a), C.byref(b), C.byref(c)), "owsm_dec_plan_info")
+        return a.value, b.value, c.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib = _lib.lib()
+            for p in self._plans.values():
+                lib.owsm_dec_plan_destroy(p)
+            self._plans.clear()
+            lib.owsm_dec_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 (interpreter shutdown)
+            pass
+
+    # ------------------------------------------------------------------ errors
+    def check(self) -> None:
+        """Raise if a bounded in-kernel wait of an earlier call gave up (its results were garbage);
+        resets the plans' counters (``MegaDecoder.check``, src/owsm_trt/megakernel.py:616-622)."""
+        code = _lib.lib().owsm_dec_get_error(self._h)
+        if code != _lib.OK:
+            for p in self._plans.values():
+                _lib.lib().owsm_dec_plan_reset(p)
+            raise RuntimeError("the decoder kernel timed out at a grid barrier (were all its CTAs resident?)")
+
+    def set_max_spin(self, polls: int) -> None:
+        """Testing hook: the in-kernel wait limit of later calls (0: the default)."""
+        _lib.check(_lib.lib().owsm_dec_set_max_spin(self._h, polls), "owsm_dec_set_max_spin")
+
+    # ------------------------------------------------------------------ calls
+    def _validate(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G):
+        R, S = tokens.shape
+        L, H, dk = self.L, self.H, 64
+        if tokens.dtype != torch.int64 or offset.dtype != torch.int64:
+            raise TypeError("tokens and offset must be int64")
+        if tokens.stride(1) != 1:
+            raise ValueError("tokens must be contiguous along the window")
+        for name, t in (("self_k", self_k), ("self_v", self_v), ("cross_k", cross_k), ("cross_v", cross_v),
+                        ("new_kv", new_kv)):  # fmt: skip
+            if t.dtype != torch.float16 or not t.is_contiguous():
+                raise TypeError(f"{name} must be contiguous fp16")
+        if logits.dtype != torch.float32 or not logits.is_contiguous():
+            raise TypeError("logits must be contiguous fp32")
+        Cc = self_k.shape[3]
+        T = cross_k.shape[3]
+        if self_k.shape != (L, R, H, Cc, dk) or self_v.shape != self_k.shape:
+            raise ValueError(f"self_k/self_v must be [L, R, H, C, 64] = {(L, R, H, Cc, dk)}, got {tuple(self_k.shape)}")
+        if cross_k.shape != (L, R // G, H, T, dk) or cross_v.shape != cross_k.shape:
+            raise ValueError(f"cross_k/cross_v must be [L, R/rows_per_utt, H, T, 64], got {tuple(cross_k.shape)}")
+        if logits.shape != (R, S, self.V) or new_kv.shape != (L, 2, R, H, S, dk):
+            raise ValueError("logits [R, S, V] / new_kv [L, 2, R, H, S, 64] shape mismatch")
+        for t in (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv):
+            if t.device != self.device:
+                raise ValueError(f"all buffers must be on {self.device}")
+        return R, S, Cc, T
+
+    def step_fn(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, kind="decode", pred=None,
+                solo=False, notime=None, *, enc_len=None, rows_per_utt: int = 1):  # fmt: skip
+        """The call on these buffers (see the module docstring). ``notime`` = (flags [R] bool, first timestamp
+        token, last one): the argmax of flagged rows leaves those ids out."""
+        G = int(rows_per_utt)
+        R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G)
+        plan = self._plan(R, S, Cc, T, G, 0)
+        lib = _lib.lib()
+        if pred is not None and (pred.dtype != torch.int64 or pred.shape != (R, S) or not pred.is_contiguous()):
+            raise ValueError("pred must be contiguous int64 [R, S]")
+        ntm, ft, lt = None, 0, -1
+        if notime is not None and pred is not None:
+            flags, ft, lt = notime
+            ntm = flags.to(torch.uint8) if flags.dtype != torch.uint8 else flags
+            ntm = ntm.contiguous()
+        if enc_len is not None:
+            if enc_len.dtype != torch.int32 or enc_len.numel() != R // G:
+                raise ValueError("enc_len must be int32 [R / rows_per_utt]")
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        args = (plan, None, ptr(tokens), tokens.stride(0), ptr(offset), offset.stride(0), ptr(self_k), ptr(self_v),
+                ptr(cross_k), ptr(cross_v), ptr(enc_len), ptr(logits), ptr(new_kv), ptr(pred), ptr(ntm), int(ft),
+                int(lt))  # fmt: skip
+        fn = lib.owsm_dec_step
+        dev = self.device
+
+        def run() -> None:
+            stream = torch.cuda.current_stream(dev).cuda_stream
+            _lib.check(fn(args[0], stream, *args[2:]), "owsm_dec_step")
+
+        run.writes_cache = True
+        run.writes_pred = pred is not None
+        run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, ntm, enc_len)
+        run.programs = self.programs
+        run.kernel = self
+        return run
+
+    def beam_fn(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent,
+                token, *, beam: int, enc_len=None):  # fmt: skip
+        """One beam step (S = 1, rows = batch x beam, utterance-major, cross K/V one per utterance): the decoder
+        call, then BeamSession._select step 1 (runtime.py:1399-1411) -- ``score`` [R] fp32 is replaced by the new
+        scores, ``parent`` / ``token`` [R] int64 written -- and the cache rows replaced by their parents'."""
+        R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, beam)
+        if S != 1:
+            raise ValueError("beam steps feed one token per row")
+        for name, t, dt in (("score", score, torch.float32), ("active", active, torch.uint8),
+                            ("parent", parent, torch.int64), ("token", token, torch.int64)):  # fmt: skip
+            if t.dtype != dt or t.shape != (R,) or not t.is_contiguous():
+                raise TypeError(f"{name} must be contiguous {dt} [R]")
+        plan = self._plan(R, S, Cc, T, beam, beam)
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        args = (ptr(tokens), tokens.stride(0), ptr(offset), offset.stride(0), ptr(self_k), ptr(self_v), ptr(cross_k),
+                ptr(cross_v), ptr(enc_len), ptr(logits), ptr(new_kv), ptr(score), ptr(active), ptr(parent),
+                ptr(token))  # fmt: skip
+        fn = _lib.lib().owsm_dec_beam_step
+        dev = self.device
+
+        def run() -> None:
+            _lib.check(fn(plan, torch.cuda.current_stream(dev).cuda_stream, *args), "owsm_dec_beam_step")
+
+        run.writes_cache = True
+        run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent, token)
+        return run

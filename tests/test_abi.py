@@ -1,0 +1,56 @@
+"""The C ABI without a GPU: the library loads and exports every function include/owsm_dec.h declares,
+and the ctypes binding declares exactly those."""
+
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def declared() -> set[str]:
+    text = (ROOT / "include" / "owsm_dec.h").read_text()
+    return set(re.findall(r"\b(owsm_dec_\w+)\s*\(", text))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from owsm_trt_b200 import _lib
+    from owsm_trt_b200.build import build
+
+    build()
+    return _lib.lib()
+
+
+def test_header_declares_the_api():
+    names = declared()
+    for n in ("owsm_dec_create", "owsm_dec_plan", "owsm_dec_step", "owsm_dec_beam_step", "owsm_dec_get_error"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared():
+        assert hasattr(lib, name), name
+
+
+def test_binding_matches_header():
+    from owsm_trt_b200 import _lib
+
+    assert set(_lib.SIGNATURES) == declared()
+
+
+def test_error_codes_without_gpu(lib):
+    """Argument errors are reported as codes, not crashes (no CUDA call is made for them)."""
+    import ctypes as C
+
+    from owsm_trt_b200 import _lib
+
+    out = C.c_void_p()
+    assert lib.owsm_dec_create(None, None, 0, 0, C.byref(out)) == _lib.ERR_ARG
+    assert b"null" in lib.owsm_dec_last_error()
+    dims = _lib.Dims(2, 100, 2, 64, 10, 16, 1e-12, 10.0)  # head size 50: refused
+    w = _lib.Weights()
+    assert lib.owsm_dec_create(C.byref(dims), C.byref(w), 0, 0, C.byref(out)) == _lib.ERR_LIMIT
+    assert lib.owsm_dec_plan(None, 1, 1, 1, 1, 1, 0, C.byref(out)) == _lib.ERR_ARG
+    assert lib.owsm_dec_get_error(None) == _lib.ERR_ARG

@@ -124,6 +124,13 @@ int owsm_dec_plan_reset(OwsmDecPlan* p);
 /* Plan facts for callers and tests: programs (CTAs), ring slots, bytes of scratch. */
 int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int64_t* scratch_bytes);
 
+/* Profiling: %globaltimer stamps of later calls of this plan into `stamps` (device, uint64
+ * [stages][programs][4]: stage start, stage end, grid-barrier exit, ns spent waiting for ring slots in the stage), or NULL to
+ * stop. The stage count of a call is owsm_dec_plan_stages(p, beam_call). Mirrors the megakernels' TS option
+ * (src/owsm_trt/megakernel.py:421-422, :612-614). */
+int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps);
+int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call);
+
 /* Testing hook: the in-kernel wait limit (polls) of later calls on this handle; 0 restores the default. */
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
 

@@ -42,6 +42,8 @@ SIGNATURES = {
     "owsm_dec_get_error": (i32, [vp]),
     "owsm_dec_plan_reset": (i32, [vp]),
     "owsm_dec_plan_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i64)]),
+    "owsm_dec_plan_trace": (i32, [vp, vp]),
+    "owsm_dec_plan_stages": (i32, [vp, i32]),
     "owsm_dec_set_max_spin": (i32, [vp, u32]),
     "owsm_dec_last_error": (C.c_char_p, []),
 }

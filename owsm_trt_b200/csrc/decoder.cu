@@ -34,7 +34,7 @@
 namespace owsm {
 
 constexpr int DK = 64;                 // head size (every OWSM model)
-constexpr int NWARP = 8;               // consumer warps
+constexpr int NWARP = 7;               // consumer warps (+1 producer: 8 warps, 2 per SM sub-partition)
 constexpr int NTHR = NWARP * 32;       // consumer threads
 constexpr int BLOCK = NTHR + 32;       // + producer warp
 constexpr int SLOT = 32768;            // ring slot bytes
@@ -53,12 +53,15 @@ struct GemmW {
   const float* b;   // [layer][N]
   int N, K, NB;     // output rows, input features, 16-row blocks
   long long lstride;  // uint4 elements per layer
+  int bstride;        // uint4 elements per 16-row block: K/16 k-blocks x 32 lanes + the block's 16 fp32 biases
 };
 
 struct PlanDev {
   int L, D, H, F, V, max_pos;
   float eps, xscale;
   int R, S, M, NT, C, T, G, U, beam, P, nslot;
+  int slot, apos;  // ring slot bytes, attention positions per chunk (slot / 128)
+  int sstride;     // bytes between slots: slot + room for a block's 64-byte bias tail
   uint32_t max_spin;
   const __half* emb;
   const float* pe;
@@ -83,7 +86,10 @@ struct PlanDev {
   __half* tmpk;   // reorder staging [L][R][H][C][DK]
   __half* tmpv;
   int Qmax;           // queries of the largest attention unit
+  unsigned long long* ts;  // optional stamps [stage][P][4] (profiling), NULL = off
   int off_pre, off_out, off_ring, off_work;  // shared-memory layout (bytes)
+  int off_sched, off_rows;  // this CTA's block lists and the rows' cache offsets (shared memory)
+  int inflight;             // bulk copies in flight per CTA (ring slots may hold more, finished)
 };
 
 struct CallArgs {
@@ -119,10 +125,32 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint4& a, uint32_t
       : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ int row_off(const PlanDev& pd, const CallArgs& a, int r) {
+__device__ __forceinline__ int row_off_global(const PlanDev& pd, const CallArgs& a, int r) {
   long long o = a.off[(long long)r * a.off_stride];
   long long hi = pd.C - pd.S;
   return (int)(o < 0 ? 0 : (o > hi ? hi : o));
+}
+
+// Per-CTA facts staged in shared memory at kernel start, so no stage waits on a global load for them
+// (under full weight streaming an L2 round trip costs microseconds): the CTA's 16-row blocks per GEMM
+// (so[gi] .. so[gi + 1] index sb) and every row's clamped cache offset.
+struct Ctx {
+  const int* so;
+  const int* sb;
+  const int* offs;
+  unsigned long long* ev;  // profiling: event stamps of this CTA (thread 0), NULL = off
+  int* nev;                // shared-memory event counter
+};
+
+constexpr int NEV = 128;  // events per CTA in the profiling log
+__device__ __forceinline__ void event(const Ctx& cx, int tag) {
+  if (cx.ev && threadIdx.x == 0 && *cx.nev < NEV - 1) {
+    long long clk;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
+    cx.ev[*cx.nev] = (globaltimer() << 8) | (unsigned)tag;
+    cx.ev[*cx.nev + 1] = (unsigned long long)clk;
+    *cx.nev += 2;
+  }
 }
 
 __device__ __forceinline__ int utt_len(const PlanDev& pd, const CallArgs& a, int u) {
@@ -213,7 +241,8 @@ __device__ __forceinline__ int gemm_of(Kind k) {
 // Chunk enumeration shared by the producer (issues the copies) and the consumer (waits for them):
 // calls f(src, bytes) for every chunk of stage g on CTA c, in consumption order.
 template <class Fn>
-__device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& fr, int g, int c, Fn&& f) {
+__device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& fr, const Ctx& cx, int g, int c,
+                           Fn&& f) {
   int layer;
   Kind k = stage_kind(pd, g, layer);
   int gi = gemm_of(k);
@@ -221,13 +250,14 @@ __device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& f
     const GemmW& gw = pd.g[gi];
     int l = (k == K_OUT) ? 0 : layer;
     int kbs = gw.K >> 4;
-    int kpc = kbs < (SLOT / 512) ? kbs : (SLOT / 512);  // k-blocks per chunk
-    for (int i = pd.goff[gi][c]; i < pd.goff[gi][c + 1]; ++i) {
-      int rb = pd.gblk[gi][i];
-      const uint4* base = gw.w + (long long)l * gw.lstride + (long long)rb * kbs * 32;
+    int kpc = kbs < (pd.slot / 512) ? kbs : (pd.slot / 512);  // k-blocks per chunk
+    for (int i = cx.so[gi]; i < cx.so[gi + 1]; ++i) {
+      int rb = cx.sb[i];
+      const uint4* base = gw.w + (long long)l * gw.lstride + (long long)rb * gw.bstride;
       for (int kb0 = 0; kb0 < kbs; kb0 += kpc) {
         int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
-        f((const void*)(base + (long long)kb0 * 32), (uint32_t)n * 512);
+        // the block's biases (64 bytes) come with its last chunk
+        f((const void*)(base + (long long)kb0 * 32), (uint32_t)n * 512 + (kb0 + n == kbs ? 64u : 0u));
       }
     }
     return;
@@ -235,10 +265,10 @@ __device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& f
   if (k == K_SATT) {
     for (int u = c; u < pd.R * pd.H; u += pd.P) {
       int b = u / pd.H, h = u % pd.H;
-      int off = row_off(pd, a, b);
+      int off = cx.offs[b];
       long long base = ((((long long)layer * pd.R + b) * pd.H + h) * pd.C) * DK;
-      for (int j0 = 0; j0 < off; j0 += APOS) {
-        int n = off - j0 < APOS ? off - j0 : APOS;
+      for (int j0 = 0; j0 < off; j0 += pd.apos) {
+        int n = off - j0 < pd.apos ? off - j0 : pd.apos;
         f((const void*)(a.kc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
         f((const void*)(a.vc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
       }
@@ -250,8 +280,8 @@ __device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& f
     Piece p;
     while (next_piece(fr, f0, f1, p)) {
       long long base = ((((long long)layer * pd.U + p.u) * pd.H + p.h) * pd.T) * DK;
-      for (int j0 = p.t0; j0 < p.t1; j0 += APOS) {
-        int n = p.t1 - j0 < APOS ? p.t1 - j0 : APOS;
+      for (int j0 = p.t0; j0 < p.t1; j0 += pd.apos) {
+        int n = p.t1 - j0 < pd.apos ? p.t1 - j0 : pd.apos;
         f((const void*)(a.ck + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
         f((const void*)(a.cv + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
       }
@@ -263,18 +293,22 @@ struct Ring {
   uint64_t* full;
   uint64_t* empty;
   uint8_t* data;
-  int ns;
+  int ns, stride;
   uint32_t i;     // chunks consumed so far
   uint32_t spin;
   int* err;
   bool dead;
+  unsigned long long waited;  // ns spent waiting for slots (thread 0, when tracing)
+  bool timing;
   __device__ uint8_t* wait() {
     int s = i % ns;
+    unsigned long long t0 = timing ? globaltimer() : 0;
     if (!dead && !mbar_wait(&full[s], (i / ns) & 1, spin)) {
       dead = true;
       atomicExch(err, E_ERR_TIMEOUT);
     }
-    return data + (size_t)s * SLOT;
+    if (timing) waited += globaltimer() - t0;
+    return data + (size_t)s * stride;
   }
   __device__ void release() {  // by every consumer warp after its last read of the slot
     __syncwarp();
@@ -307,33 +341,46 @@ struct Work {  // shared-memory work area, carved per stage
   uint8_t* p;
 };
 
-// LayerNorm of the residual stream x [M][D] (eps) into B-fragment order (fp16) in shared memory.
+// LayerNorm of the residual stream x [M][D] (eps) into B-fragment order (fp16) in shared memory. One warp
+// per token; a lane holds its D / 32 values in registers (all loads issued at once: one L2 round trip).
+constexpr int MAXV4 = 8;  // D <= 1024: float4 loads per lane
 __device__ void ln_to_frag(const PlanDev& pd, __half* bbuf) {
-  const int D = pd.D, M = pd.M, NT = pd.NT;
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // zero the padding tokens' fragments
-  for (int m = M + warp; m < NT * 8; m += NWARP)
+  const int D = pd.D, M = pd.M, NT = pd.NT, nv4 = D / 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
     for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
   for (int m = warp; m < M; m += NWARP) {
-    const float* xr = pd.x + (long long)m * D;
+    const float4* xr = reinterpret_cast<const float4*>(pd.x + (long long)m * D);
+    float4 v[MAXV4];
+#pragma unroll
+    for (int i = 0; i < MAXV4; ++i)
+      if (i < nv4) v[i] = __ldcg(xr + i * 32 + lane);
     float s = 0.f;
-    for (int k = lane; k < D; k += 32) s += __ldcg(xr + k);
+#pragma unroll
+    for (int i = 0; i < MAXV4; ++i)
+      if (i < nv4) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    float mean = s / D;
-    float v = 0.f;
-    for (int k = lane; k < D; k += 32) {
-      float d = __ldcg(xr + k) - mean;
-      v += d * d;
-    }
+    const float mean = s / D;
+    float q = 0.f;
 #pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    float rstd = rsqrtf(v / D + pd.eps);
-    for (int k = lane * 2; k < D; k += 64) {
-      float2 xv = __ldcg(reinterpret_cast<const float2*>(xr + k));
-      __half2 hv = __floats2half2_rn((xv.x - mean) * rstd, (xv.y - mean) * rstd);
-      *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) = hv;
-    }
+    for (int i = 0; i < MAXV4; ++i)
+      if (i < nv4) {
+        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+        q += (a * a + b * b) + (c * c + d * d);
+      }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    const float rstd = rsqrtf(q / D + pd.eps);
+#pragma unroll
+    for (int i = 0; i < MAXV4; ++i)
+      if (i < nv4) {
+        const int k = (i * 32 + lane) * 4;
+        *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) =
+            __floats2half2_rn((v[i].x - mean) * rstd, (v[i].y - mean) * rstd);
+        *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k + 2, NT)]) =
+            __floats2half2_rn((v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
+      }
   }
 }
 
@@ -347,159 +394,250 @@ struct OutState {  // per-token running results of the output stage (shared memo
   float* tile;  // [16][M] values of the current row block
 };
 
-__device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, Kind kind, int layer, int c,
-                           uint8_t* work, OutState& os) {
+// Epilogue of one 16-row block: the CTA's reduced accumulators red[w][nt][lane][4] summed over the warps;
+// thread (nt, lane) owns rows g, g + 8 and tokens 2t, 2t + 1 of n-tile nt.
+__device__ __forceinline__ void gemm_epilogue(const PlanDev& pd, const CallArgs& a, Kind kind, const GemmW& gw,
+                                              const float (&bia)[2], int rb, const float* red, OutState& os,
+                                              const float (&xpre)[4]) {
+  const int NT = pd.NT, M = pd.M;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (kind == K_OUT && a.beam_mode) {
+    // values of the block to the tile [16][M], then one thread per token merges them
+    for (int nt = warp; nt < NT; nt += NWARP) {
+      const int ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int w = 0; w < NWARP; ++w) {
+        const float4 q = lds128f(&red[((w * NT + nt) * 32 + ln2) * 4]);
+        v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+        if (m < M) {
+          const float y = v[e] + bia[e >> 1];
+          if (n < pd.V) a.logits[(long long)m * pd.V + n] = y;
+          os.tile[row * M + m] = (n < pd.V) ? y : -INFINITY;
+        }
+      }
+    }
+    csync();
+    if (tid < M) {
+      const int m = tid;
+      const float mx = os.rmax[m];
+      float bmx = mx;
+      for (int row = 0; row < 16; ++row) bmx = fmaxf(bmx, os.tile[row * M + m]);
+      if (bmx > -INFINITY) {
+        float sm = (mx > -INFINITY ? os.rsum[m] * expf(mx - bmx) : 0.f);
+        for (int row = 0; row < 16; ++row) {
+          const float y = os.tile[row * M + m];
+          if (y > -INFINITY) sm += expf(y - bmx);
+        }
+        os.rmax[m] = bmx;
+        os.rsum[m] = sm;
+      }
+      float* tv = os.topv + m * KTOP;
+      int* ti = os.topi + m * KTOP;
+      for (int row = 0; row < 16; ++row) {
+        const float y = os.tile[row * M + m];
+        const int n = rb * 16 + row;
+        if (!(y > tv[KTOP - 1])) continue;  // ties keep the earlier (lower) index
+        int j = KTOP - 1;
+        while (j > 0 && y > tv[j - 1]) {
+          tv[j] = tv[j - 1];
+          ti[j] = ti[j - 1];
+          --j;
+        }
+        tv[j] = y;
+        ti[j] = n;
+      }
+    }
+    return;
+  }
+  for (int nt = warp; nt < NT; nt += NWARP) {  // warp-uniform: the argmax below shuffles within the warp
+  const int ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
+  float v[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < NWARP; ++w) {
+    const float4 q = lds128f(&red[((w * NT + nt) * 32 + ln2) * 4]);
+    v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+  }
+  const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
+  float xin[4] = {xpre[0], xpre[1], xpre[2], xpre[3]};  // prefetched at block start for nt == warp
+  if (res && nt != warp) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+      xin[e] = (m < M && n < gw.N) ? __ldcg(pd.x + (long long)m * pd.D + n) : 0.f;
+    }
+  }
+  float best[2] = {-INFINITY, -INFINITY};
+  int besti[2] = {0x7fffffff, 0x7fffffff};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+    if (m >= M || n >= gw.N) continue;
+    const float y = v[e] + bia[e >> 1];
+    switch (kind) {
+      case K_QKV: pd.qkv[(long long)m * 3 * pd.D + n] = __float2half_rn(y); break;
+      case K_CQ: pd.q2[(long long)m * pd.D + n] = __float2half_rn(y); break;
+      case K_F1: pd.hB[bfrag_idx(m, n, NT)] = __float2half_rn(fmaxf(y, 0.f)); break;
+      case K_WO: case K_WCO: case K_F2: pd.x[(long long)m * pd.D + n] = xin[e] + y; break;
+      case K_OUT: {
+        a.logits[(long long)m * pd.V + n] = y;
+        float ya = y;
+        if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
+        const int s = e & 1;
+        if (ya > best[s] || (ya == best[s] && n < besti[s])) {
+          best[s] = ya;
+          besti[s] = n;
+        }
+        break;
+      }
+      default: break;
+    }
+  }
+  if (kind == K_OUT) {
+    // reduce over the 8 row groups (lanes with the same t), then merge into the running best
+#pragma unroll
+    for (int s = 0; s < 2; ++s) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best[s], o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti[s], o);
+        if (ov > best[s] || (ov == best[s] && oi < besti[s])) {
+          best[s] = ov;
+          besti[s] = oi;
+        }
+      }
+      const int m = nt * 8 + 2 * t + s;
+      if (g == 0 && m < M) {
+        const float cur = os.amax[m];
+        const int ci = os.aidx[m];
+        if (best[s] > cur || (best[s] == cur && besti[s] < ci)) {
+          os.amax[m] = best[s];
+          os.aidx[m] = besti[s];
+        }
+      }
+    }
+  }
+  }
+}
+
+// B fragments (activations from global memory) of batch t of a block: KBB k-blocks x NT n-tiles per lane.
+template <int KBB, int NT>
+struct BFrag {
+  uint2 v[KBB][NT];
+};
+
+template <int KBB, int NT>
+__device__ __forceinline__ BFrag<KBB, NT> load_bfrag(const uint2* __restrict__ gsrc, int t, int bpc, int cpu, int kpc,
+                                                   int kbs, int warp, int lane) {
+  BFrag<KBB, NT> f;
+  const int ch = (t / bpc) % cpu, b = t % bpc;
+  const int kb0 = ch * kpc;
+  const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
+#pragma unroll
+  for (int jj = 0; jj < KBB; ++jj) {
+    const int kb = warp + NWARP * (b * KBB + jj);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+      f.v[jj][nt] = kb < n ? __ldcg(gsrc + ((long long)(kb0 + kb) * NT + nt) * 32 + lane) : make_uint2(0u, 0u);
+  }
+  return f;
+}
+
+// One GEMM stage on this CTA: its 16-row blocks, each streamed through the ring in chunks of k-blocks.
+// Warp w takes k-blocks w, w + 8, ... of a chunk, in batches of KBB; B fragments come from shared memory
+// (LayerNorm stages: normalised here) or from global memory (the attention outputs / FFN hidden), in which
+// case the next batch's fragments are loaded while the current batch multiplies (across chunk and block
+// boundaries, so a stage sees one L2 round trip, not one per k-block).
+template <int NT>
+__device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, Kind kind, int layer,
+                           int c, uint8_t* work, OutState& os) {
+  constexpr int KBB = NT <= 2 ? 4 : 8 / NT;
   const int gi = gemm_of(kind);
   const GemmW& gw = pd.g[gi];
-  const int nb0 = pd.goff[gi][c], nb1 = pd.goff[gi][c + 1];
+  const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
-  const int NT = pd.NT, M = pd.M;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool ln = (kind == K_QKV || kind == K_CQ || kind == K_F1 || kind == K_OUT);
   const int l = (kind == K_OUT) ? 0 : layer;
   __half* bbuf = reinterpret_cast<__half*>(work);
   float* red = reinterpret_cast<float*>(work + (ln ? (size_t)NT * (pd.D / 16) * 256 : 0));
-  const __half* gsrc = (kind == K_F2) ? pd.hB : pd.oB;
+  const uint2* gsrc = reinterpret_cast<const uint2*>((kind == K_F2) ? pd.hB : pd.oB);
   if (ln) {
     ln_to_frag(pd, bbuf);
     csync();
   }
   const int kbs = gw.K >> 4;
-  const int kpc = kbs < (SLOT / 512) ? kbs : (SLOT / 512);
-  const float* bias = gw.b + (long long)l * gw.N;
-  for (int i = nb0; i < nb1; ++i) {
-    const int rb = pd.gblk[gi][i];
-    float acc[MAXNT][4];
+  const int kpc = kbs < (pd.slot / 512) ? kbs : (pd.slot / 512);
+  const int cpu = (kbs + kpc - 1) / kpc;            // chunks per block
+  const int bpc = ((kpc + NWARP - 1) / NWARP + KBB - 1) / KBB;  // batches per chunk
+  const int per_unit = cpu * bpc;
+  const int total = (nb1 - nb0) * per_unit;
+
+  BFrag<KBB, NT> bcur, bnxt;
+  float acc[NT][4];
+  float xpre[4] = {0.f, 0.f, 0.f, 0.f};
+  float bia[2] = {0.f, 0.f};
+  const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
+  const uint4* slot = nullptr;
+  for (int t = 0; t < total; ++t) {
+    const int ch = (t / bpc) % cpu, b = t % bpc;
+    const int kb0 = ch * kpc;
+    const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
+    if (ch == 0 && b == 0) {
 #pragma unroll
-    for (int nt = 0; nt < MAXNT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-    for (int kb0 = 0; kb0 < kbs; kb0 += kpc) {
-      const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
-      const uint4* slot = reinterpret_cast<const uint4*>(ring.wait());
-      for (int kb = warp; kb < n; kb += NWARP) {
-        uint4 af = slot[kb * 32 + lane];
-        const int kg = kb0 + kb;
+      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+      if (!ln) bcur = load_bfrag<KBB, NT>(gsrc, t, bpc, cpu, kpc, kbs, warp, lane);  // (within a block only)
+      if (res && warp < NT) {  // this warp's epilogue residuals, loaded with the B fragments
+        const int rb = cx.sb[nb0 + t / per_unit], g = lane >> 2, tt = lane & 3;
 #pragma unroll
-        for (int nt = 0; nt < MAXNT; ++nt) {
-          if (nt < NT) {
-            uint2 bf;
-            long long bi = (((long long)kg * NT + nt) * 32 + lane) * 4;
-            if (ln) bf = *reinterpret_cast<const uint2*>(bbuf + bi);
-            else bf = __ldcg(reinterpret_cast<const uint2*>(gsrc + bi));
-            mma16816(acc[nt], af, bf.x, bf.y);
-          }
-        }
-      }
-      ring.release();
-    }
-    // reduce over warps
-#pragma unroll
-    for (int nt = 0; nt < MAXNT; ++nt)
-      if (nt < NT)
-        *reinterpret_cast<float4*>(&red[((warp * NT + nt) * 32 + lane) * 4]) =
-            make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
-    csync();
-    const int tid = threadIdx.x;
-    if (kind == K_OUT && a.beam_mode) {
-      // values of the block to the tile [16][M], then one thread per token merges them
-      if (tid < NT * 32) {
-        int nt = tid >> 5, ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int w = 0; w < NWARP; ++w) {
-          float4 q = *reinterpret_cast<const float4*>(&red[((w * NT + nt) * 32 + ln2) * 4]);
-          v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
-        }
         for (int e = 0; e < 4; ++e) {
-          int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
-          if (m < M) {
-            float y = v[e] + (n < gw.N ? bias[n] : 0.f);
-            if (n < pd.V) a.logits[(long long)m * pd.V + n] = y;
-            os.tile[row * M + m] = (n < pd.V) ? y : -INFINITY;
-          }
-        }
-      }
-      csync();
-      if (tid < M) {
-        int m = tid;
-        float mx = os.rmax[m], sm = os.rsum[m];
-        float bmx = mx;
-        for (int row = 0; row < 16; ++row) bmx = fmaxf(bmx, os.tile[row * M + m]);
-        if (bmx > -INFINITY) {
-          sm = (mx > -INFINITY ? sm * expf(mx - bmx) : 0.f);
-          for (int row = 0; row < 16; ++row) {
-            float y = os.tile[row * M + m];
-            if (y > -INFINITY) sm += expf(y - bmx);
-          }
-          os.rmax[m] = bmx;
-          os.rsum[m] = sm;
-        }
-        float* tv = os.topv + m * KTOP;
-        int* ti = os.topi + m * KTOP;
-        for (int row = 0; row < 16; ++row) {
-          float y = os.tile[row * M + m];
-          int n = rb * 16 + row;
-          if (!(y > tv[KTOP - 1])) continue;  // ties keep the earlier (lower) index
-          int j = KTOP - 1;
-          while (j > 0 && y > tv[j - 1]) { tv[j] = tv[j - 1]; ti[j] = ti[j - 1]; --j; }
-          tv[j] = y; ti[j] = n;
-        }
-      }
-      csync();
-      continue;
-    }
-    if (tid < NT * 32) {
-      const int nt = tid >> 5, ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int w = 0; w < NWARP; ++w) {
-        float4 q = *reinterpret_cast<const float4*>(&red[((w * NT + nt) * 32 + ln2) * 4]);
-        v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
-      }
-      float best[2] = {-INFINITY, -INFINITY};
-      int besti[2] = {0x7fffffff, 0x7fffffff};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
-        if (m >= M || n >= gw.N) continue;
-        float y = v[e] + bias[n];
-        switch (kind) {
-          case K_QKV: pd.qkv[(long long)m * 3 * pd.D + n] = __float2half_rn(y); break;
-          case K_CQ: pd.q2[(long long)m * pd.D + n] = __float2half_rn(y); break;
-          case K_F1: pd.hB[bfrag_idx(m, n, NT)] = __float2half_rn(fmaxf(y, 0.f)); break;
-          case K_WO: case K_WCO: case K_F2: {
-            float* xp = pd.x + (long long)m * pd.D + n;
-            *xp = __ldcg(xp) + y;
-            break;
-          }
-          case K_OUT: {
-            a.logits[(long long)m * pd.V + n] = y;
-            float ya = y;
-            if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
-            int s = e & 1;
-            if (ya > best[s] || (ya == best[s] && n < besti[s])) { best[s] = ya; besti[s] = n; }
-            break;
-          }
-          default: break;
-        }
-      }
-      if (kind == K_OUT) {
-        // reduce over the 8 row groups (lanes with the same t), then merge into the running best
-#pragma unroll
-        for (int s = 0; s < 2; ++s) {
-#pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            float ov = __shfl_xor_sync(0xffffffffu, best[s], o);
-            int oi = __shfl_xor_sync(0xffffffffu, besti[s], o);
-            if (ov > best[s] || (ov == best[s] && oi < besti[s])) { best[s] = ov; besti[s] = oi; }
-          }
-          const int m = nt * 8 + 2 * t + s;
-          if (g == 0 && m < M) {
-            float cur = os.amax[m];
-            int ci = os.aidx[m];
-            if (best[s] > cur || (best[s] == cur && besti[s] < ci)) { os.amax[m] = best[s]; os.aidx[m] = besti[s]; }
-          }
+          const int row = g + (e >> 1) * 8, m = warp * 8 + 2 * tt + (e & 1), n = rb * 16 + row;
+          xpre[e] = (m < pd.M && n < gw.N) ? __ldcg(pd.x + (long long)m * pd.D + n) : 0.f;
         }
       }
     }
-    csync();
+    if (b == 0) {
+      if (kind == K_OUT) event(cx, 1);
+      slot = reinterpret_cast<const uint4*>(ring.wait());
+      if (kind == K_OUT) event(cx, 2);
+    }
+    if (!ln && (t + 1) % per_unit != 0) bnxt = load_bfrag<KBB, NT>(gsrc, t + 1, bpc, cpu, kpc, kbs, warp, lane);
+#pragma unroll
+    for (int jj = 0; jj < KBB; ++jj) {
+      const int kb = warp + NWARP * (b * KBB + jj);
+      if (kb < n) {
+        const uint4 af = lds128(slot + kb * 32 + lane);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          uint2 bf;
+          if (ln) bf = lds64(bbuf + (((kb0 + kb) * NT + nt) * 32 + lane) * 4);
+          else bf = bcur.v[jj][nt];
+          mma16816(acc[nt], af, bf.x, bf.y);
+        }
+      }
+    }
+    if (!ln) bcur = bnxt;
+    if (ch == cpu - 1 && b == bpc - 1 && warp < NT) {  // the block's biases (rows g, g + 8) from the slot tail
+      const float* tail = reinterpret_cast<const float*>(slot + n * 32);
+      bia[0] = tail[lane >> 2];
+      bia[1] = tail[(lane >> 2) + 8];
+    }
+    if (b == bpc - 1) ring.release();
+    if (kind == K_OUT && b == bpc - 1) event(cx, 3);
+    if (ch == cpu - 1 && b == bpc - 1) {  // block done: reduce over warps, epilogue
+      const int rb = cx.sb[nb0 + t / per_unit];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        sts128f(&red[((warp * NT + nt) * 32 + lane) * 4], make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+      csync();
+      if (kind == K_OUT) event(cx, 4);
+      gemm_epilogue(pd, a, kind, gw, bia, rb, red, os, xpre);
+      if (kind == K_OUT) event(cx, 5);
+      csync();
+      if (kind == K_OUT) event(cx, 6);
+    }
   }
 }
 
@@ -607,6 +745,7 @@ struct AttnSmem {
   float* lrun;
   float* alpha;
   float* knew;   // [MAXQ][64] (self-attention: the new keys, fp32)
+  float* vnew;   // [MAXQ][64] (self-attention: the new values, fp32)
   float* out;    // [MAXQ][64]
   float* scratch;  // [NWARP][MAXQ][64]
   int* flag;
@@ -621,6 +760,7 @@ __device__ AttnSmem carve_attn(uint8_t* work, int Q) {
   s.lrun = p; p += MAXQ;
   s.alpha = p; p += MAXQ;
   s.knew = p; p += Q * DK;
+  s.vnew = p; p += Q * DK;
   s.out = p; p += Q * DK;
   s.scratch = p; p += NWARP * Q * DK;
   s.flag = reinterpret_cast<int*>(p);
@@ -629,29 +769,31 @@ __device__ AttnSmem carve_attn(uint8_t* work, int Q) {
 
 // Bytes of carve_attn(Q).
 __host__ __device__ constexpr size_t attn_smem(int Q) {
-  return sizeof(float) * ((size_t)Q * DK * 3 + (size_t)Q * APOS + 3 * MAXQ + (size_t)NWARP * Q * DK) + 16;
+  return sizeof(float) * ((size_t)Q * DK * 4 + (size_t)Q * APOS + 3 * MAXQ + (size_t)NWARP * Q * DK) + 16;
 }
 
-__device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, int layer, int c, uint8_t* work) {
+__device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, int layer, int c,
+                                uint8_t* work) {
   AttnSmem s = carve_attn(work, pd.Qmax);
   const int S = pd.S, D = pd.D, H = pd.H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int u = c; u < pd.R * H; u += pd.P) {
     const int b = u / H, h = u % H;
-    const int off = row_off(pd, a, b);
+    const int off = cx.offs[b];
     for (int idx = threadIdx.x; idx < S * DK; idx += NTHR) {
       int q = idx / DK, d = idx % DK;
       const __half* row = pd.qkv + (long long)(b * S + q) * 3 * D + h * DK + d;
       s.q[q * DK + d] = __half2float(__ldcg(row)) * 0.125f;
       s.knew[q * DK + d] = __half2float(__ldcg(row + D));
+      s.vnew[q * DK + d] = __half2float(__ldcg(row + 2 * D));
     }
     if (threadIdx.x < S) { s.mrun[threadIdx.x] = -INFINITY; s.lrun[threadIdx.x] = 0.f; }
     AttnAcc acc;
 #pragma unroll
     for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
     csync();
-    for (int j0 = 0; j0 < off; j0 += APOS) {
-      const int npos = off - j0 < APOS ? off - j0 : APOS;
+    for (int j0 = 0; j0 < off; j0 += pd.apos) {
+      const int npos = off - j0 < pd.apos ? off - j0 : pd.apos;
       const __half* kt = reinterpret_cast<const __half*>(ring.wait());
       attn_scores(s.q, kt, npos, S, s.sc);
       ring.release();
@@ -678,8 +820,7 @@ __device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring
       for (int q = 0; q < MAXQ; ++q)
         if (q < S) { acc.o[q][0] *= s.alpha[q]; acc.o[q][1] *= s.alpha[q]; }
       for (int j = warp; j < S; j += NWARP) {
-        const __half* vr = pd.qkv + (long long)(b * S + j) * 3 * D + 2 * D + h * DK;
-        float2 v = __half22float2(__ldcg(reinterpret_cast<const __half2*>(vr) + lane));
+        const float2 v = make_float2(s.vnew[j * DK + 2 * lane], s.vnew[j * DK + 2 * lane + 1]);
 #pragma unroll
         for (int q = 0; q < MAXQ; ++q)
           if (q < S) {
@@ -697,9 +838,9 @@ __device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring
       int m = b * S + q;
       *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
           __floats2half2_rn(s.out[q * DK + d] * inv, s.out[q * DK + d + 1] * inv);
-      const __half* row = pd.qkv + (long long)m * 3 * D + h * DK + d;
-      __half2 kn = __ldcg(reinterpret_cast<const __half2*>(row + D));
-      __half2 vn = __ldcg(reinterpret_cast<const __half2*>(row + 2 * D));
+      // (fp16 -> fp32 -> fp16 is exact: the cache gets the projection's fp16 values)
+      const __half2 kn = __floats2half2_rn(s.knew[q * DK + d], s.knew[q * DK + d + 1]);
+      const __half2 vn = __floats2half2_rn(s.vnew[q * DK + d], s.vnew[q * DK + d + 1]);
       long long cslot = ((((long long)layer * pd.R + b) * H + h) * pd.C + off + q) * DK + d;
       *reinterpret_cast<__half2*>(a.kc + cslot) = kn;
       *reinterpret_cast<__half2*>(a.vc + cslot) = vn;
@@ -730,8 +871,8 @@ __device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& rin
 #pragma unroll
     for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
     csync();
-    for (int j0 = p.t0; j0 < p.t1; j0 += APOS) {
-      const int npos = p.t1 - j0 < APOS ? p.t1 - j0 : APOS;
+    for (int j0 = p.t0; j0 < p.t1; j0 += pd.apos) {
+      const int npos = p.t1 - j0 < pd.apos ? p.t1 - j0 : pd.apos;
       const __half* kt = reinterpret_cast<const __half*>(ring.wait());
       attn_scores(s.q, kt, npos, Q, s.sc);
       ring.release();
@@ -764,23 +905,56 @@ __device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& rin
     }
     csync();
     if (*s.flag) {
+      // combine the contributors' partials in rank order, RT at a time staged in shared memory
       const float* base = pd.xpart + ((long long)seg * pd.P * Q) * (DK + 2);
-      for (int idx = threadIdx.x; idx < Q * (DK / 2); idx += NTHR) {
-        int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
-        float mx = -INFINITY;
-        for (int r = 0; r < ncontrib; ++r) mx = fmaxf(mx, __ldcg(base + ((long long)r * Q + q) * (DK + 2) + DK));
-        float num0 = 0.f, num1 = 0.f, den = 0.f;
-        for (int r = 0; r < ncontrib; ++r) {
-          const float* pr = base + ((long long)r * Q + q) * (DK + 2);
-          float mr = __ldcg(pr + DK);
-          float w = mr > -INFINITY ? expf(mr - mx) : 0.f;
-          den += w * __ldcg(pr + DK + 1);
-          num0 += w * __ldcg(pr + d);
-          num1 += w * __ldcg(pr + d + 1);
+      const int RT = (NWARP * DK) / (DK + 2);  // contributors per tile (scratch holds NWARP * Q * 64 floats)
+      float* mx = s.mrun;
+      float* den = s.lrun;
+      if (threadIdx.x < Q) { mx[threadIdx.x] = -INFINITY; den[threadIdx.x] = 0.f; }
+      for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) s.out[idx] = 0.f;
+      csync();
+      for (int r0 = 0; r0 < ncontrib; r0 += RT) {
+        const int nr = ncontrib - r0 < RT ? ncontrib - r0 : RT;
+        const float* src = base + (long long)r0 * Q * (DK + 2);
+        const int nval = nr * Q * (DK + 2);
+#pragma unroll 4
+        for (int idx = threadIdx.x; idx < nval; idx += NTHR) s.scratch[idx] = __ldcg(src + idx);
+        csync();
+        // thread (q, d): new running max from the tile, rescale, accumulate
+        for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
+          const int q = idx / DK, d = idx % DK;
+          float m1 = mx[q];
+          for (int r = 0; r < nr; ++r) m1 = fmaxf(m1, s.scratch[(r * Q + q) * (DK + 2) + DK]);
+          const float al = mx[q] > -INFINITY ? expf(mx[q] - m1) : 0.f;
+          float num = s.out[idx] * al;
+          for (int r = 0; r < nr; ++r) {
+            const float* pr = s.scratch + (r * Q + q) * (DK + 2);
+            const float mr = pr[DK];
+            if (mr > -INFINITY) num += expf(mr - m1) * pr[d];
+          }
+          s.out[idx] = num;
         }
-        int m = u * Q + q;
+        csync();
+        if (threadIdx.x < Q) {
+          const int q = threadIdx.x;
+          float m1 = mx[q];
+          for (int r = 0; r < nr; ++r) m1 = fmaxf(m1, s.scratch[(r * Q + q) * (DK + 2) + DK]);
+          float dd = mx[q] > -INFINITY ? den[q] * expf(mx[q] - m1) : 0.f;
+          for (int r = 0; r < nr; ++r) {
+            const float* pr = s.scratch + (r * Q + q) * (DK + 2);
+            if (pr[DK] > -INFINITY) dd += expf(pr[DK] - m1) * pr[DK + 1];
+          }
+          mx[q] = m1;
+          den[q] = dd;
+        }
+        csync();
+      }
+      for (int idx = threadIdx.x; idx < Q * (DK / 2); idx += NTHR) {
+        const int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
+        const float inv = 1.f / den[q];
+        const int m = u * Q + q;
         *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
-            __floats2half2_rn(num0 / den, num1 / den);
+            __floats2half2_rn(s.out[q * DK + d] * inv, s.out[q * DK + d + 1] * inv);
       }
       if (threadIdx.x == 0) atomicExch(&pd.xcnt[seg], 0u);
     }
@@ -789,7 +963,7 @@ __device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& rin
 }
 
 // ------------------------------------------------------------------------------------------------ other stages
-__device__ void embed_stage(const PlanDev& pd, const CallArgs& a, int c) {
+__device__ void embed_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
   const long long total = (long long)pd.M * pd.D;
   const long long lo = total * c / pd.P, hi = total * (c + 1) / pd.P;
   for (long long i = lo + threadIdx.x; i < hi; i += NTHR) {
@@ -797,14 +971,15 @@ __device__ void embed_stage(const PlanDev& pd, const CallArgs& a, int c) {
     int r = m / pd.S, s = m % pd.S;
     long long t = a.tok[(long long)r * a.tok_stride + s];
     t = t < 0 ? 0 : (t >= pd.V ? pd.V - 1 : t);
-    long long pos = (long long)row_off(pd, a, r) + s;
+    long long pos = (long long)cx.offs[r] + s;
     pos = pos >= pd.max_pos ? pd.max_pos - 1 : pos;
     pd.x[i] = __half2float(pd.emb[t * pd.D + n]) * pd.xscale + pd.pe[pos * pd.D + n];
   }
 }
 
-// After the output stage: per-CTA argmax partials -> global; the last CTA to arrive reduces them.
-__device__ void argmax_finish(const PlanDev& pd, const CallArgs& a, int c, OutState& os, int* flag) {
+// After the output stage: per-CTA argmax partials -> global; the last CTA to arrive reduces them (all
+// partials loaded into shared memory at once, then a warp per token).
+__device__ void argmax_finish(const PlanDev& pd, const CallArgs& a, int c, OutState& os, int* flag, uint8_t* work) {
   for (int m = threadIdx.x; m < pd.M; m += NTHR) {
     __stcg(pd.amax + (long long)c * pd.M + m, os.amax[m]);
     __stcg(pd.aidx + (long long)c * pd.M + m, os.aidx[m]);
@@ -814,16 +989,31 @@ __device__ void argmax_finish(const PlanDev& pd, const CallArgs& a, int c, OutSt
   if (threadIdx.x == 0) *flag = (atom_acq_rel_add(&pd.ctr[2], 1) == (uint32_t)(pd.P - 1));
   csync();
   if (!*flag) return;
-  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+  const int n = pd.P * pd.M;
+  float* sv = reinterpret_cast<float*>(work);
+  int* si = reinterpret_cast<int*>(sv + n);
+#pragma unroll 4
+  for (int i = threadIdx.x; i < n; i += NTHR) {
+    sv[i] = __ldcg(pd.amax + i);
+    si[i] = __ldcg(pd.aidx + i);
+  }
+  csync();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int m = warp; m < pd.M; m += NWARP) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int q = 0; q < pd.P; ++q) {
-      float v = __ldcg(pd.amax + (long long)q * pd.M + m);
-      int i = __ldcg(pd.aidx + (long long)q * pd.M + m);
+    for (int q = lane; q < pd.P; q += 32) {
+      const float v = sv[q * pd.M + m];
+      const int i = si[q * pd.M + m];
       if (v > best || (v == best && i < bi)) { best = v; bi = i; }
     }
-    if (bi == 0x7fffffff) bi = 0;
-    a.pred[(long long)(m / pd.S) * pd.S + (m % pd.S)] = bi;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    if (lane == 0) a.pred[m] = bi == 0x7fffffff ? 0 : bi;
   }
   if (threadIdx.x == 0) atomicExch(&pd.ctr[2], 0u);
 }
@@ -841,77 +1031,96 @@ __device__ void beam_partials(const PlanDev& pd, int c, OutState& os) {
 
 constexpr float LOG_ZERO = -1.0e10f;
 
-// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials, candidates
-// score + (logit - lse) from every CTA's per-row top-K (LOG_ZERO for inactive rows), top-`beam` by
-// (value desc, flat index asc); candidates are scanned in place, the picks kept in shared memory.
+// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials (a warp per
+// row), candidates score + (logit - lse) from every CTA's per-row top-K staged in shared memory
+// (LOG_ZERO for inactive rows), top-`beam` by (value desc, flat index asc).
 __device__ void select_stage(const PlanDev& pd, const CallArgs& a, int c, uint8_t* work) {
   const int K = pd.beam, V = pd.V, P = pd.P;
   const int B = pd.R / K;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* lmx = reinterpret_cast<float*>(work);  // [KTOP] row max of the logits
   float* lse = lmx + KTOP;                      // [KTOP] log of the row's sum of exp(logit - max)
   float* pickv = lse + KTOP;                    // [KTOP]
   float* rv = pickv + KTOP;                     // [NTHR]
   int* ri = reinterpret_cast<int*>(rv + NTHR);  // [NTHR]
   int* picked = ri + NTHR;                      // [KTOP]
+  float* cv = reinterpret_cast<float*>(picked + KTOP);  // [K][P*K + K] candidate values
   const int per_row = P * K + K;
   const int ncand = K * per_row;
+  int* ci = reinterpret_cast<int*>(cv + ncand);  // flat indices
   for (int u = c; u < B; u += P) {
-    for (int k = threadIdx.x; k < K; k += NTHR) {
+    for (int k = warp; k < K; k += NWARP) {
       const int r = u * K + k;
       float mx = -INFINITY;
-      for (int q = 0; q < P; ++q) mx = fmaxf(mx, __ldcg(pd.lmax + (long long)q * pd.M + r));
+      for (int q = lane; q < P; q += 32) mx = fmaxf(mx, __ldcg(pd.lmax + (long long)q * pd.M + r));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       float sm = 0.f;
-      for (int q = 0; q < P; ++q) {
-        float mq = __ldcg(pd.lmax + (long long)q * pd.M + r);
+      for (int q = lane; q < P; q += 32) {
+        const float mq = __ldcg(pd.lmax + (long long)q * pd.M + r);
         if (mq > -INFINITY) sm += __ldcg(pd.lsum + (long long)q * pd.M + r) * expf(mq - mx);
       }
-      lmx[k] = mx;
-      lse[k] = logf(sm);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
+      if (lane == 0) {
+        lmx[k] = mx;
+        lse[k] = logf(sm);
+      }
+    }
+    csync();
+#pragma unroll 4
+    for (int idx = threadIdx.x; idx < ncand; idx += NTHR) {
+      const int k = idx / per_row, j = idx % per_row;
+      const int r = u * K + k;
+      const bool act = a.active[r] != 0;
+      float v = -INFINITY;
+      int fi = 0x7fffffff;
+      if (j < P * K) {
+        if (act) {
+          const int q = j / K, e = j % K;
+          const float lv = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
+          if (lv > -INFINITY) {
+            v = a.score[r] + ((lv - lmx[k]) - lse[k]);  // log_softmax = (x - max) - log(sum)
+            fi = k * V + __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
+          }
+        }
+      } else if (!act) {
+        v = LOG_ZERO;
+        fi = k * V + (j - P * K);
+      }
+      cv[idx] = v;
+      ci[idx] = fi;
     }
     csync();
     for (int sel = 0; sel < K; ++sel) {
       float bv = -INFINITY;
-      int bi = 0x7fffffff;
+      int bi = 0x7fffffff, bp = -1;
       for (int idx = threadIdx.x; idx < ncand; idx += NTHR) {
-        const int k = idx / per_row, j = idx % per_row;
-        const int r = u * K + k;
-        const bool act = a.active[r] != 0;
-        float v;
-        int fi;
-        if (j < P * K) {
-          if (!act) continue;
-          const int q = j / K, e = j % K;
-          const float lv = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
-          if (!(lv > -INFINITY)) continue;
-          v = a.score[r] + ((lv - lmx[k]) - lse[k]);  // log_softmax = (x - max) - log(sum)
-          fi = k * V + __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
-        } else {
-          if (act) continue;
-          v = LOG_ZERO;
-          fi = k * V + (j - P * K);
-        }
-        bool taken = false;
-        for (int t = 0; t < sel; ++t) taken |= (picked[t] == fi);
-        if (taken) continue;
-        if (v > bv || (v == bv && fi < bi)) { bv = v; bi = fi; }
+        const float v = cv[idx];
+        const int fi = ci[idx];
+        if (fi != 0x7fffffff && (v > bv || (v == bv && fi < bi))) { bv = v; bi = fi; bp = idx; }
       }
-      rv[threadIdx.x] = bv;
-      ri[threadIdx.x] = bi;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const int op = __shfl_xor_sync(0xffffffffu, bp, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bp = op; }
+      }
+      if (lane == 0) {
+        rv[warp] = bv;
+        ri[warp] = bi;
+        ri[NWARP + warp] = bp;
+      }
       csync();
-      for (int st = NTHR / 2; st > 0; st >>= 1) {
-        if (threadIdx.x < st) {
-          const float ov = rv[threadIdx.x + st];
-          const int oi = ri[threadIdx.x + st];
-          if (ov > rv[threadIdx.x] || (ov == rv[threadIdx.x] && oi < ri[threadIdx.x])) {
-            rv[threadIdx.x] = ov;
-            ri[threadIdx.x] = oi;
-          }
-        }
-        csync();
-      }
       if (threadIdx.x == 0) {
-        picked[sel] = ri[0];
-        pickv[sel] = rv[0];
+        float v0 = rv[0];
+        int i0 = ri[0], p0 = ri[NWARP];
+        for (int w = 1; w < NWARP; ++w)
+          if (rv[w] > v0 || (rv[w] == v0 && ri[w] < i0)) { v0 = rv[w]; i0 = ri[w]; p0 = ri[NWARP + w]; }
+        picked[sel] = i0;
+        pickv[sel] = v0;
+        if (p0 >= 0) ci[p0] = 0x7fffffff;  // taken
       }
       csync();
     }
@@ -927,8 +1136,13 @@ __device__ void select_stage(const PlanDev& pd, const CallArgs& a, int c, uint8_
   }
 }
 
+// Bytes of the select stage's shared memory.
+__host__ __device__ constexpr size_t select_smem(int K, int P) {
+  return sizeof(float) * (3 * KTOP + 2 * NTHR + KTOP) + (size_t)K * (P * K + K) * 8;
+}
+
 // Cache reorder (BeamSession._select: buf.index_select(1, parent)), in two stages through a staging copy.
-__device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, int c, bool to_tmp) {
+__device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, bool to_tmp) {
   const int N = pd.R, H = pd.H;
   const long long units = (long long)pd.L * N * H;
   for (long long uidx = c; uidx < units; uidx += pd.P) {
@@ -937,7 +1151,7 @@ __device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, int c, bool 
     int l = (int)(uidx / ((long long)H * N));
     int par = (int)__ldcg(reinterpret_cast<const long long*>(a.parent) + r);
     if (par == r || par < 0 || par >= N) continue;
-    int len = row_off(pd, a, par) + pd.S;
+    int len = cx.offs[par] + pd.S;
     long long src = ((((long long)l * N + par) * H + h) * pd.C) * DK;
     long long dst = ((((long long)l * N + r) * H + h) * pd.C) * DK;
     long long n16 = (long long)len * DK * 2 / 16;
@@ -946,6 +1160,7 @@ __device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, int c, bool 
       __half* tmp = kv ? pd.tmpv : pd.tmpk;
       const uint4* s = reinterpret_cast<const uint4*>(to_tmp ? cache + src : tmp + dst);
       uint4* d = reinterpret_cast<uint4*>(to_tmp ? tmp + dst : cache + dst);
+#pragma unroll 4
       for (long long i = threadIdx.x; i < n16; i += NTHR) d[i] = __ldcg(s + i);
     }
   }
@@ -967,8 +1182,11 @@ __device__ OutState carve_out(uint8_t* p, int M) {
 
 __host__ __device__ constexpr size_t out_smem(int M) { return sizeof(float) * ((size_t)M * (4 + 2 * KTOP) + 16 * M); }
 
-__global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __restrict__ pdp, CallArgs a) {
-  const PlanDev& pd = *pdp;
+// The plan and the call's pointers are __grid_constant__ parameters: read from the constant bank where used,
+// not held in registers across the stage loop.
+template <int NT>
+__global__ void __launch_bounds__(BLOCK, 1)
+    decoder_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAXSLOT;
@@ -979,6 +1197,9 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_stages = 8 * pd.L + 2 + (a.beam_mode ? 3 : 0);
 
+  int* so = reinterpret_cast<int*>(smem + pd.off_sched);
+  int* sb = so + NGEMM + 1;
+  int* offs = reinterpret_cast<int*>(smem + pd.off_rows);
   if (threadIdx.x == 0) {
     for (int s = 0; s < pd.nslot; ++s) {
       mbar_init(&full[s], 1);
@@ -987,8 +1208,21 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
     fence_barrier_init();
     pre[0] = 0;
     for (int u = 0; u < pd.U; ++u) pre[u + 1] = pre[u] + utt_len(pd, a, u);
+    so[0] = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) so[gi + 1] = so[gi] + (pd.goff[gi][c + 1] - pd.goff[gi][c]);
+  }
+  for (int r = threadIdx.x; r < pd.R; r += BLOCK) offs[r] = row_off_global(pd, a, r);
+  __syncthreads();
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const int base = pd.goff[gi][c];
+    for (int i = threadIdx.x; i < so[gi + 1] - so[gi]; i += BLOCK) sb[so[gi] + i] = pd.gblk[gi][base + i];
   }
   __syncthreads();
+  unsigned long long* evlog =
+      pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
+  int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
+  if (threadIdx.x == 0) *nev = 0;
+  const Ctx cx{so, sb, offs, evlog, nev};
   Frames fr;
   fr.total = (long long)pd.H * pre[pd.U];
   fr.U = pd.U;
@@ -1002,7 +1236,7 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
       uint32_t i = 0;
       bool dead = false;
       for (int g = 0; g < n_stages && !dead; ++g) {
-        for_chunks(pd, a, fr, g, c, [&](const void* src, uint32_t bytes) {
+        for_chunks(pd, a, fr, cx, g, c, [&](const void* src, uint32_t bytes) {
           if (dead) return;
           const int s = i % pd.nslot;
           if (!mbar_wait(&empty[s], ((i / pd.nslot) & 1) ^ 1, pd.max_spin)) {
@@ -1010,8 +1244,18 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
             atomicExch(pd.err, E_ERR_TIMEOUT);
             return;
           }
+          // at most `inflight` copies outstanding: the rest of the memory system stays responsive to the
+          // consumers' small loads (their latency grows with the bytes queued ahead of them)
+          if (i >= (uint32_t)pd.inflight) {
+            const uint32_t j = i - pd.inflight;
+            if (!mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, pd.max_spin)) {
+              dead = true;
+              atomicExch(pd.err, E_ERR_TIMEOUT);
+              return;
+            }
+          }
           mbar_arrive_expect_tx(&full[s], bytes);
-          bulk_g2s(ringdata + (size_t)s * SLOT, src, bytes, &full[s], pol);
+          bulk_g2s(ringdata + (size_t)s * pd.sstride, src, bytes, &full[s], pol);
           ++i;
         });
       }
@@ -1024,7 +1268,7 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
     return;
   }
 
-  Ring ring{full, empty, ringdata, pd.nslot, 0, pd.max_spin, pd.err, false};
+  Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
   OutState os = carve_out(smem + pd.off_out, pd.M);
   for (int m = threadIdx.x; m < pd.M; m += NTHR) {
     os.amax[m] = -INFINITY;
@@ -1041,21 +1285,29 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
   for (int g = 0; g < n_stages; ++g) {
     int layer;
     const Kind k = stage_kind(pd, g, layer);
+    unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     switch (k) {
-      case K_EMBED: embed_stage(pd, a, c); break;
-      case K_SATT: self_attn_stage(pd, a, ring, layer, c, work); break;
+      case K_EMBED: embed_stage(pd, a, cx, c); break;
+      case K_SATT: self_attn_stage(pd, a, ring, cx, layer, c, work); break;
       case K_XATT: cross_attn_stage(pd, a, ring, layer, c, work, fr); break;
       case K_SELECT: select_stage(pd, a, c, work); break;
-      case K_REORD_A: reorder_stage(pd, a, c, true); break;
-      case K_REORD_B: reorder_stage(pd, a, c, false); break;
-      default: gemm_stage(pd, a, ring, k, layer, c, work, os); break;
+      case K_REORD_A: reorder_stage(pd, a, cx, c, true); break;
+      case K_REORD_B: reorder_stage(pd, a, cx, c, false); break;
+      default: gemm_stage<NT>(pd, a, ring, cx, k, layer, c, work, os); break;
     }
     if (k == K_OUT) {
       csync();
       if (a.beam_mode) beam_partials(pd, c, os);
-      else if (a.pred) argmax_finish(pd, a, c, os, flag);
+      else if (a.pred) argmax_finish(pd, a, c, os, flag, work);
     }
+    if (ts && threadIdx.x == 0) ts[1] = globaltimer();
     if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead);
+    if (ts && threadIdx.x == 0) {
+      ts[2] = globaltimer();
+      ts[3] = ring.waited;
+    }
+    ring.waited = 0;
   }
   // the last CTA out resets the barrier counter for the next call
   csync();
@@ -1071,7 +1323,7 @@ __global__ void __launch_bounds__(BLOCK, 1) decoder_kernel(const PlanDev* __rest
 // Weights [N, K] (fp32 or fp16, row-major) -> fragment order of rows [row0, row0 + N) of the destination;
 // optional column scale (LayerNorm gamma). One thread per (row block, k block, lane).
 __global__ void pack_kernel(const void* __restrict__ w, int dtype, int N, int K, const float* __restrict__ gamma,
-                            uint4* __restrict__ out, int row0) {
+                            uint4* __restrict__ out, int row0, int bstride) {
   const long long kbs = K >> 4;
   const long long total = (long long)((N + 15) >> 4) * kbs * 32;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -1101,7 +1353,7 @@ __global__ void pack_kernel(const void* __restrict__ w, int dtype, int N, int K,
       __half2 h = __floats2half2_rn(v0, v1);
       regs[r] = *reinterpret_cast<uint32_t*>(&h);
     }
-    const long long dst = ((long long)((row0 >> 4) + rb) * kbs + kb) * 32 + lane;
+    const long long dst = (long long)((row0 >> 4) + rb) * bstride + kb * 32 + lane;
     out[dst] = make_uint4(regs[0], regs[1], regs[2], regs[3]);
   }
 }
@@ -1129,6 +1381,14 @@ __global__ void to_half_kernel(const void* __restrict__ src, int dtype, long lon
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
     dst[i] = dtype == OWSM_DEC_F32 ? __float2half_rn(reinterpret_cast<const float*>(src)[i])
                                    : reinterpret_cast<const __half*>(src)[i];
+}
+
+// Folded biases [N] -> the 16-float tail of each 16-row block of the packed stream.
+__global__ void place_bias_kernel(const float* __restrict__ b, int N, uint4* __restrict__ out, int bstride, int kbs) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  if (n >= N) return;
+  float* tail = reinterpret_cast<float*>(out + (long long)(n >> 4) * bstride + (long long)kbs * 32);
+  tail[n & 15] = b[n];
 }
 
 }  // namespace owsm
@@ -1183,7 +1443,6 @@ struct OwsmDec {
 struct OwsmDecPlan {
   OwsmDec* h = nullptr;
   PlanDev pd{};
-  PlanDev* pd_dev = nullptr;
   std::vector<void*> allocs;
   size_t smem = 0;
   int64_t scratch_bytes = 0;
@@ -1221,11 +1480,11 @@ int dev_alloc(std::vector<void*>& list, T** out, size_t count, int64_t* total = 
   return OWSM_DEC_OK;
 }
 
-int launch_pack(const void* w, int dtype, int N, int K, const float* gamma, uint4* out, int row0) {
+int launch_pack(const void* w, int dtype, int N, int K, const float* gamma, uint4* out, int row0, int bstride) {
   if (!w) return fail(OWSM_DEC_ERR_ARG, "missing weight pointer");
   long long total = (long long)((N + 15) / 16) * (K / 16) * 32;
   int blocks = (int)std::min<long long>((total + 255) / 256, 65535);
-  pack_kernel<<<blocks, 256>>>(w, dtype, N, K, gamma, out, row0);
+  pack_kernel<<<blocks, 256>>>(w, dtype, N, K, gamma, out, row0, bstride);
   CUDA_TRY(cudaGetLastError());
   return OWSM_DEC_OK;
 }
@@ -1281,6 +1540,18 @@ void assign_blocks(const GemmW* g, int P, std::vector<int> off[NGEMM], std::vect
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+using KernelFn = void (*)(PlanDev, CallArgs);
+
+KernelFn kernel_for(int NT) {
+  switch (NT) {
+    case 1: return decoder_kernel<1>;
+    case 2: return decoder_kernel<2>;
+    case 4: return decoder_kernel<4>;
+    default: return decoder_kernel<8>;
+  }
+}
+
+
 }  // namespace
 
 extern "C" {
@@ -1292,6 +1563,7 @@ int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device
   *out = nullptr;
   const OwsmDecDims d = *dims;
   if (d.L < 1 || d.H < 1 || d.D != d.H * DK) return fail(OWSM_DEC_ERR_LIMIT, "the head size must be 64 (D = 64 * H)");
+  if (d.D % 128 || d.D > 1024) return fail(OWSM_DEC_ERR_LIMIT, "d_model must be a multiple of 128, at most 1024");
   if (d.D % 16 || d.F % 16 || d.F < 16 || d.V < 1 || d.max_pos < 1)
     return fail(OWSM_DEC_ERR_LIMIT, "D and F must be multiples of 16");
   if (w->weight_dtype != OWSM_DEC_F32 && w->weight_dtype != OWSM_DEC_F16)
@@ -1321,7 +1593,8 @@ int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device
     gw.N = spec[gi].N;
     gw.K = spec[gi].K;
     gw.NB = (gw.N + 15) / 16;
-    gw.lstride = (long long)gw.NB * (gw.K / 16) * 32;
+    gw.bstride = (gw.K / 16) * 32 + 4;
+    gw.lstride = (long long)gw.NB * gw.bstride;
     uint4* wp;
     float* bp;
     if ((rc = dev_alloc(h->allocs, &wp, (size_t)gw.lstride * spec[gi].layers))) return bail(rc);
@@ -1337,11 +1610,11 @@ int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device
       const void* ws[3] = {ly.wq, ly.wk, ly.wv};
       const float* bs[3] = {ly.bq, ly.bk, ly.bv};
       for (int i = 0; i < 3; ++i) {
-        if ((rc = launch_pack(ws[i], dt, D, D, ly.ln1_g, wq, i * D))) return bail(rc);
+        if ((rc = launch_pack(ws[i], dt, D, D, ly.ln1_g, wq, i * D, h->g[G_QKV].bstride))) return bail(rc);
         if ((rc = launch_fold(ws[i], dt, D, D, ly.ln1_b, bs[i], bq + i * D))) return bail(rc);
       }
     } else {
-      if ((rc = launch_pack(ly.wq, dt, 3 * D, D, ly.ln1_g, wq, 0))) return bail(rc);
+      if ((rc = launch_pack(ly.wq, dt, 3 * D, D, ly.ln1_g, wq, 0, h->g[G_QKV].bstride))) return bail(rc);
       if ((rc = launch_fold(ly.wq, dt, 3 * D, D, ly.ln1_b, ly.bq, bq))) return bail(rc);
     }
     struct One {
@@ -1359,15 +1632,24 @@ int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device
       GemmW& gw = h->g[o.gi];
       uint4* wp = const_cast<uint4*>(gw.w) + (long long)l * gw.lstride;
       float* bp = const_cast<float*>(gw.b) + (long long)l * gw.N;
-      if ((rc = launch_pack(o.w, dt, gw.N, gw.K, o.g, wp, 0))) return bail(rc);
+      if ((rc = launch_pack(o.w, dt, gw.N, gw.K, o.g, wp, 0, gw.bstride))) return bail(rc);
       if ((rc = launch_fold(o.w, dt, gw.N, gw.K, o.beta, o.b, bp))) return bail(rc);
     }
   }
   {
     GemmW& gw = h->g[G_OUT];
-    if ((rc = launch_pack(w->wout, dt, V, D, w->lnf_g, const_cast<uint4*>(gw.w), 0))) return bail(rc);
+    if ((rc = launch_pack(w->wout, dt, V, D, w->lnf_g, const_cast<uint4*>(gw.w), 0, gw.bstride))) return bail(rc);
     if ((rc = launch_fold(w->wout, dt, V, D, w->lnf_b, w->bout, const_cast<float*>(gw.b)))) return bail(rc);
   }
+  for (int gi = 0; gi < NGEMM; ++gi) {  // biases into the packed streams
+    const GemmW& gw = h->g[gi];
+    for (int l = 0; l < spec[gi].layers; ++l) {
+      place_bias_kernel<<<(gw.N + 255) / 256, 256>>>(gw.b + (long long)l * gw.N, gw.N,
+                                                     const_cast<uint4*>(gw.w) + (long long)l * gw.lstride, gw.bstride,
+                                                     gw.K / 16);
+    }
+  }
+  if (cudaGetLastError() != cudaSuccess) return bail(fail(OWSM_DEC_ERR_CUDA, "bias placement failed"));
   if ((rc = dev_alloc(h->allocs, &h->emb, (size_t)V * D))) return bail(rc);
   to_half_kernel<<<1024, 256>>>(w->emb, dt, (long long)V * D, h->emb);
   if (cudaGetLastError() != cudaSuccess) return bail(fail(OWSM_DEC_ERR_CUDA, "embedding copy failed"));
@@ -1407,7 +1689,7 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   PlanDev& pd = p->pd;
   pd.L = d.L; pd.D = d.D; pd.H = d.H; pd.F = d.F; pd.V = d.V; pd.max_pos = d.max_pos;
   pd.eps = d.eps; pd.xscale = d.xscale;
-  pd.R = R; pd.S = S; pd.M = M; pd.NT = (M + 7) / 8; pd.C = C; pd.T = T; pd.G = G; pd.U = U; pd.beam = beam;
+  pd.R = R; pd.S = S; pd.M = M; pd.NT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; pd.C = C; pd.T = T; pd.G = G; pd.U = U; pd.beam = beam;
   pd.P = h->programs;
   pd.max_spin = h->max_spin;
   pd.emb = h->emb;
@@ -1453,31 +1735,49 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
     if ((rc = dev_alloc(p->allocs, &pd.tmpk, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
     if ((rc = dev_alloc(p->allocs, &pd.tmpv, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
   }
-  // shared memory: barriers | utterance prefix sums + flag | output-stage state | ring | work area
+  // shared memory: barriers | utterance prefix sums + flag | block lists | row offsets | output-stage state |
+  // ring | work area
+  size_t max_blocks = 0;
+  for (int c = 0; c < pd.P; ++c) {
+    size_t n = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) n += off[gi][c + 1] - off[gi][c];
+    max_blocks = std::max(max_blocks, n);
+  }
   size_t off_pre = 256;
-  size_t off_out = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  size_t off_sched = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_blocks) + 127) & ~(size_t)127;
+  size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
   size_t off_ring = (off_out + out_smem(M) + 1023) & ~(size_t)1023;
   size_t gemm_work = (size_t)NT * (D / 16) * 256 + (size_t)NWARP * NT * 32 * 16;
   size_t work = std::max(gemm_work, attn_smem(pd.Qmax));
-  work = std::max(work, sizeof(float) * (3 * KTOP + 2 * NTHR + KTOP));
+  work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);  // argmax partials of all CTAs
+  if (beam) work = std::max(work, select_smem(beam, pd.P));
   cudaDeviceProp prop;
   CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
   const size_t limit = prop.sharedMemPerBlockOptin;
-  if (off_ring + 2 * (size_t)SLOT + work > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
-  int nslot = (int)std::min<size_t>((limit - off_ring - work) / SLOT, 6);
+  // 32 KB slots while at least 4 fit (up to 6), else 16 KB slots (at least 2)
+  size_t slot = SLOT;
+  if (off_ring + work > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
+  if ((limit - off_ring - work) / (slot + 128) < 4) slot = SLOT / 2;
+  if ((limit - off_ring - work) / (slot + 128) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
+  int nslot = (int)std::min<size_t>((limit - off_ring - work) / (slot + 128), slot == SLOT ? 6 : 8);
   pd.nslot = nslot;
+  pd.slot = (int)slot;
+  pd.apos = (int)(slot / (DK * 2));
   pd.off_pre = (int)off_pre;
+  pd.off_sched = (int)off_sched;
+  pd.off_rows = (int)off_rows;
+  pd.inflight = std::min(nslot, (int)(65536 / slot));  // 64 KB of copies in flight per CTA
   pd.off_out = (int)off_out;
   pd.off_ring = (int)off_ring;
-  pd.off_work = (int)(off_ring + (size_t)nslot * SLOT);
+  pd.sstride = (int)slot + 128;
+  pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);
   p->smem = (size_t)pd.off_work + work;
   // the attribute is per function: set it to the device maximum once, so plans of other sizes coexist
-  CUDA_TRY(cudaFuncSetAttribute(decoder_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+  CUDA_TRY(cudaFuncSetAttribute(kernel_for(pd.NT), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
   int per_sm = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decoder_kernel, BLOCK, p->smem));
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for(pd.NT), BLOCK, p->smem));
   if (per_sm < 1) return bail(fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM"));
-  if ((rc = dev_alloc(p->allocs, &p->pd_dev, 1, tot))) return bail(rc);
-  CUDA_TRY(cudaMemcpy(p->pd_dev, &pd, sizeof(PlanDev), cudaMemcpyHostToDevice));
   *out = p;
   return OWSM_DEC_OK;
 }
@@ -1486,10 +1786,7 @@ void owsm_dec_plan_destroy(OwsmDecPlan* p) { delete p; }
 
 static int launch(OwsmDecPlan* p, void* stream, const CallArgs& a) {
   DeviceGuard guard(p->h->device);
-  if (p->pd.max_spin != p->h->max_spin) {
-    p->pd.max_spin = p->h->max_spin;
-    CUDA_TRY(cudaMemcpy(p->pd_dev, &p->pd, sizeof(PlanDev), cudaMemcpyHostToDevice));
-  }
+  p->pd.max_spin = p->h->max_spin;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;
@@ -1500,8 +1797,7 @@ static int launch(OwsmDecPlan* p, void* stream, const CallArgs& a) {
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const PlanDev* pdp = p->pd_dev;
-  CUDA_TRY(cudaLaunchKernelEx(&cfg, decoder_kernel, pdp, a));
+  CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel_for(p->pd.NT), p->pd, a));
   return OWSM_DEC_OK;
 }
 
@@ -1580,6 +1876,18 @@ int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int
   if (ring_slots) *ring_slots = p->pd.nslot;
   if (scratch_bytes) *scratch_bytes = p->scratch_bytes;
   return OWSM_DEC_OK;
+}
+
+int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  DeviceGuard guard(p->h->device);
+  p->pd.ts = reinterpret_cast<unsigned long long*>(stamps);
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  return 8 * p->pd.L + 2 + (beam_call ? 3 : 0);
 }
 
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls) {

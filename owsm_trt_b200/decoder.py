@@ -223,6 +223,8 @@ class B200Decoder:
 
         run.writes_cache = True
         run.writes_pred = pred is not None
+        run.plan = plan
+        run.beam = False
         run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, ntm, enc_len)
         run.programs = self.programs
         run.kernel = self
@@ -252,5 +254,7 @@ class B200Decoder:
             _lib.check(fn(plan, torch.cuda.current_stream(dev).cuda_stream, *args), "owsm_dec_beam_step")
 
         run.writes_cache = True
+        run.plan = plan
+        run.beam = True
         run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent, token)
         return run

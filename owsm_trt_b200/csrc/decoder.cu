@@ -90,6 +90,7 @@ struct PlanDev {
   int off_pre, off_out, off_ring, off_work;  // shared-memory layout (bytes)
   int off_sched, off_rows;  // this CTA's block lists and the rows' cache offsets (shared memory)
   int inflight;             // bulk copies in flight per CTA (ring slots may hold more, finished)
+  int stage_b;              // largest non-LayerNorm B operand staged in shared memory (bytes)
 };
 
 struct CallArgs {
@@ -247,7 +248,7 @@ __device__ void for_chunks(const PlanDev& pd, const CallArgs& a, const Frames& f
   Kind k = stage_kind(pd, g, layer);
   int gi = gemm_of(k);
   if (gi >= 0) {
-    const GemmW& gw = pd.g[gi];
+    const GemmW gw = pd.g[gi];
     int l = (k == K_OUT) ? 0 : layer;
     int kbs = gw.K >> 4;
     int kpc = kbs < (pd.slot / 512) ? kbs : (pd.slot / 512);  // k-blocks per chunk
@@ -314,6 +315,21 @@ struct Ring {
     __syncwarp();
     if ((threadIdx.x & 31) == 0) mbar_arrive(&empty[i % ns]);
     ++i;
+  }
+  // One warp alone consumes chunk `idx` (its arrival counts for all the consumer warps).
+  __device__ uint8_t* wait_at(uint32_t idx) {
+    const int s = idx % ns;
+    unsigned long long t0 = timing ? globaltimer() : 0;
+    if (!dead && !mbar_wait(&full[s], (idx / ns) & 1, spin)) {
+      dead = true;
+      atomicExch(err, E_ERR_TIMEOUT);
+    }
+    if (timing) waited += globaltimer() - t0;
+    return data + (size_t)s * stride;
+  }
+  __device__ void release_at(uint32_t idx) {
+    __syncwarp();
+    if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(&empty[idx % ns], NWARP);
   }
 };
 
@@ -384,260 +400,340 @@ __device__ void ln_to_frag(const PlanDev& pd, __half* bbuf) {
   }
 }
 
-struct OutState {  // per-token running results of the output stage (shared memory)
-  float* amax;
+// Per-token running results of the output stage (shared memory). The CTA-level arrays hold the stage's
+// result; the per-warp arrays the warps' running state while they multiply their own blocks.
+struct OutState {
+  float* amax;  // [M] argmax (greedy)
   int* aidx;
-  float* rmax;
+  float* rmax;  // [M] log-softmax partials and top-K (beam)
   float* rsum;
   float* topv;  // [M][KTOP]
   int* topi;
-  float* tile;  // [16][M] values of the current row block
+  float* wamax;  // [NWARP][M]
+  int* waidx;
+  float* wrmax;  // [NWARP][M] (beam)
+  float* wrsum;
+  float* wtopv;  // [NWARP][M][KTOP]
+  int* wtopi;
+  float* wtile;  // [NWARP][16][M]
 };
 
-// Epilogue of one 16-row block: the CTA's reduced accumulators red[w][nt][lane][4] summed over the warps;
-// thread (nt, lane) owns rows g, g + 8 and tokens 2t, 2t + 1 of n-tile nt.
-__device__ __forceinline__ void gemm_epilogue(const PlanDev& pd, const CallArgs& a, Kind kind, const GemmW& gw,
-                                              const float (&bia)[2], int rb, const float* red, OutState& os,
-                                              const float (&xpre)[4]) {
-  const int NT = pd.NT, M = pd.M;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  if (kind == K_OUT && a.beam_mode) {
-    // values of the block to the tile [16][M], then one thread per token merges them
-    for (int nt = warp; nt < NT; nt += NWARP) {
-      const int ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
-      float v[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int w = 0; w < NWARP; ++w) {
-        const float4 q = lds128f(&red[((w * NT + nt) * 32 + ln2) * 4]);
-        v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
+__device__ __forceinline__ void merge_best(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+// Output stage, beam calls: the 16 values of a block (tile[16][M], this warp's) into the warp's running
+// log-sum-exp and top-K per token; lane m handles token m (and m + 32).
+__device__ __forceinline__ void beam_merge_block(OutState& os, int warp, int lane, int M, int rb) {
+  const float* tile = os.wtile + (size_t)warp * 16 * M;
+  for (int m = lane; m < M; m += 32) {
+    float* rm = os.wrmax + warp * M + m;
+    float* rs = os.wrsum + warp * M + m;
+    float bmx = *rm;
+    for (int row = 0; row < 16; ++row) bmx = fmaxf(bmx, tile[row * M + m]);
+    if (bmx > -INFINITY) {
+      float sm = (*rm > -INFINITY) ? *rs * expf(*rm - bmx) : 0.f;
+      for (int row = 0; row < 16; ++row) {
+        const float y = tile[row * M + m];
+        if (y > -INFINITY) sm += expf(y - bmx);
       }
+      *rm = bmx;
+      *rs = sm;
+    }
+    float* tv = os.wtopv + ((size_t)warp * M + m) * KTOP;
+    int* ti = os.wtopi + ((size_t)warp * M + m) * KTOP;
+    for (int row = 0; row < 16; ++row) {
+      const float y = tile[row * M + m];
+      const int n = rb * 16 + row;
+      if (!(y > tv[KTOP - 1] || (y == tv[KTOP - 1] && n < ti[KTOP - 1]))) continue;
+      int j = KTOP - 1;
+      while (j > 0 && (y > tv[j - 1] || (y == tv[j - 1] && n < ti[j - 1]))) {
+        tv[j] = tv[j - 1];
+        ti[j] = ti[j - 1];
+        --j;
+      }
+      tv[j] = y;
+      ti[j] = n;
+    }
+  }
+}
+
+// Epilogue of one 16-row block from a warp's accumulators: lane (g, t) owns rows g, g + 8 and tokens
+// 2t, 2t + 1 of every n-tile. bia = the block's biases of rows g, g + 8; xres = residual inputs (prefetched).
+template <int NT>
+__device__ __forceinline__ void block_epilogue(const PlanDev& pd, const CallArgs& a, Kind kind, int rb,
+                                               const float (&acc)[NT][4], const float (&bia)[2],
+                                               const float (&xres)[NT][4], float (&best)[NT][2],
+                                               int (&besti)[NT][2], OutState& os, int warp, int lane) {
+  const int M = pd.M, D = pd.D, V = pd.V, N = pd.g[gemm_of(kind)].N;
+  const int g = lane >> 2, t = lane & 3;
+  if (kind == K_OUT && a.beam_mode) {
+    float* tile = os.wtile + (size_t)warp * 16 * M;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
         if (m < M) {
-          const float y = v[e] + bia[e >> 1];
-          if (n < pd.V) a.logits[(long long)m * pd.V + n] = y;
-          os.tile[row * M + m] = (n < pd.V) ? y : -INFINITY;
+          const float y = acc[nt][e] + bia[e >> 1];
+          if (n < V) a.logits[(long long)m * V + n] = y;
+          tile[row * M + m] = (n < V) ? y : -INFINITY;
         }
       }
-    }
-    csync();
-    if (tid < M) {
-      const int m = tid;
-      const float mx = os.rmax[m];
-      float bmx = mx;
-      for (int row = 0; row < 16; ++row) bmx = fmaxf(bmx, os.tile[row * M + m]);
-      if (bmx > -INFINITY) {
-        float sm = (mx > -INFINITY ? os.rsum[m] * expf(mx - bmx) : 0.f);
-        for (int row = 0; row < 16; ++row) {
-          const float y = os.tile[row * M + m];
-          if (y > -INFINITY) sm += expf(y - bmx);
-        }
-        os.rmax[m] = bmx;
-        os.rsum[m] = sm;
-      }
-      float* tv = os.topv + m * KTOP;
-      int* ti = os.topi + m * KTOP;
-      for (int row = 0; row < 16; ++row) {
-        const float y = os.tile[row * M + m];
-        const int n = rb * 16 + row;
-        if (!(y > tv[KTOP - 1])) continue;  // ties keep the earlier (lower) index
-        int j = KTOP - 1;
-        while (j > 0 && y > tv[j - 1]) {
-          tv[j] = tv[j - 1];
-          ti[j] = ti[j - 1];
-          --j;
-        }
-        tv[j] = y;
-        ti[j] = n;
-      }
-    }
+    __syncwarp();
+    beam_merge_block(os, warp, lane, M, rb);
+    __syncwarp();
     return;
   }
-  for (int nt = warp; nt < NT; nt += NWARP) {  // warp-uniform: the argmax below shuffles within the warp
-  const int ln2 = tid & 31, g = ln2 >> 2, t = ln2 & 3;
-  float v[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int w = 0; w < NWARP; ++w) {
-    const float4 q = lds128f(&red[((w * NT + nt) * 32 + ln2) * 4]);
-    v[0] += q.x; v[1] += q.y; v[2] += q.z; v[3] += q.w;
-  }
-  const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
-  float xin[4] = {xpre[0], xpre[1], xpre[2], xpre[3]};  // prefetched at block start for nt == warp
-  if (res && nt != warp) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
-      xin[e] = (m < M && n < gw.N) ? __ldcg(pd.x + (long long)m * pd.D + n) : 0.f;
-    }
-  }
-  float best[2] = {-INFINITY, -INFINITY};
-  int besti[2] = {0x7fffffff, 0x7fffffff};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
-    if (m >= M || n >= gw.N) continue;
-    const float y = v[e] + bia[e >> 1];
-    switch (kind) {
-      case K_QKV: pd.qkv[(long long)m * 3 * pd.D + n] = __float2half_rn(y); break;
-      case K_CQ: pd.q2[(long long)m * pd.D + n] = __float2half_rn(y); break;
-      case K_F1: pd.hB[bfrag_idx(m, n, NT)] = __float2half_rn(fmaxf(y, 0.f)); break;
-      case K_WO: case K_WCO: case K_F2: pd.x[(long long)m * pd.D + n] = xin[e] + y; break;
-      case K_OUT: {
-        a.logits[(long long)m * pd.V + n] = y;
-        float ya = y;
-        if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
-        const int s = e & 1;
-        if (ya > best[s] || (ya == best[s] && n < besti[s])) {
-          best[s] = ya;
-          besti[s] = n;
+      if (m >= M || n >= N) continue;
+      const float y = acc[nt][e] + bia[e >> 1];
+      switch (kind) {
+        case K_QKV: pd.qkv[(long long)m * 3 * D + n] = __float2half_rn(y); break;
+        case K_CQ: pd.q2[(long long)m * D + n] = __float2half_rn(y); break;
+        case K_F1: pd.hB[bfrag_idx(m, n, NT)] = __float2half_rn(fmaxf(y, 0.f)); break;
+        case K_WO: case K_WCO: case K_F2: pd.x[(long long)m * D + n] = xres[nt][e] + y; break;
+        case K_OUT: {
+          a.logits[(long long)m * V + n] = y;
+          float ya = y;
+          if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
+          merge_best(best[nt][e & 1], besti[nt][e & 1], ya, n);
+          break;
         }
-        break;
-      }
-      default: break;
-    }
-  }
-  if (kind == K_OUT) {
-    // reduce over the 8 row groups (lanes with the same t), then merge into the running best
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best[s], o);
-        const int oi = __shfl_xor_sync(0xffffffffu, besti[s], o);
-        if (ov > best[s] || (ov == best[s] && oi < besti[s])) {
-          best[s] = ov;
-          besti[s] = oi;
-        }
-      }
-      const int m = nt * 8 + 2 * t + s;
-      if (g == 0 && m < M) {
-        const float cur = os.amax[m];
-        const int ci = os.aidx[m];
-        if (best[s] > cur || (best[s] == cur && besti[s] < ci)) {
-          os.amax[m] = best[s];
-          os.aidx[m] = besti[s];
-        }
+        default: break;
       }
     }
-  }
-  }
 }
 
-// B fragments (activations from global memory) of batch t of a block: KBB k-blocks x NT n-tiles per lane.
-template <int KBB, int NT>
-struct BFrag {
-  uint2 v[KBB][NT];
-};
-
-template <int KBB, int NT>
-__device__ __forceinline__ BFrag<KBB, NT> load_bfrag(const uint2* __restrict__ gsrc, int t, int bpc, int cpu, int kpc,
-                                                   int kbs, int warp, int lane) {
-  BFrag<KBB, NT> f;
-  const int ch = (t / bpc) % cpu, b = t % bpc;
-  const int kb0 = ch * kpc;
-  const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
-#pragma unroll
-  for (int jj = 0; jj < KBB; ++jj) {
-    const int kb = warp + NWARP * (b * KBB + jj);
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-      f.v[jj][nt] = kb < n ? __ldcg(gsrc + ((long long)(kb0 + kb) * NT + nt) * 32 + lane) : make_uint2(0u, 0u);
-  }
-  return f;
-}
-
-// One GEMM stage on this CTA: its 16-row blocks, each streamed through the ring in chunks of k-blocks.
-// Warp w takes k-blocks w, w + 8, ... of a chunk, in batches of KBB; B fragments come from shared memory
-// (LayerNorm stages: normalised here) or from global memory (the attention outputs / FFN hidden), in which
-// case the next batch's fragments are loaded while the current batch multiplies (across chunk and block
-// boundaries, so a stage sees one L2 round trip, not one per k-block).
+// One GEMM stage on this CTA. Work items are the ring chunks of the CTA's 16-row blocks (a chunk: 16 rows x
+// up to 64 k-blocks); warp w multiplies chunks w, w + 7, ... from start to end (two accumulator chains,
+// pointer-increment addressing), and writes the block's outputs from its registers. Blocks longer than one
+// chunk (FFN2 at K = 4096) leave per-chunk partial sums in shared memory, added up in chunk order after the
+// stage. The B operand (activations) is in shared memory: LayerNorm stages normalise x there; the others
+// copy the attention output / FFN hidden there once per stage when it fits, else read it from L2.
 template <int NT>
 __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, Kind kind, int layer,
                            int c, uint8_t* work, OutState& os) {
-  constexpr int KBB = NT <= 2 ? 4 : 8 / NT;
   const int gi = gemm_of(kind);
-  const GemmW& gw = pd.g[gi];
+  const GemmW gw = pd.g[gi];
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int M = pd.M, D = pd.D;
   const bool ln = (kind == K_QKV || kind == K_CQ || kind == K_F1 || kind == K_OUT);
+  const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
   const int l = (kind == K_OUT) ? 0 : layer;
+  const int kbs = gw.K >> 4;
+  const int kpc = kbs < (pd.slot / 512) ? kbs : (pd.slot / 512);
+  const int cpu = (kbs + kpc - 1) / kpc;  // chunks per block
+  const int nb = nb1 - nb0, nch = nb * cpu;
   __half* bbuf = reinterpret_cast<__half*>(work);
-  float* red = reinterpret_cast<float*>(work + (ln ? (size_t)NT * (pd.D / 16) * 256 : 0));
+  const size_t bbytes = (size_t)NT * kbs * 256;
+  const bool staged = ln || bbytes <= (size_t)pd.stage_b;
+  float* red = reinterpret_cast<float*>(work + (staged ? bbytes : 0));  // [nch][NT][32][4] + [nb][16] biases
+  float* redb = red + (size_t)nch * NT * 128;
   const uint2* gsrc = reinterpret_cast<const uint2*>((kind == K_F2) ? pd.hB : pd.oB);
   if (ln) {
     ln_to_frag(pd, bbuf);
-    csync();
+  } else if (staged) {  // the whole B operand of the stage into shared memory: one L2 round trip
+    const uint4* src = reinterpret_cast<const uint4*>(gsrc);
+    uint4* dst = reinterpret_cast<uint4*>(bbuf);
+    const int n16 = (int)(bbytes / 16);
+#pragma unroll 4
+    for (int i = threadIdx.x; i < n16; i += NTHR) dst[i] = __ldcg(src + i);
   }
-  const int kbs = gw.K >> 4;
-  const int kpc = kbs < (pd.slot / 512) ? kbs : (pd.slot / 512);
-  const int cpu = (kbs + kpc - 1) / kpc;            // chunks per block
-  const int bpc = ((kpc + NWARP - 1) / NWARP + KBB - 1) / KBB;  // batches per chunk
-  const int per_unit = cpu * bpc;
-  const int total = (nb1 - nb0) * per_unit;
-
-  BFrag<KBB, NT> bcur, bnxt;
-  float acc[NT][4];
-  float xpre[4] = {0.f, 0.f, 0.f, 0.f};
-  float bia[2] = {0.f, 0.f};
-  const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
-  const uint4* slot = nullptr;
-  for (int t = 0; t < total; ++t) {
-    const int ch = (t / bpc) % cpu, b = t % bpc;
-    const int kb0 = ch * kpc;
+  if (kind == K_OUT) {  // this warp's running output state
+    for (int m = lane; m < M; m += 32) {
+      os.wamax[warp * M + m] = -INFINITY;
+      os.waidx[warp * M + m] = 0x7fffffff;
+      if (a.beam_mode) {
+        os.wrmax[warp * M + m] = -INFINITY;
+        os.wrsum[warp * M + m] = 0.f;
+        for (int j = 0; j < KTOP; ++j) {
+          os.wtopv[((size_t)warp * M + m) * KTOP + j] = -INFINITY;
+          os.wtopi[((size_t)warp * M + m) * KTOP + j] = 0x7fffffff;
+        }
+      }
+    }
+  }
+  csync();
+  float best[NT][2];
+  int besti[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) best[nt][0] = best[nt][1] = -INFINITY, besti[nt][0] = besti[nt][1] = 0x7fffffff;
+  const uint32_t bsh = smem_u32(bbuf);
+  const int g = lane >> 2, t = lane & 3;
+  // Warp w takes the chunks that land in ring slot w (warps beyond the slot count idle here): each slot is
+  // consumed by one warp in order, so no waiter is ever two phases ahead of a slot's barrier (a parity wait
+  // cannot tell phases two apart).
+  const int ns = ring.ns;
+  const int j0 = warp < ns ? (warp - (int)(ring.i % (uint32_t)ns) + ns) % ns : nch;
+  for (int j = j0; j < nch; j += ns) {
+    const int u = j / cpu, part = j - u * cpu;
+    const int rb = cx.sb[nb0 + u];
+    const int kb0 = part * kpc;
     const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
-    if (ch == 0 && b == 0) {
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
-      if (!ln) bcur = load_bfrag<KBB, NT>(gsrc, t, bpc, cpu, kpc, kbs, warp, lane);  // (within a block only)
-      if (res && warp < NT) {  // this warp's epilogue residuals, loaded with the B fragments
-        const int rb = cx.sb[nb0 + t / per_unit], g = lane >> 2, tt = lane & 3;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = g + (e >> 1) * 8, m = warp * 8 + 2 * tt + (e & 1), n = rb * 16 + row;
-          xpre[e] = (m < pd.M && n < gw.N) ? __ldcg(pd.x + (long long)m * pd.D + n) : 0.f;
-        }
-      }
-    }
-    if (b == 0) {
-      if (kind == K_OUT) event(cx, 1);
-      slot = reinterpret_cast<const uint4*>(ring.wait());
-      if (kind == K_OUT) event(cx, 2);
-    }
-    if (!ln && (t + 1) % per_unit != 0) bnxt = load_bfrag<KBB, NT>(gsrc, t + 1, bpc, cpu, kpc, kbs, warp, lane);
-#pragma unroll
-    for (int jj = 0; jj < KBB; ++jj) {
-      const int kb = warp + NWARP * (b * KBB + jj);
-      if (kb < n) {
-        const uint4 af = lds128(slot + kb * 32 + lane);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          uint2 bf;
-          if (ln) bf = lds64(bbuf + (((kb0 + kb) * NT + nt) * 32 + lane) * 4);
-          else bf = bcur.v[jj][nt];
-          mma16816(acc[nt], af, bf.x, bf.y);
-        }
-      }
-    }
-    if (!ln) bcur = bnxt;
-    if (ch == cpu - 1 && b == bpc - 1 && warp < NT) {  // the block's biases (rows g, g + 8) from the slot tail
-      const float* tail = reinterpret_cast<const float*>(slot + n * 32);
-      bia[0] = tail[lane >> 2];
-      bia[1] = tail[(lane >> 2) + 8];
-    }
-    if (b == bpc - 1) ring.release();
-    if (kind == K_OUT && b == bpc - 1) event(cx, 3);
-    if (ch == cpu - 1 && b == bpc - 1) {  // block done: reduce over warps, epilogue
-      const int rb = cx.sb[nb0 + t / per_unit];
+    const bool last = (part == cpu - 1);
+    float xres[NT][4];
+    if (res && cpu == 1) {  // residual inputs of this block, in flight while the chunk multiplies
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
-        sts128f(&red[((warp * NT + nt) * 32 + lane) * 4], make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
-      csync();
-      if (kind == K_OUT) event(cx, 4);
-      gemm_epilogue(pd, a, kind, gw, bia, rb, red, os, xpre);
-      if (kind == K_OUT) event(cx, 5);
-      csync();
-      if (kind == K_OUT) event(cx, 6);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = nt * 8 + 2 * t + (e & 1), nn = rb * 16 + g + (e >> 1) * 8;
+          xres[nt][e] = (m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f;
+        }
     }
+    const uint8_t* slot = ring.wait_at(ring.i + j);
+    const uint32_t ash = smem_u32(slot) + lane * 16;
+    float acc0[NT][4], acc1[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc0[nt][e] = acc1[nt][e] = 0.f;
+    if (staged) {
+      uint32_t bp = bsh + ((uint32_t)kb0 * NT * 32 + lane) * 8;
+#pragma unroll 2
+      for (int kb = 0; kb < n; kb += 2) {
+        const uint4 a0 = lds128_u32(ash + kb * 512);
+        const uint4 a1 = lds128_u32(ash + (kb + 1) * 512);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint2 b0 = lds64_u32(bp + nt * 256);
+          const uint2 b1 = lds64_u32(bp + (NT + nt) * 256);
+          mma16816(acc0[nt], a0, b0.x, b0.y);
+          mma16816(acc1[nt], a1, b1.x, b1.y);
+        }
+        bp += 2 * NT * 256;
+      }
+    } else {
+      const uint2* bg = gsrc + ((long long)kb0 * NT) * 32 + lane;
+#pragma unroll 2
+      for (int kb = 0; kb < n; kb += 2) {
+        const uint4 a0 = lds128_u32(ash + kb * 512);
+        const uint4 a1 = lds128_u32(ash + (kb + 1) * 512);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const uint2 b0 = __ldcg(bg + nt * 32);
+          const uint2 b1 = __ldcg(bg + (NT + nt) * 32);
+          mma16816(acc0[nt], a0, b0.x, b0.y);
+          mma16816(acc1[nt], a1, b1.x, b1.y);
+        }
+        bg += 2 * NT * 32;
+      }
+    }
+    float bia[2] = {0.f, 0.f};
+    if (last) {  // the block's biases (rows g, g + 8) from the chunk's tail
+      const float* tail = reinterpret_cast<const float*>(slot + (size_t)n * 512);
+      bia[0] = tail[g];
+      bia[1] = tail[g + 8];
+    }
+    ring.release_at(ring.i + j);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc0[nt][e] += acc1[nt][e];
+    if (cpu == 1) {
+      block_epilogue<NT>(pd, a, kind, rb, acc0, bia, xres, best, besti, os, warp, lane);
+    } else {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+        sts128f(&red[(((size_t)j * NT + nt) * 32 + lane) * 4],
+                make_float4(acc0[nt][0], acc0[nt][1], acc0[nt][2], acc0[nt][3]));
+      if (last && t == 0) {
+        redb[u * 16 + g] = bia[0];
+        redb[u * 16 + g + 8] = bia[1];
+      }
+    }
+  }
+  ring.i += nch;
+  if (cpu > 1) {  // blocks of several chunks: their partial sums in chunk order
+    csync();
+    for (int u = warp; u < nb; u += NWARP) {
+      const int rb = cx.sb[nb0 + u];
+      float acc[NT][4], xres[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int m = nt * 8 + 2 * t + (e & 1), nn = rb * 16 + g + (e >> 1) * 8;
+          xres[nt][e] = (res && m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f;
+          acc[nt][e] = 0.f;
+        }
+      for (int part = 0; part < cpu; ++part) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const float4 q = lds128f(&red[((((size_t)u * cpu + part) * NT + nt) * 32 + lane) * 4]);
+          acc[nt][0] += q.x; acc[nt][1] += q.y; acc[nt][2] += q.z; acc[nt][3] += q.w;
+        }
+      }
+      const float bia[2] = {redb[u * 16 + g], redb[u * 16 + g + 8]};
+      block_epilogue<NT>(pd, a, kind, rb, acc, bia, xres, best, besti, os, warp, lane);
+    }
+  }
+  if (kind == K_OUT && !a.beam_mode) {  // the warp's best per token (over its row groups), then over the warps
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int s2 = 0; s2 < 2; ++s2) {
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, best[nt][s2], o);
+          const int oi = __shfl_xor_sync(0xffffffffu, besti[nt][s2], o);
+          merge_best(best[nt][s2], besti[nt][s2], ov, oi);
+        }
+        const int m = nt * 8 + 2 * t + s2;
+        if (g == 0 && m < M) {
+          os.wamax[warp * M + m] = best[nt][s2];
+          os.waidx[warp * M + m] = besti[nt][s2];
+        }
+      }
+  }
+  csync();
+  if (kind == K_OUT) {  // per-CTA results from the warps' states
+    for (int m = threadIdx.x; m < M; m += NTHR) {
+      if (!a.beam_mode) {
+        float bv = os.amax[m];
+        int bi = os.aidx[m];
+        for (int w = 0; w < NWARP; ++w) merge_best(bv, bi, os.wamax[w * M + m], os.waidx[w * M + m]);
+        os.amax[m] = bv;
+        os.aidx[m] = bi;
+      } else {
+        float mx = os.rmax[m];
+        for (int w = 0; w < NWARP; ++w) mx = fmaxf(mx, os.wrmax[w * M + m]);
+        float sm = (os.rmax[m] > -INFINITY) ? os.rsum[m] * expf(os.rmax[m] - mx) : 0.f;
+        for (int w = 0; w < NWARP; ++w) {
+          const float wm = os.wrmax[w * M + m];
+          if (wm > -INFINITY) sm += os.wrsum[w * M + m] * expf(wm - mx);
+        }
+        os.rmax[m] = mx;
+        os.rsum[m] = sm;
+        float* tv = os.topv + m * KTOP;
+        int* ti = os.topi + m * KTOP;
+        for (int w = 0; w < NWARP; ++w)
+          for (int e = 0; e < KTOP; ++e) {
+            const float y = os.wtopv[((size_t)w * M + m) * KTOP + e];
+            const int n = os.wtopi[((size_t)w * M + m) * KTOP + e];
+            if (!(y > tv[KTOP - 1] || (y == tv[KTOP - 1] && n < ti[KTOP - 1]))) continue;
+            int jj = KTOP - 1;
+            while (jj > 0 && (y > tv[jj - 1] || (y == tv[jj - 1] && n < ti[jj - 1]))) {
+              tv[jj] = tv[jj - 1];
+              ti[jj] = ti[jj - 1];
+              --jj;
+            }
+            tv[jj] = y;
+            ti[jj] = n;
+          }
+      }
+    }
+    csync();
   }
 }
 
@@ -1167,7 +1263,7 @@ __device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& c
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
-__device__ OutState carve_out(uint8_t* p, int M) {
+__device__ OutState carve_out(uint8_t* p, int M, bool beam) {
   OutState os;
   float* f = reinterpret_cast<float*>(p);
   os.amax = f; f += M;
@@ -1176,11 +1272,24 @@ __device__ OutState carve_out(uint8_t* p, int M) {
   os.rsum = f; f += M;
   os.topv = f; f += M * KTOP;
   os.topi = reinterpret_cast<int*>(f); f += M * KTOP;
-  os.tile = f;
+  os.wamax = f; f += NWARP * M;
+  os.waidx = reinterpret_cast<int*>(f); f += NWARP * M;
+  os.wrmax = os.wrsum = os.wtopv = os.wtile = nullptr;
+  os.wtopi = nullptr;
+  if (beam) {
+    os.wrmax = f; f += NWARP * M;
+    os.wrsum = f; f += NWARP * M;
+    os.wtopv = f; f += NWARP * M * KTOP;
+    os.wtopi = reinterpret_cast<int*>(f); f += NWARP * M * KTOP;
+    os.wtile = f;
+  }
   return os;
 }
 
-__host__ __device__ constexpr size_t out_smem(int M) { return sizeof(float) * ((size_t)M * (4 + 2 * KTOP) + 16 * M); }
+__host__ __device__ constexpr size_t out_smem(int M, bool beam) {
+  return sizeof(float) * ((size_t)M * (4 + 2 * KTOP) + (size_t)NWARP * M * 2 +
+                          (beam ? (size_t)NWARP * M * (2 + 2 * KTOP + 16) : 0));
+}
 
 // The plan and the call's pointers are __grid_constant__ parameters: read from the constant bank where used,
 // not held in registers across the stage loop.
@@ -1269,7 +1378,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   }
 
   Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
-  OutState os = carve_out(smem + pd.off_out, pd.M);
+  OutState os = carve_out(smem + pd.off_out, pd.M, a.beam_mode != 0);
   for (int m = threadIdx.x; m < pd.M; m += NTHR) {
     os.amax[m] = -INFINITY;
     os.aidx[m] = 0x7fffffff;
@@ -1747,8 +1856,27 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   size_t off_sched = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
   size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_blocks) + 127) & ~(size_t)127;
   size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
-  size_t off_ring = (off_out + out_smem(M) + 1023) & ~(size_t)1023;
-  size_t gemm_work = (size_t)NT * (D / 16) * 256 + (size_t)NWARP * NT * 32 * 16;
+  size_t off_ring = (off_out + out_smem(M, beam > 0) + 1023) & ~(size_t)1023;
+  // GEMM stages: the B operand staged in shared memory (LayerNorm stages always; the others when the copy
+  // fits stage_b) + per-chunk partial sums of blocks longer than one chunk
+  const size_t cand_f = (size_t)NT * std::max(D, F) * 16, cand_d = (size_t)NT * D * 16;
+  pd.stage_b = (int)(cand_f <= 128 * 1024 ? cand_f : (cand_d <= 128 * 1024 ? cand_d : 0));
+  size_t gemm_work = 0;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const GemmW& gw = pd.g[gi];
+    const int kbs = gw.K / 16;
+    const bool lnk = (gi == G_QKV || gi == G_CQ || gi == G_F1 || gi == G_OUT);
+    const size_t bb = (size_t)NT * kbs * 256;
+    size_t need = lnk ? bb : (bb <= (size_t)pd.stage_b ? bb : 0);
+    const int kpc = std::min(kbs, SLOT / 2 / 512);  // chunks are counted with the smaller slot to be safe
+    const int cpu = (kbs + kpc - 1) / kpc;
+    if (kbs > SLOT / 2 / 512 || cpu > 1) {
+      size_t mb = 0;
+      for (int c = 0; c < pd.P; ++c) mb = std::max(mb, (size_t)(off[gi][c + 1] - off[gi][c]));
+      need += mb * cpu * NT * 512 + mb * 64;
+    }
+    gemm_work = std::max(gemm_work, need);
+  }
   size_t work = std::max(gemm_work, attn_smem(pd.Qmax));
   work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);  // argmax partials of all CTAs
   if (beam) work = std::max(work, select_smem(beam, pd.P));

@@ -34,6 +34,7 @@
 namespace owsm {
 
 constexpr int DK = 64;                 // head size (every OWSM model)
+constexpr int XPS = DK + 4;            // floats per query of a cross-attention partial: 64 outputs, max, sum, 2 pad
 constexpr int NWARP = 7;               // consumer warps (+1 producer: 8 warps, 2 per SM sub-partition)
 constexpr int NTHR = NWARP * 32;       // consumer threads
 constexpr int BLOCK = NTHR + 32;       // + producer warp
@@ -73,7 +74,7 @@ struct PlanDev {
   __half* q2;     // [M][D]
   __half* oB;     // attention outputs, B-fragment order [D/16][NT][32][4]
   __half* hB;     // FFN hidden, B-fragment order [F/16][NT][32][4]
-  float* xpart;   // cross-attention partials [U*H][P][Q][66]
+  float* xpart;   // cross-attention partials [U*H][P][Q][XPS]
   uint32_t* xcnt; // [U*H]
   float* amax;    // [P][M]
   int* aidx;      // [P][M]
@@ -91,6 +92,7 @@ struct PlanDev {
   int off_sched, off_rows;  // this CTA's block lists and the rows' cache offsets (shared memory)
   int inflight;             // bulk copies in flight per CTA (ring slots may hold more, finished)
   int stage_b;              // largest non-LayerNorm B operand staged in shared memory (bytes)
+  int work_bytes;           // size of the work area
 };
 
 struct CallArgs {
@@ -512,6 +514,9 @@ __device__ __forceinline__ void block_epilogue(const PlanDev& pd, const CallArgs
     }
 }
 
+__device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __half* bbuf, float* stage, int cap,
+                                      int* offs_s);
+
 // One GEMM stage on this CTA. Work items are the ring chunks of the CTA's 16-row blocks (a chunk: 16 rows x
 // up to 64 k-blocks); warp w multiplies chunks w, w + 7, ... from start to end (two accumulator chains,
 // pointer-increment addressing), and writes the block's outputs from its registers. Blocks longer than one
@@ -519,8 +524,8 @@ __device__ __forceinline__ void block_epilogue(const PlanDev& pd, const CallArgs
 // stage. The B operand (activations) is in shared memory: LayerNorm stages normalise x there; the others
 // copy the attention output / FFN hidden there once per stage when it fits, else read it from L2.
 template <int NT>
-__device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, Kind kind, int layer,
-                           int c, uint8_t* work, OutState& os) {
+__device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, const Frames& fr,
+                           Kind kind, int layer, int c, uint8_t* work, OutState& os) {
   const int gi = gemm_of(kind);
   const GemmW gw = pd.g[gi];
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
@@ -536,12 +541,35 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
   const int nb = nb1 - nb0, nch = nb * cpu;
   __half* bbuf = reinterpret_cast<__half*>(work);
   const size_t bbytes = (size_t)NT * kbs * 256;
-  const bool staged = ln || bbytes <= (size_t)pd.stage_b;
+  const bool staged = ln || kind == K_WO || kind == K_WCO || bbytes <= (size_t)pd.stage_b;
   float* red = reinterpret_cast<float*>(work + (staged ? bbytes : 0));  // [nch][NT][32][4] + [nb][16] biases
   float* redb = red + (size_t)nch * NT * 128;
   const uint2* gsrc = reinterpret_cast<const uint2*>((kind == K_F2) ? pd.hB : pd.oB);
+  const int g = lane >> 2, t = lane & 3;
+  const int ns = ring.ns;
+  const int j0 = warp < ns ? (warp - (int)(ring.i % (uint32_t)ns) + ns) % ns : nch;
+  // residual inputs of this warp's first block, in flight together with the B operand's loads
+  float xfirst[NT][4];
+  if (res) {
+    const int u0 = (cpu == 1) ? j0 : warp;  // multi-chunk blocks: the block this warp finishes first
+    const bool have = (cpu == 1) ? (j0 < nch) : (warp < nb);
+    const int rb0 = have ? cx.sb[nb0 + u0] : 0;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int m = nt * 8 + 2 * t + (e & 1), nn = rb0 * 16 + g + (e >> 1) * 8;
+        xfirst[nt][e] = (have && m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f;
+      }
+  }
   if (ln) {
     ln_to_frag(pd, bbuf);
+  } else if (kind == K_WCO) {  // combine the cross-attention partials into the B operand
+    // staging area: the work area after the B operand, minus a small table of segment offsets
+    int* segoff = reinterpret_cast<int*>(work + pd.work_bytes) - (pd.U * pd.H + 1 + NWARP + 4);
+    float* stage = reinterpret_cast<float*>(work + bbytes);
+    const int cap = (int)((reinterpret_cast<uint8_t*>(segoff) - reinterpret_cast<uint8_t*>(stage)) / 4) - 64;
+    combine_cross_to_frag(pd, fr, bbuf, stage, cap, segoff);
   } else if (staged) {  // the whole B operand of the stage into shared memory: one L2 round trip
     const uint4* src = reinterpret_cast<const uint4*>(gsrc);
     uint4* dst = reinterpret_cast<uint4*>(bbuf);
@@ -549,6 +577,7 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
 #pragma unroll 4
     for (int i = threadIdx.x; i < n16; i += NTHR) dst[i] = __ldcg(src + i);
   }
+  event(cx, 10 + kind);
   if (kind == K_OUT) {  // this warp's running output state
     for (int m = lane; m < M; m += 32) {
       os.wamax[warp * M + m] = -INFINITY;
@@ -564,17 +593,15 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
     }
   }
   csync();
+  event(cx, 30);
   float best[NT][2];
   int besti[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) best[nt][0] = best[nt][1] = -INFINITY, besti[nt][0] = besti[nt][1] = 0x7fffffff;
   const uint32_t bsh = smem_u32(bbuf);
-  const int g = lane >> 2, t = lane & 3;
   // Warp w takes the chunks that land in ring slot w (warps beyond the slot count idle here): each slot is
   // consumed by one warp in order, so no waiter is ever two phases ahead of a slot's barrier (a parity wait
   // cannot tell phases two apart).
-  const int ns = ring.ns;
-  const int j0 = warp < ns ? (warp - (int)(ring.i % (uint32_t)ns) + ns) % ns : nch;
   for (int j = j0; j < nch; j += ns) {
     const int u = j / cpu, part = j - u * cpu;
     const int rb = cx.sb[nb0 + u];
@@ -582,16 +609,17 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
     const int n = kbs - kb0 < kpc ? kbs - kb0 : kpc;
     const bool last = (part == cpu - 1);
     float xres[NT][4];
-    if (res && cpu == 1) {  // residual inputs of this block, in flight while the chunk multiplies
+    if (res && cpu == 1) {  // residual inputs of this block (the first block's were loaded with the B operand)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int m = nt * 8 + 2 * t + (e & 1), nn = rb * 16 + g + (e >> 1) * 8;
-          xres[nt][e] = (m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f;
+          xres[nt][e] = (j == j0) ? xfirst[nt][e] : ((m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f);
         }
     }
     const uint8_t* slot = ring.wait_at(ring.i + j);
+    event(cx, 31);
     const uint32_t ash = smem_u32(slot) + lane * 16;
     float acc0[NT][4], acc1[NT][4];
 #pragma unroll
@@ -636,6 +664,7 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
       bia[1] = tail[g + 8];
     }
     ring.release_at(ring.i + j);
+    event(cx, 32);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -653,6 +682,7 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
       }
     }
   }
+  event(cx, 33);
   ring.i += nch;
   if (cpu > 1) {  // blocks of several chunks: their partial sums in chunk order
     csync();
@@ -664,7 +694,8 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int m = nt * 8 + 2 * t + (e & 1), nn = rb * 16 + g + (e >> 1) * 8;
-          xres[nt][e] = (res && m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f;
+          xres[nt][e] = (u == warp) ? xfirst[nt][e]
+                                    : ((res && m < M && nn < gw.N) ? __ldcg(pd.x + (long long)m * D + nn) : 0.f);
           acc[nt][e] = 0.f;
         }
       for (int part = 0; part < cpu; ++part) {
@@ -739,30 +770,74 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
 
 // ------------------------------------------------------------------------------------------------ attention
 // Online-softmax attention of Q queries (q_s [Q][64], scaled) over chunks of keys/values; each warp keeps
-// partial outputs for positions j = warp (mod 8) in registers: lane owns dims 2*lane, 2*lane + 1.
+// partial outputs for positions j = warp (mod NWARP) in registers: lane owns dims 2*lane, 2*lane + 1.
+// QM = compile-time bound of Q (1: single-query units, the greedy decode step).
+template <int QM>
 struct AttnAcc {
-  float o[MAXQ][2];
+  float o[QM][2];
 };
 
-// scores[q][j] = q . K[j] for j < npos (K rows in shared memory, 128 bytes each).
-__device__ __forceinline__ void attn_scores(const float* qs, const __half* kt, int npos, int Q, float* sc) {
+// scores[q][j] = q . K[j] for j < npos (K rows in shared memory, 128 bytes each), several queries:
+// a thread per (query, position).
+__device__ __forceinline__ void attn_scores_multi(const float* qs, const __half* kt, int npos, int Q, float* sc) {
   for (int idx = threadIdx.x; idx < Q * npos; idx += NTHR) {
-    int q = idx / npos, j = idx - q * npos;
+    const int q = idx / npos, j = idx - q * npos;
     const uint4* kr = reinterpret_cast<const uint4*>(kt + (long long)j * DK);
     const float* qq = qs + q * DK;
     float s = 0.f;
 #pragma unroll
     for (int cc = 0; cc < 8; ++cc) {
-      int ch = (cc + j) & 7;  // rotate the 16-byte chunk per position: fewer bank conflicts
-      uint4 kv = kr[ch];
+      const int ch = (cc + j) & 7;  // rotate the 16-byte chunk per position: fewer bank conflicts
+      const uint4 kv = kr[ch];
       const __half2* h2 = reinterpret_cast<const __half2*>(&kv);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float2 f = __half22float2(h2[e]);
+        const float2 f = __half22float2(h2[e]);
         s += f.x * qq[ch * 8 + 2 * e] + f.y * qq[ch * 8 + 2 * e + 1];
       }
     }
     sc[q * APOS + j] = s;
+  }
+}
+
+// One query: four lanes per position (16 dims each, the query's 16 dims in registers), eight positions per
+// warp per step; each lane's quarter of the row is rotated by its position group so the eight rows of a
+// step fall in different banks.
+struct Q1Regs {
+  float q[16];
+  int part;
+};
+
+__device__ __forceinline__ Q1Regs q1_load(const float* qs) {
+  Q1Regs r;
+  const int lane = threadIdx.x & 31;
+  r.part = ((lane & 3) + (lane >> 2)) & 3;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) r.q[i] = qs[r.part * 16 + i];
+  return r;
+}
+
+__device__ __forceinline__ void attn_scores_q1(const Q1Regs& qr, const __half* kt, int npos, float* sc) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(kt) + qr.part * 32;
+  for (int j0 = warp * 8; j0 < npos; j0 += NWARP * 8) {
+    const int j = j0 + (lane >> 2);
+    float s = 0.f;
+    if (j < npos) {
+      const uint4 k0 = lds128_u32(base + j * 128);
+      const uint4 k1 = lds128_u32(base + j * 128 + 16);
+      const __half2* h0 = reinterpret_cast<const __half2*>(&k0);
+      const __half2* h1 = reinterpret_cast<const __half2*>(&k1);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f0 = __half22float2(h0[e]);
+        const float2 f1 = __half22float2(h1[e]);
+        s += f0.x * qr.q[2 * e] + f0.y * qr.q[2 * e + 1] + f1.x * qr.q[8 + 2 * e] + f1.y * qr.q[9 + 2 * e];
+      }
+    }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((lane & 3) == 0 && j < npos) sc[j] = s;
   }
 }
 
@@ -771,25 +846,25 @@ __device__ __forceinline__ void attn_scores(const float* qs, const __half* kt, i
 template <class Valid>
 __device__ __forceinline__ void attn_softmax(float* sc, int npos, int Q, float* mrun, float* lrun, float* alpha,
                                              Valid valid) {
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int q = warp; q < Q; q += NWARP) {
     float mx = -INFINITY;
     for (int j = lane; j < npos; j += 32)
       if (valid(q, j)) mx = fmaxf(mx, sc[q * APOS + j]);
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float mold = mrun[q];
-    float mnew = fmaxf(mold, mx);
+    const float mold = mrun[q];
+    const float mnew = fmaxf(mold, mx);
     float sum = 0.f;
     for (int j = lane; j < npos; j += 32) {
-      float p = (valid(q, j) && mnew > -INFINITY) ? expf(sc[q * APOS + j] - mnew) : 0.f;
+      const float p = (valid(q, j) && mnew > -INFINITY) ? expf(sc[q * APOS + j] - mnew) : 0.f;
       sc[q * APOS + j] = p;
       sum += p;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (lane == 0) {
-      float al = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
+      const float al = (mold > -INFINITY) ? expf(mold - mnew) : 0.f;
       alpha[q] = al;
       lrun[q] = lrun[q] * al + sum;
       mrun[q] = mnew;
@@ -797,18 +872,25 @@ __device__ __forceinline__ void attn_softmax(float* sc, int npos, int Q, float* 
   }
 }
 
-__device__ __forceinline__ void attn_accum(AttnAcc& acc, const float* sc, const float* alpha, const __half* vt,
+template <int QM>
+__device__ __forceinline__ void attn_accum(AttnAcc<QM>& acc, const float* sc, const float* alpha, const __half* vt,
                                            int npos, int Q) {
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-  for (int q = 0; q < MAXQ; ++q)
-    if (q < Q) { acc.o[q][0] *= alpha[q]; acc.o[q][1] *= alpha[q]; }
+  for (int q = 0; q < QM; ++q)
+    if (q < Q) {
+      acc.o[q][0] *= alpha[q];
+      acc.o[q][1] *= alpha[q];
+    }
+  const uint32_t vb = smem_u32(vt) + lane * 4;
   for (int j = warp; j < npos; j += NWARP) {
-    float2 v = __half22float2(reinterpret_cast<const __half2*>(vt + (long long)j * DK)[lane]);
+    uint32_t raw;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(raw) : "r"(vb + j * 128));
+    const float2 v = __half22float2(*reinterpret_cast<__half2*>(&raw));
 #pragma unroll
-    for (int q = 0; q < MAXQ; ++q)
+    for (int q = 0; q < QM; ++q)
       if (q < Q) {
-        float p = sc[q * APOS + j];
+        const float p = sc[q * APOS + j];
         acc.o[q][0] += p * v.x;
         acc.o[q][1] += p * v.y;
       }
@@ -816,17 +898,18 @@ __device__ __forceinline__ void attn_accum(AttnAcc& acc, const float* sc, const 
 }
 
 // Sum the warps' partial outputs into out[q][64] (shared memory).
-__device__ __forceinline__ void attn_reduce(const AttnAcc& acc, int Q, float* scratch, float* out) {
-  int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+template <int QM>
+__device__ __forceinline__ void attn_reduce(const AttnAcc<QM>& acc, int Q, float* scratch, float* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-  for (int q = 0; q < MAXQ; ++q)
+  for (int q = 0; q < QM; ++q)
     if (q < Q) {
       scratch[(warp * Q + q) * DK + 2 * lane] = acc.o[q][0];
       scratch[(warp * Q + q) * DK + 2 * lane + 1] = acc.o[q][1];
     }
   csync();
   for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
-    int q = idx / DK, d = idx % DK;
+    const int q = idx / DK, d = idx % DK;
     float s = 0.f;
     for (int w = 0; w < NWARP; ++w) s += scratch[(w * Q + q) * DK + d];
     out[q * DK + d] = s;
@@ -835,15 +918,15 @@ __device__ __forceinline__ void attn_reduce(const AttnAcc& acc, int Q, float* sc
 }
 
 struct AttnSmem {
-  float* q;      // [MAXQ][64]
-  float* sc;     // [MAXQ][APOS]
+  float* q;      // [Q][64]
+  float* sc;     // [Q][APOS]
   float* mrun;   // [MAXQ]
   float* lrun;
   float* alpha;
-  float* knew;   // [MAXQ][64] (self-attention: the new keys, fp32)
-  float* vnew;   // [MAXQ][64] (self-attention: the new values, fp32)
-  float* out;    // [MAXQ][64]
-  float* scratch;  // [NWARP][MAXQ][64]
+  float* knew;   // [Q][64] (self-attention: the new keys, fp32)
+  float* vnew;   // [Q][64] (self-attention: the new values, fp32)
+  float* out;    // [Q][64]
+  float* scratch;  // [NWARP][Q][64]
   int* flag;
 };
 
@@ -868,6 +951,14 @@ __host__ __device__ constexpr size_t attn_smem(int Q) {
   return sizeof(float) * ((size_t)Q * DK * 4 + (size_t)Q * APOS + 3 * MAXQ + (size_t)NWARP * Q * DK) + 16;
 }
 
+// Scores of one chunk of keys (K rows in the ring slot) for Q queries.
+template <int QM>
+__device__ __forceinline__ void chunk_scores(const AttnSmem& s, const Q1Regs& qr, const __half* kt, int npos, int Q) {
+  if (QM == 1) attn_scores_q1(qr, kt, npos, s.sc);
+  else attn_scores_multi(s.q, kt, npos, Q, s.sc);
+}
+
+template <int QM>
 __device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, int layer, int c,
                                 uint8_t* work) {
   AttnSmem s = carve_attn(work, pd.Qmax);
@@ -877,71 +968,78 @@ __device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring
     const int b = u / H, h = u % H;
     const int off = cx.offs[b];
     for (int idx = threadIdx.x; idx < S * DK; idx += NTHR) {
-      int q = idx / DK, d = idx % DK;
+      const int q = idx / DK, d = idx % DK;
       const __half* row = pd.qkv + (long long)(b * S + q) * 3 * D + h * DK + d;
       s.q[q * DK + d] = __half2float(__ldcg(row)) * 0.125f;
       s.knew[q * DK + d] = __half2float(__ldcg(row + D));
       s.vnew[q * DK + d] = __half2float(__ldcg(row + 2 * D));
     }
-    if (threadIdx.x < S) { s.mrun[threadIdx.x] = -INFINITY; s.lrun[threadIdx.x] = 0.f; }
-    AttnAcc acc;
+    if (threadIdx.x < S) {
+      s.mrun[threadIdx.x] = -INFINITY;
+      s.lrun[threadIdx.x] = 0.f;
+    }
+    AttnAcc<QM> acc;
 #pragma unroll
-    for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
+    for (int q = 0; q < QM; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
     csync();
+    Q1Regs qr;
+    if (QM == 1) qr = q1_load(s.q);
     for (int j0 = 0; j0 < off; j0 += pd.apos) {
       const int npos = off - j0 < pd.apos ? off - j0 : pd.apos;
       const __half* kt = reinterpret_cast<const __half*>(ring.wait());
-      attn_scores(s.q, kt, npos, S, s.sc);
+      chunk_scores<QM>(s, qr, kt, npos, S);
       ring.release();
       csync();
       attn_softmax(s.sc, npos, S, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
       csync();
       const __half* vt = reinterpret_cast<const __half*>(ring.wait());
-      attn_accum(acc, s.sc, s.alpha, vt, npos, S);
+      attn_accum<QM>(acc, s.sc, s.alpha, vt, npos, S);
       ring.release();
       csync();
     }
-    // the new tokens, causally (keys/values from the QKV projection)
-    for (int idx = threadIdx.x; idx < S * S; idx += NTHR) {
-      int q = idx / S, j = idx % S;
-      float sum = 0.f;
-      for (int d = 0; d < DK; ++d) sum += s.q[q * DK + d] * s.knew[j * DK + d];
-      s.sc[q * APOS + j] = sum;
+    // the new tokens, causally (keys/values from the QKV projection): a warp per (query, key) dot product
+    for (int pr = warp; pr < S * S; pr += NWARP) {
+      const int q = pr / S, j = pr % S;
+      float sum = s.q[q * DK + lane] * s.knew[j * DK + lane] + s.q[q * DK + lane + 32] * s.knew[j * DK + lane + 32];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) s.sc[q * APOS + j] = sum;
     }
     csync();
     attn_softmax(s.sc, S, S, s.mrun, s.lrun, s.alpha, [](int q, int j) { return j <= q; });
     csync();
-    {
 #pragma unroll
-      for (int q = 0; q < MAXQ; ++q)
-        if (q < S) { acc.o[q][0] *= s.alpha[q]; acc.o[q][1] *= s.alpha[q]; }
-      for (int j = warp; j < S; j += NWARP) {
-        const float2 v = make_float2(s.vnew[j * DK + 2 * lane], s.vnew[j * DK + 2 * lane + 1]);
-#pragma unroll
-        for (int q = 0; q < MAXQ; ++q)
-          if (q < S) {
-            float p = s.sc[q * APOS + j];
-            acc.o[q][0] += p * v.x;
-            acc.o[q][1] += p * v.y;
-          }
+    for (int q = 0; q < QM; ++q)
+      if (q < S) {
+        acc.o[q][0] *= s.alpha[q];
+        acc.o[q][1] *= s.alpha[q];
       }
+    for (int j = warp; j < S; j += NWARP) {
+      const float2 v = make_float2(s.vnew[j * DK + 2 * lane], s.vnew[j * DK + 2 * lane + 1]);
+#pragma unroll
+      for (int q = 0; q < QM; ++q)
+        if (q < S) {
+          const float p = s.sc[q * APOS + j];
+          acc.o[q][0] += p * v.x;
+          acc.o[q][1] += p * v.y;
+        }
     }
-    attn_reduce(acc, S, s.scratch, s.out);
+    attn_reduce<QM>(acc, S, s.scratch, s.out);
     // outputs: o (B-fragment order for the out-projection), the cache slots, new_kv
     for (int idx = threadIdx.x; idx < S * (DK / 2); idx += NTHR) {
-      int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
-      float inv = 1.f / s.lrun[q];
-      int m = b * S + q;
+      const int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
+      const float inv = 1.f / s.lrun[q];
+      const int m = b * S + q;
       *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
           __floats2half2_rn(s.out[q * DK + d] * inv, s.out[q * DK + d + 1] * inv);
       // (fp16 -> fp32 -> fp16 is exact: the cache gets the projection's fp16 values)
       const __half2 kn = __floats2half2_rn(s.knew[q * DK + d], s.knew[q * DK + d + 1]);
       const __half2 vn = __floats2half2_rn(s.vnew[q * DK + d], s.vnew[q * DK + d + 1]);
-      long long cslot = ((((long long)layer * pd.R + b) * H + h) * pd.C + off + q) * DK + d;
+      const long long cslot = ((((long long)layer * pd.R + b) * H + h) * pd.C + off + q) * DK + d;
       *reinterpret_cast<__half2*>(a.kc + cslot) = kn;
       *reinterpret_cast<__half2*>(a.vc + cslot) = vn;
-      long long nk = ((((long long)layer * 2 * pd.R + b) * H + h) * S + q) * DK + d;
-      long long nv = nk + (long long)pd.R * H * S * DK;
+      const long long nk = ((((long long)layer * 2 * pd.R + b) * H + h) * S + q) * DK + d;
+      const long long nv = nk + (long long)pd.R * H * S * DK;
       *reinterpret_cast<__half2*>(a.new_kv + nk) = kn;
       *reinterpret_cast<__half2*>(a.new_kv + nv) = vn;
     }
@@ -949,6 +1047,10 @@ __device__ void self_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring
   }
 }
 
+// Cross-attention: every CTA computes its pieces (frames of one (utterance, head) segment) and stores the
+// partial softmax (unnormalised output, running max, running sum) per query in xpart[seg][rank]; the
+// out-projection stage combines a segment's partials in rank order while it stages its B operand.
+template <int QM>
 __device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, int layer, int c, uint8_t* work,
                                  const Frames& fr) {
   AttnSmem s = carve_attn(work, pd.Qmax);
@@ -958,104 +1060,143 @@ __device__ void cross_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& rin
   while (next_piece(fr, f0, f1, p)) {
     const int u = p.u, h = p.h;
     for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
-      int q = idx / DK, d = idx % DK;
-      int m = u * Q + q;  // rows u*G .. u*G+G-1, tokens s: token index (u*G + q/S)*S + q%S = u*Q + q
+      const int q = idx / DK, d = idx % DK;
+      const int m = u * Q + q;  // rows u*G .. u*G+G-1, tokens s: token index (u*G + q/S)*S + q%S = u*Q + q
       s.q[q * DK + d] = __half2float(__ldcg(pd.q2 + (long long)m * D + h * DK + d)) * 0.125f;
     }
-    if (threadIdx.x < Q) { s.mrun[threadIdx.x] = -INFINITY; s.lrun[threadIdx.x] = 0.f; }
-    AttnAcc acc;
+    if (threadIdx.x < Q) {
+      s.mrun[threadIdx.x] = -INFINITY;
+      s.lrun[threadIdx.x] = 0.f;
+    }
+    AttnAcc<QM> acc;
 #pragma unroll
-    for (int q = 0; q < MAXQ; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
+    for (int q = 0; q < QM; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
     csync();
+    Q1Regs qr;
+    if (QM == 1) qr = q1_load(s.q);
     for (int j0 = p.t0; j0 < p.t1; j0 += pd.apos) {
       const int npos = p.t1 - j0 < pd.apos ? p.t1 - j0 : pd.apos;
       const __half* kt = reinterpret_cast<const __half*>(ring.wait());
-      attn_scores(s.q, kt, npos, Q, s.sc);
+      chunk_scores<QM>(s, qr, kt, npos, Q);
       ring.release();
       csync();
       attn_softmax(s.sc, npos, Q, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
       csync();
       const __half* vt = reinterpret_cast<const __half*>(ring.wait());
-      attn_accum(acc, s.sc, s.alpha, vt, npos, Q);
+      attn_accum<QM>(acc, s.sc, s.alpha, vt, npos, Q);
       ring.release();
       csync();
     }
-    attn_reduce(acc, Q, s.scratch, s.out);
-    // partial -> xpart[seg][rank]; the last contributor of the segment combines in rank order
+    attn_reduce<QM>(acc, Q, s.scratch, s.out);
     const int seg = u * H + h;
     const int len = fr.pre[u + 1] - fr.pre[u];
     const long long sbeg = (long long)H * fr.pre[u] + (long long)h * len;
-    const int first = fr.owner(sbeg), last = fr.owner(sbeg + len - 1);
-    const int ncontrib = last - first + 1, rank = c - first;
-    float* part = pd.xpart + (((long long)seg * pd.P + rank) * Q) * (DK + 2);
-    for (int idx = threadIdx.x; idx < Q * (DK + 2); idx += NTHR) {
-      int q = idx / (DK + 2), d = idx % (DK + 2);
-      float v = d < DK ? s.out[q * DK + d] : (d == DK ? s.mrun[q] : s.lrun[q]);
+    const int rank = c - fr.owner(sbeg);
+    float* part = pd.xpart + (((long long)seg * pd.P + rank) * Q) * XPS;
+    for (int idx = threadIdx.x; idx < Q * XPS; idx += NTHR) {
+      const int q = idx / XPS, d = idx % XPS;
+      const float v = d < DK ? s.out[q * DK + d] : (d == DK ? s.mrun[q] : (d == DK + 1 ? s.lrun[q] : 0.f));
       __stcg(part + idx, v);
-    }
-    __threadfence();
-    csync();
-    if (threadIdx.x == 0) {
-      uint32_t old = atom_acq_rel_add(&pd.xcnt[seg], 1);
-      *s.flag = (old == (uint32_t)(ncontrib - 1));
-    }
-    csync();
-    if (*s.flag) {
-      // combine the contributors' partials in rank order, RT at a time staged in shared memory
-      const float* base = pd.xpart + ((long long)seg * pd.P * Q) * (DK + 2);
-      const int RT = (NWARP * DK) / (DK + 2);  // contributors per tile (scratch holds NWARP * Q * 64 floats)
-      float* mx = s.mrun;
-      float* den = s.lrun;
-      if (threadIdx.x < Q) { mx[threadIdx.x] = -INFINITY; den[threadIdx.x] = 0.f; }
-      for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) s.out[idx] = 0.f;
-      csync();
-      for (int r0 = 0; r0 < ncontrib; r0 += RT) {
-        const int nr = ncontrib - r0 < RT ? ncontrib - r0 : RT;
-        const float* src = base + (long long)r0 * Q * (DK + 2);
-        const int nval = nr * Q * (DK + 2);
-#pragma unroll 4
-        for (int idx = threadIdx.x; idx < nval; idx += NTHR) s.scratch[idx] = __ldcg(src + idx);
-        csync();
-        // thread (q, d): new running max from the tile, rescale, accumulate
-        for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
-          const int q = idx / DK, d = idx % DK;
-          float m1 = mx[q];
-          for (int r = 0; r < nr; ++r) m1 = fmaxf(m1, s.scratch[(r * Q + q) * (DK + 2) + DK]);
-          const float al = mx[q] > -INFINITY ? expf(mx[q] - m1) : 0.f;
-          float num = s.out[idx] * al;
-          for (int r = 0; r < nr; ++r) {
-            const float* pr = s.scratch + (r * Q + q) * (DK + 2);
-            const float mr = pr[DK];
-            if (mr > -INFINITY) num += expf(mr - m1) * pr[d];
-          }
-          s.out[idx] = num;
-        }
-        csync();
-        if (threadIdx.x < Q) {
-          const int q = threadIdx.x;
-          float m1 = mx[q];
-          for (int r = 0; r < nr; ++r) m1 = fmaxf(m1, s.scratch[(r * Q + q) * (DK + 2) + DK]);
-          float dd = mx[q] > -INFINITY ? den[q] * expf(mx[q] - m1) : 0.f;
-          for (int r = 0; r < nr; ++r) {
-            const float* pr = s.scratch + (r * Q + q) * (DK + 2);
-            if (pr[DK] > -INFINITY) dd += expf(pr[DK] - m1) * pr[DK + 1];
-          }
-          mx[q] = m1;
-          den[q] = dd;
-        }
-        csync();
-      }
-      for (int idx = threadIdx.x; idx < Q * (DK / 2); idx += NTHR) {
-        const int q = idx / (DK / 2), d = (idx % (DK / 2)) * 2;
-        const float inv = 1.f / den[q];
-        const int m = u * Q + q;
-        *reinterpret_cast<__half2*>(&pd.oB[bfrag_idx(m, h * DK + d, pd.NT)]) =
-            __floats2half2_rn(s.out[q * DK + d] * inv, s.out[q * DK + d + 1] * inv);
-      }
-      if (threadIdx.x == 0) atomicExch(&pd.xcnt[seg], 0u);
     }
     csync();
   }
+}
+
+// Exclusive prefix sum of v[0 .. n) in shared memory (n <= NTHR * 8), all consumer threads.
+__device__ void block_exclusive_scan(int* v, int n, int* warp_tot) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int per = (n + NTHR - 1) / NTHR;
+  const int lo = tid * per, hi = min(n, lo + per);
+  int local = 0;
+  for (int i = lo; i < hi; ++i) local += v[i];
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  csync();
+  int base = 0;
+  for (int w = 0; w < warp; ++w) base += warp_tot[w];
+  int run = base + incl - local;
+  for (int i = lo; i < hi; ++i) {
+    const int x = v[i];
+    v[i] = run;
+    run += x;
+  }
+  csync();
+}
+
+// The out-projection's B operand from the cross-attention partials. Segment (utterance, head) s has nc(s)
+// contributors, whose partials lie contiguously at xpart[s][0 .. nc) (Q x XPS floats each). The segments are
+// staged into shared memory a round at a time (as many whole segments as fit, every thread issuing its
+// loads back to back: one L2 round trip per round), then for every (segment, query, pair of dims) the
+// contributors are combined in rank order (online max / rescale), normalised, and written in B-fragment
+// order (padding tokens zero). A segment larger than the staging area is read from L2 directly.
+__device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __half* bbuf, float* stage, int cap,
+                                      int* offs_s) {
+  const int H = pd.H, Q = pd.G * pd.S, NT = pd.NT, M = pd.M;
+  const int nseg = pd.U * H, row = Q * XPS;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* wtot = offs_s + nseg + 1;
+  for (int sg = threadIdx.x; sg < nseg; sg += NTHR) {
+    const int u = sg / H, h = sg % H;
+    const int len = fr.pre[u + 1] - fr.pre[u];
+    const long long sbeg = (long long)H * fr.pre[u] + (long long)h * len;
+    offs_s[sg] = (fr.owner(sbeg + len - 1) - fr.owner(sbeg) + 1) * row;  // floats of the segment
+  }
+  if (threadIdx.x == 0) offs_s[nseg] = 0;
+  csync();
+  block_exclusive_scan(offs_s, nseg + 1, wtot);  // offs_s[s] = dense offset, offs_s[nseg] = total
+  int s0 = 0;
+  while (s0 < nseg) {
+    // the round: segments s0 .. s1 - 1 whose dense data fits `cap` floats (at least one segment)
+    int lo = s0 + 1, hi = nseg;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (offs_s[mid] - offs_s[s0] <= cap) lo = mid; else hi = mid - 1;
+    }
+    const int s1 = lo;
+    const bool direct = offs_s[s0 + 1] - offs_s[s0] > cap;  // one oversize segment: straight from L2
+    if (!direct) {
+      // a warp per segment, 16-byte asynchronous copies (all in flight at once, one wait)
+      for (int sg = s0 + warp; sg < s1; sg += NWARP) {
+        const float* src = pd.xpart + (long long)sg * pd.P * row;
+        float* dst = stage + (offs_s[sg] - offs_s[s0]);
+        const int n4 = (offs_s[sg + 1] - offs_s[sg]) >> 2;
+        for (int i = lane; i < n4; i += 32) cp_async16(dst + 4 * i, src + 4 * i);
+      }
+      cp_async_wait_all();
+      csync();
+    }
+    const int items = (s1 - s0) * Q * (DK / 2);
+    for (int it = threadIdx.x; it < items; it += NTHR) {
+      const int dp = it % (DK / 2), q = (it / (DK / 2)) % Q, sg = s0 + it / ((DK / 2) * Q);
+      const int nc = (offs_s[sg + 1] - offs_s[sg]) / row;
+      const float* base = direct ? pd.xpart + (long long)sg * pd.P * row : stage + (offs_s[sg] - offs_s[s0]);
+      float mx = -INFINITY, den = 0.f, n0 = 0.f, n1 = 0.f;
+      for (int r = 0; r < nc; ++r) {
+        const float* pr = base + r * row + q * XPS;
+        const float mr = pr[DK], lr = pr[DK + 1];
+        if (mr > -INFINITY) {
+          const float m1 = fmaxf(mx, mr);
+          const float sc = mx > -INFINITY ? expf(mx - m1) : 0.f, w = expf(mr - m1);
+          den = den * sc + w * lr;
+          n0 = n0 * sc + w * pr[2 * dp];
+          n1 = n1 * sc + w * pr[2 * dp + 1];
+          mx = m1;
+        }
+      }
+      const int u = sg / H, h = sg % H;
+      const int m = u * Q + q;
+      *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, h * DK + 2 * dp, NT)]) = __floats2half2_rn(n0 / den, n1 / den);
+    }
+    csync();
+    s0 = s1;
+  }
+  for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens
+    for (int k = lane * 2; k < pd.D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
 }
 
 // ------------------------------------------------------------------------------------------------ other stages
@@ -1398,12 +1539,18 @@ __global__ void __launch_bounds__(BLOCK, 1)
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     switch (k) {
       case K_EMBED: embed_stage(pd, a, cx, c); break;
-      case K_SATT: self_attn_stage(pd, a, ring, cx, layer, c, work); break;
-      case K_XATT: cross_attn_stage(pd, a, ring, layer, c, work, fr); break;
+      case K_SATT:
+        if (pd.S == 1) self_attn_stage<1>(pd, a, ring, cx, layer, c, work);
+        else self_attn_stage<MAXQ>(pd, a, ring, cx, layer, c, work);
+        break;
+      case K_XATT:
+        if (pd.G * pd.S == 1) cross_attn_stage<1>(pd, a, ring, layer, c, work, fr);
+        else cross_attn_stage<MAXQ>(pd, a, ring, layer, c, work, fr);
+        break;
       case K_SELECT: select_stage(pd, a, c, work); break;
       case K_REORD_A: reorder_stage(pd, a, cx, c, true); break;
       case K_REORD_B: reorder_stage(pd, a, cx, c, false); break;
-      default: gemm_stage<NT>(pd, a, ring, cx, k, layer, c, work, os); break;
+      default: gemm_stage<NT>(pd, a, ring, cx, fr, k, layer, c, work, os); break;
     }
     if (k == K_OUT) {
       csync();
@@ -1831,7 +1978,7 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.oB, (size_t)NT * 8 * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.hB, (size_t)NT * 8 * F, tot))) return bail(rc);
-  if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * (DK + 2), tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * XPS, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
@@ -1878,6 +2025,9 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
     gemm_work = std::max(gemm_work, need);
   }
   size_t work = std::max(gemm_work, attn_smem(pd.Qmax));
+  // the cross-out stage: its B operand + room to stage cross-attention partials + the segment table
+  // (at least 16 KB of staging; bigger rounds use whatever the other stages already need)
+  work = std::max(work, (size_t)NT * D * 16 + 16384 + 4 * (size_t)(U * d.H + 16) + 256);
   work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);  // argmax partials of all CTAs
   if (beam) work = std::max(work, select_smem(beam, pd.P));
   cudaDeviceProp prop;
@@ -1900,6 +2050,7 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   pd.off_ring = (int)off_ring;
   pd.sstride = (int)slot + 128;
   pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);
+  pd.work_bytes = (int)work;
   p->smem = (size_t)pd.off_work + work;
   // the attribute is per function: set it to the device maximum once, so plans of other sizes coexist
   CUDA_TRY(cudaFuncSetAttribute(kernel_for(pd.NT), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));

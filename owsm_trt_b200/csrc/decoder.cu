@@ -2008,36 +2008,49 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   // fits stage_b) + per-chunk partial sums of blocks longer than one chunk
   const size_t cand_f = (size_t)NT * std::max(D, F) * 16, cand_d = (size_t)NT * D * 16;
   pd.stage_b = (int)(cand_f <= 128 * 1024 ? cand_f : (cand_d <= 128 * 1024 ? cand_d : 0));
-  size_t gemm_work = 0;
-  for (int gi = 0; gi < NGEMM; ++gi) {
-    const GemmW& gw = pd.g[gi];
-    const int kbs = gw.K / 16;
-    const bool lnk = (gi == G_QKV || gi == G_CQ || gi == G_F1 || gi == G_OUT);
-    const size_t bb = (size_t)NT * kbs * 256;
-    size_t need = lnk ? bb : (bb <= (size_t)pd.stage_b ? bb : 0);
-    const int kpc = std::min(kbs, SLOT / 2 / 512);  // chunks are counted with the smaller slot to be safe
-    const int cpu = (kbs + kpc - 1) / kpc;
-    if (kbs > SLOT / 2 / 512 || cpu > 1) {
-      size_t mb = 0;
-      for (int c = 0; c < pd.P; ++c) mb = std::max(mb, (size_t)(off[gi][c + 1] - off[gi][c]));
-      need += mb * cpu * NT * 512 + mb * 64;
+  // the work area for a given ring slot size (chunks of slot / 512 k-blocks)
+  auto work_for = [&](size_t slot_bytes) {
+    size_t gemm_work = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) {
+      const GemmW& gw = pd.g[gi];
+      const int kbs = gw.K / 16;
+      const bool lnk = (gi == G_QKV || gi == G_CQ || gi == G_F1 || gi == G_OUT);
+      const size_t bb = (size_t)NT * kbs * 256;
+      size_t need = lnk ? bb : (bb <= (size_t)pd.stage_b ? bb : 0);
+      const int kpc = std::min(kbs, (int)(slot_bytes / 512));
+      const int cpu = (kbs + kpc - 1) / kpc;
+      if (cpu > 1) {
+        size_t mb = 0;
+        for (int c = 0; c < pd.P; ++c) mb = std::max(mb, (size_t)(off[gi][c + 1] - off[gi][c]));
+        need += mb * cpu * NT * 512 + mb * 64;
+      }
+      gemm_work = std::max(gemm_work, need);
     }
-    gemm_work = std::max(gemm_work, need);
-  }
-  size_t work = std::max(gemm_work, attn_smem(pd.Qmax));
-  // the cross-out stage: its B operand + room to stage cross-attention partials + the segment table
-  // (at least 16 KB of staging; bigger rounds use whatever the other stages already need)
-  work = std::max(work, (size_t)NT * D * 16 + 16384 + 4 * (size_t)(U * d.H + 16) + 256);
-  work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);  // argmax partials of all CTAs
-  if (beam) work = std::max(work, select_smem(beam, pd.P));
+    size_t w = std::max(gemm_work, attn_smem(pd.Qmax));
+    // the cross-out stage: its B operand + the segment table (+ staging for the partials, below)
+    w = std::max(w, (size_t)NT * D * 16 + 4 * (size_t)(U * d.H + 16) + 256);
+    w = std::max(w, sizeof(float) * 2 * (size_t)pd.P * M);  // argmax partials of all CTAs
+    if (beam) w = std::max(w, select_smem(beam, pd.P));
+    return w;
+  };
   cudaDeviceProp prop;
   CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
   const size_t limit = prop.sharedMemPerBlockOptin;
-  // 32 KB slots while at least 4 fit (up to 6), else 16 KB slots (at least 2)
-  size_t slot = SLOT;
-  if (off_ring + work > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
-  if ((limit - off_ring - work) / (slot + 128) < 4) slot = SLOT / 2;
-  if ((limit - off_ring - work) / (slot + 128) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
+  auto slots_left = [&](size_t w, size_t sl) { return off_ring + w > limit ? (size_t)0 : (limit - off_ring - w) / (sl + 128); };
+  // 32 KB slots while at least 4 fit (up to 6); else 16 KB slots while 4 fit; else the larger of the two
+  // that leaves at least 2 slots
+  size_t slot = SLOT, work = work_for(SLOT);
+  if (slots_left(work, SLOT) < 4) {
+    const size_t w16 = work_for(SLOT / 2);
+    if (slots_left(w16, SLOT / 2) >= 4 || slots_left(work, SLOT) < 2) slot = SLOT / 2, work = w16;
+  }
+  if (slots_left(work, slot) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
+  // staging for the cross-attention partials of the cross-out stage: 16 KB more when that leaves the ring as
+  // it is (segments that do not fit are read from L2)
+  {
+    const size_t wco = (size_t)NT * D * 16 + 4 * (size_t)(U * d.H + 16) + 256 + 16384;
+    if (slots_left(std::max(work, wco), slot) >= std::min<size_t>(slots_left(work, slot), 4)) work = std::max(work, wco);
+  }
   int nslot = (int)std::min<size_t>((limit - off_ring - work) / (slot + 128), slot == SLOT ? 6 : 8);
   pd.nslot = nslot;
   pd.slot = (int)slot;

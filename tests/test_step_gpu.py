@@ -292,6 +292,21 @@ def test_cuda_graph_replay(kern):
     assert torch.equal(logits, eager)
 
 
+_MEDIUM = []
+
+
+def _medium():
+    """The 1B-shaped test model (plain weights, seed 0) and its kernel, built once per session."""
+    _gpu()
+    from owsm_trt_b200.decoder import B200Decoder
+    from owsm_trt_b200.synthetic import MEDIUM_1B
+
+    if not _MEDIUM:
+        sd = decoder_state_dict(MEDIUM_1B, 0, False)
+        _MEDIUM.append((sd, B200Decoder.from_state_dict(sd, MEDIUM_1B.H, DEV)))
+    return _MEDIUM[0]
+
+
 @pytest.mark.slow
 def test_medium_step_matches_reference_golden():
     """The 18-layer d=1024 decoder (plain weights, b1, T=750) against owsm-trt's own fp32 step:
@@ -301,11 +316,10 @@ def test_medium_step_matches_reference_golden():
     from owsm_trt_b200.synthetic import MEDIUM_1B, cross_kv
 
     d = MEDIUM_1B
-    sd = decoder_state_dict(d, 0, False)
+    sd, k = _medium()
     tokens, offset, kc, vc, enc = cases.medium_inputs(d)
     kv = cross_kv(sd, d, enc).half()
     gold = np.load(f"{GOLD}/medium_step.npz")
-    k = B200Decoder.from_state_dict(sd, d.H, DEV)
     logits, new_kv, kc2, vc2, pred = _run_step(k, d, tokens, offset, kc.to(DEV), vc.to(DEV), kv[:, 0].contiguous(),
                                                 kv[:, 1].contiguous())  # fmt: skip
     lg = logits[0, 0].cpu()
@@ -314,3 +328,30 @@ def test_medium_step_matches_reference_golden():
     assert err < 3e-2, err
     assert int(pred[0, 0]) == int(idx[0]) or float(gold["top_val"][0] - gold["top_val"][1]) < 1e-3
     assert abs(float(lg.double().sum()) - float(gold["sum"])) < 3e-2 * d.V ** 0.5
+
+
+@pytest.mark.slow
+@pytest.mark.parametrize("R,S", [(16, 4), (64, 1), (1, 16), (15, 1)])
+def test_medium_row_counts_plan_and_run(R, S):
+    """Every row count the benchmarks use on the 1B-shaped model (prefill of 16 x 4, 64 rows, a 16-token
+    window, 15 beam rows) gets a plan within shared memory and runs: finite logits, argmax bit-exact
+    against them, the cache written at each row's offset."""
+    from owsm_trt_b200.synthetic import MEDIUM_1B
+
+    d = MEDIUM_1B
+    _, k = _medium()
+    g = torch.Generator().manual_seed(R * 100 + S)
+    gd = torch.Generator(device=DEV).manual_seed(R * 100 + S)
+    C, T = 64, 192
+    tokens = torch.randint(0, d.V, (R, S), generator=g)
+    offset = torch.randint(0, C - S, (R,), generator=g)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=gd, device=DEV) * 0.5).half()
+
+    kc, vc = rnd(d.L, R, d.H, C, d.dk), rnd(d.L, R, d.H, C, d.dk)
+    ck, cv = rnd(d.L, R, d.H, T, d.dk), rnd(d.L, R, d.H, T, d.dk)
+    logits, new_kv, kc2, vc2, pred = _run_step(k, d, tokens, offset, kc, vc, ck, cv)
+    assert bool(torch.isfinite(logits).all())
+    assert torch.equal(pred.cpu(), ref.argmax_first(logits.cpu()))
+    _check_cache(kc, vc, kc2, vc2, new_kv, offset)

@@ -21,6 +21,7 @@ import argparse
 import json
 import math
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -59,6 +60,16 @@ def peaks() -> tuple[float, str]:
         except Exception:  # noqa: BLE001
             pass
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(batch: int) -> int | None:
+    """DRAM bytes (read + write) of one decoder launch of this workload, from the committed ncu summary of
+    the same command (profiles/decoder_kernel_b16_full.md); None for other batch sizes or if absent."""
+    p = Path(__file__).resolve().parent / "profiles" / "decoder_kernel_b16_full.md"
+    if batch != BATCH or not p.exists():
+        return None
+    m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", p.read_text(), re.M)
+    return int(m.group(1)) if m else None
 
 
 def step_bytes(d, batch: int, pos: int, enc_lens: list[int], rows_per_utt: int = 1) -> int:
@@ -282,7 +293,7 @@ def run_ours(args, world, rank, local) -> dict | None:
                 "d2h_bytes_per_step": B * 8, "steps": K2},  # fmt: skip
         "gpu_launches": K,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                     "frac": round(achieved / hbm, 4), "traffic": None, "peak_source": hbm_src,
+                     "frac": round(achieved / hbm, 4), "traffic": profiled_traffic(B), "peak_source": hbm_src,
                      "algorithmic_bytes_per_step": int(avg_bytes)},  # fmt: skip
         "clocks": clk.summary(),
         "us_per_step": round(per_step_ms * 1e3, 2),

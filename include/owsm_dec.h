@@ -134,6 +134,22 @@ int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call);
 /* Testing hook: the in-kernel wait limit (polls) of later calls on this handle; 0 restores the default. */
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
 
+/* owsm_dec_step without a plan and without any device allocation (no counterpart in owsm-trt, whose
+ * launchers allocate their scratch in step_fn). For callers that may not allocate device memory when they
+ * decode: a thread that must not block on cudaMalloc (it can synchronise the device), or a host whose device
+ * memory belongs to an outside pool. Greedy calls only (rows_per_utt = 1, no beam), at most 8 tokens
+ * (R x S) per call and 8 MiB of scratch; a larger shape fails with OWSM_DEC_ERR_LIMIT and a message naming
+ * the bytes it needs. The scratch is one fixed array of the library per device: the first call for a
+ * handle and shape on a device looks it up (cudaGetSymbolAddress, with the handle's device current),
+ * zeroes it and uploads the block tables, synchronously -- make that first call before any stream capture.
+ * Every call then zeroes the inter-CTA counters on `stream` and launches. Calls that overlap on one device
+ * (other streams, other threads, other handles) share the array and race: run one at a time per device.
+ * Arguments as owsm_dec_step, plus the call shape R, S, C (cache slots), T (encoder frames). */
+int owsm_dec_step_static(OwsmDec* h, void* stream, int R, int S, int C, int T, const int64_t* tokens,
+                         int64_t tok_stride, const int64_t* offset, int64_t off_stride, void* self_k, void* self_v,
+                         const void* cross_k, const void* cross_v, const int32_t* enc_len, float* logits,
+                         void* new_kv, int64_t* pred, const uint8_t* notime, int first_time, int last_time);
+
 /* Last CUDA / argument error message of this thread ("" if none). */
 const char* owsm_dec_last_error(void);
 

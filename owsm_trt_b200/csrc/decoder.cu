@@ -24,7 +24,9 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1676,7 +1678,10 @@ struct DevBuf {
 
 }  // namespace
 
+static std::atomic<uint64_t> g_handle_serial{0};
+
 struct OwsmDec {
+  uint64_t serial = ++g_handle_serial;  // tells handles apart even when one is freed and its address reused
   int device = 0;
   int programs = 0;
   int sms = 0;
@@ -2185,6 +2190,230 @@ int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls) {
   if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
   h->max_spin = polls ? polls : DEFAULT_SPIN;
+  return OWSM_DEC_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------------------------------------ fixed scratch
+// owsm_dec_step_static: the greedy call of owsm_dec_step for callers that must not allocate device memory
+// when they decide to decode -- an audio or serving thread that may not block on cudaMalloc (it can
+// synchronise the device and stall every stream of the process), or code whose device memory is owned by an
+// outside pool that forbids allocations of its own. Its per-call scratch (residual stream, activations,
+// cross-attention partials, argmax partials, barrier counters, block tables) lives in one array of this
+// library per device, sized at compile time; nothing is allocated, not at set-up and not per call.
+namespace {
+
+constexpr size_t STATIC_SCRATCH_BYTES = (size_t)8 << 20;  // 8 MiB per device
+constexpr int STATIC_MAX_TOKENS = 8;                       // rows x window per fixed-scratch call
+constexpr int STATIC_MAX_DEVICES = 64;
+
+// What one device's fixed scratch is laid out for: the handle and call shape of the last set-up.
+struct StaticLayout {
+  uint64_t serial = 0;  // handle serial (0: never set up)
+  int R = 0, S = 0, C = 0, T = 0;
+  uint8_t* base = nullptr;  // device address of owsm_static_scratch on this device
+  PlanDev pd{};
+  size_t smem = 0;
+};
+StaticLayout g_static[STATIC_MAX_DEVICES];
+std::mutex g_static_mu;
+
+}  // namespace
+
+static __device__ __align__(256) uint8_t owsm_static_scratch[STATIC_SCRATCH_BYTES];
+
+// The launch description of a greedy call of shape (R rows, S tokens, C cache slots, T frames, one row per
+// utterance) with its scratch carved from `base`, as owsm_dec_plan builds it from allocations. Returns the
+// bytes the carve needs in `need`; writes nothing to the device when `base` is null (a dry run) and uploads
+// the block tables otherwise.
+static int static_layout(OwsmDec* h, int R, int S, int C, int T, uint8_t* base, PlanDev& pd, size_t& smem,
+                         size_t& need) {
+  const OwsmDecDims& d = h->dims;
+  const int M = R * S, U = R, Q = S;
+  pd = PlanDev{};
+  pd.L = d.L; pd.D = d.D; pd.H = d.H; pd.F = d.F; pd.V = d.V; pd.max_pos = d.max_pos;
+  pd.eps = d.eps; pd.xscale = d.xscale;
+  pd.R = R; pd.S = S; pd.M = M; pd.NT = M <= 8 ? 1 : 2; pd.C = C; pd.T = T; pd.G = 1; pd.U = U; pd.beam = 0;
+  pd.P = h->programs;
+  pd.max_spin = h->max_spin;
+  pd.emb = h->emb;
+  pd.pe = h->pe;
+  for (int gi = 0; gi < NGEMM; ++gi) pd.g[gi] = h->g[gi];
+  pd.err = h->err;
+  pd.Qmax = S;
+  const int NT = pd.NT, P = pd.P, D = d.D, F = d.F;
+  std::vector<int> off[NGEMM], blk[NGEMM];  // host-side schedule (host memory only)
+  assign_blocks(pd.g, P, off, blk);
+  size_t at = 0;
+  auto take = [&](size_t bytes) {
+    at = (at + 255) & ~(size_t)255;
+    uint8_t* q = base ? base + at : nullptr;
+    at += bytes ? bytes : 16;
+    return q;
+  };
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    pd.goff[gi] = reinterpret_cast<const int*>(take(off[gi].size() * 4));
+    pd.gblk[gi] = reinterpret_cast<const int*>(take(std::max<size_t>(blk[gi].size(), 1) * 4));
+  }
+  pd.x = reinterpret_cast<float*>(take((size_t)M * D * 4));
+  pd.qkv = reinterpret_cast<__half*>(take((size_t)M * 3 * D * 2));
+  pd.q2 = reinterpret_cast<__half*>(take((size_t)M * D * 2));
+  pd.oB = reinterpret_cast<__half*>(take((size_t)NT * 8 * D * 2));
+  pd.hB = reinterpret_cast<__half*>(take((size_t)NT * 8 * F * 2));
+  pd.xpart = reinterpret_cast<float*>(take((size_t)U * d.H * P * Q * XPS * 4));
+  pd.xcnt = reinterpret_cast<uint32_t*>(take((size_t)U * d.H * 4));
+  pd.amax = reinterpret_cast<float*>(take((size_t)P * M * 4));
+  pd.aidx = reinterpret_cast<int*>(take((size_t)P * M * 4));
+  pd.ctr = reinterpret_cast<uint32_t*>(take(8 * 4));
+  need = at;
+  if (need > STATIC_SCRATCH_BYTES) return OWSM_DEC_OK;  // the caller rejects the shape
+  // shared memory, as owsm_dec_plan lays it out for a greedy call
+  size_t max_blocks = 0;
+  for (int c = 0; c < P; ++c) {
+    size_t n = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) n += off[gi][c + 1] - off[gi][c];
+    max_blocks = std::max(max_blocks, n);
+  }
+  const size_t off_pre = 256;
+  const size_t off_sched = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  const size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_blocks) + 127) & ~(size_t)127;
+  const size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
+  const size_t off_ring = (off_out + out_smem(M, false) + 1023) & ~(size_t)1023;
+  const size_t cand_f = (size_t)NT * std::max(D, F) * 16, cand_d = (size_t)NT * D * 16;
+  pd.stage_b = (int)(cand_f <= 128 * 1024 ? cand_f : (cand_d <= 128 * 1024 ? cand_d : 0));
+  auto work_for = [&](size_t slot_bytes) {
+    size_t gemm_work = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) {
+      const GemmW& gw = pd.g[gi];
+      const int kbs = gw.K / 16;
+      const bool lnk = (gi == G_QKV || gi == G_CQ || gi == G_F1 || gi == G_OUT);
+      const size_t bb = (size_t)NT * kbs * 256;
+      size_t nd = lnk ? bb : (bb <= (size_t)pd.stage_b ? bb : 0);
+      const int kpc = std::min(kbs, (int)(slot_bytes / 512));
+      const int cpu = (kbs + kpc - 1) / kpc;
+      if (cpu > 1) {
+        size_t mb = 0;
+        for (int c = 0; c < P; ++c) mb = std::max(mb, (size_t)(off[gi][c + 1] - off[gi][c]));
+        nd += mb * cpu * NT * 512 + mb * 64;
+      }
+      gemm_work = std::max(gemm_work, nd);
+    }
+    size_t w = std::max(gemm_work, attn_smem(pd.Qmax));
+    w = std::max(w, (size_t)NT * D * 16 + 4 * (size_t)(U * d.H + 16) + 256);
+    w = std::max(w, sizeof(float) * 2 * (size_t)P * M);
+    return w;
+  };
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
+  const size_t limit = prop.sharedMemPerBlockOptin;
+  auto slots_left = [&](size_t w, size_t sl) { return off_ring + w > limit ? (size_t)0 : (limit - off_ring - w) / (sl + 128); };
+  size_t slot = SLOT, work = work_for(SLOT);
+  if (slots_left(work, SLOT) < 4) {
+    const size_t w16 = work_for(SLOT / 2);
+    if (slots_left(w16, SLOT / 2) >= 4 || slots_left(work, SLOT) < 2) slot = SLOT / 2, work = w16;
+  }
+  if (slots_left(work, slot) < 2) return fail(OWSM_DEC_ERR_LIMIT, "shared memory too small");
+  {
+    const size_t wco = (size_t)NT * D * 16 + 4 * (size_t)(U * d.H + 16) + 256 + 16384;
+    if (slots_left(std::max(work, wco), slot) >= std::min<size_t>(slots_left(work, slot), 4)) work = std::max(work, wco);
+  }
+  const int nslot = (int)std::min<size_t>((limit - off_ring - work) / (slot + 128), slot == SLOT ? 6 : 8);
+  pd.nslot = nslot;
+  pd.slot = (int)slot;
+  pd.apos = (int)(slot / (DK * 2));
+  pd.off_pre = (int)off_pre;
+  pd.off_sched = (int)off_sched;
+  pd.off_rows = (int)off_rows;
+  pd.inflight = std::min(nslot, (int)(65536 / slot));
+  pd.off_out = (int)off_out;
+  pd.off_ring = (int)off_ring;
+  pd.sstride = (int)slot + 128;
+  pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);
+  pd.work_bytes = (int)work;
+  smem = (size_t)pd.off_work + work;
+  if (!base) return OWSM_DEC_OK;
+  // set-up writes: the whole carved area to zero (the state owsm_dec_plan's fresh allocations start in),
+  // then the block tables
+  CUDA_TRY(cudaMemset(base, 0, need));
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    CUDA_TRY(cudaMemcpy(const_cast<int*>(pd.goff[gi]), off[gi].data(), off[gi].size() * 4, cudaMemcpyHostToDevice));
+    if (!blk[gi].empty())
+      CUDA_TRY(cudaMemcpy(const_cast<int*>(pd.gblk[gi]), blk[gi].data(), blk[gi].size() * 4, cudaMemcpyHostToDevice));
+  }
+  CUDA_TRY(cudaFuncSetAttribute(kernel_for(pd.NT), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for(pd.NT), BLOCK, smem));
+  if (per_sm < 1) return fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM");
+  return OWSM_DEC_OK;
+}
+
+extern "C" {
+
+int owsm_dec_step_static(OwsmDec* h, void* stream, int R, int S, int C, int T, const int64_t* tokens,
+                         int64_t tok_stride, const int64_t* offset, int64_t off_stride, void* self_k, void* self_v,
+                         const void* cross_k, const void* cross_v, const int32_t* enc_len, float* logits,
+                         void* new_kv, int64_t* pred, const uint8_t* notime, int first_time, int last_time) {
+  if (!h || !tokens || !offset || !self_k || !self_v || !cross_k || !cross_v || !logits || !new_kv)
+    return fail(OWSM_DEC_ERR_ARG, "null argument");
+  if (!aligned16(self_k) || !aligned16(self_v) || !aligned16(cross_k) || !aligned16(cross_v))
+    return fail(OWSM_DEC_ERR_ARG, "K/V buffers must be 16-byte aligned");
+  if (R < 1 || S < 1 || C < S || T < 1) return fail(OWSM_DEC_ERR_ARG, "bad call shape");
+  if (R * S > STATIC_MAX_TOKENS)
+    return fail(OWSM_DEC_ERR_LIMIT, "owsm_dec_step_static takes at most " + std::to_string(STATIC_MAX_TOKENS) +
+                                        " tokens (rows x window) per call; use owsm_dec_plan + owsm_dec_step");
+  if (h->device < 0 || h->device >= STATIC_MAX_DEVICES) return fail(OWSM_DEC_ERR_LIMIT, "device index too large");
+  DeviceGuard guard(h->device);  // the handle's device is current for the symbol lookup and the launch
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  StaticLayout& sl = g_static[h->device];
+  if (sl.serial != h->serial || sl.R != R || sl.S != S || sl.C != C || sl.T != T) {
+    // first call for this handle and shape on the device: find the array, check the shape fits, lay it out
+    PlanDev pd{};
+    size_t smem = 0, need = 0;
+    int rc = static_layout(h, R, S, C, T, nullptr, pd, smem, need);
+    if (rc) return rc;
+    if (need > STATIC_SCRATCH_BYTES)
+      return fail(OWSM_DEC_ERR_LIMIT, "this call needs " + std::to_string(need) + " bytes of scratch; the fixed area holds " +
+                                          std::to_string(STATIC_SCRATCH_BYTES) + " (use owsm_dec_plan + owsm_dec_step)");
+    if (!sl.base) {
+      void* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, owsm_static_scratch);
+      if (e != cudaSuccess) return fail(OWSM_DEC_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+      sl.base = reinterpret_cast<uint8_t*>(ptr);
+    }
+    sl.serial = 0;
+    CUDA_TRY(cudaDeviceSynchronize());  // no earlier fixed-scratch call may still read the old layout
+    rc = static_layout(h, R, S, C, T, sl.base, pd, smem, need);
+    if (rc) return rc;
+    sl.pd = pd;
+    sl.smem = smem;
+    sl.R = R; sl.S = S; sl.C = C; sl.T = T;
+    sl.serial = h->serial;
+  }
+  PlanDev pd = sl.pd;
+  pd.max_spin = h->max_spin;
+  // the inter-CTA counters start every call at zero (a call that gave up may have left them set)
+  CUDA_TRY(cudaMemsetAsync(pd.ctr, 0, 8 * sizeof(uint32_t), reinterpret_cast<cudaStream_t>(stream)));
+  CallArgs a{};
+  a.tok = tokens; a.tok_stride = tok_stride;
+  a.off = offset; a.off_stride = off_stride;
+  a.kc = reinterpret_cast<__half*>(self_k); a.vc = reinterpret_cast<__half*>(self_v);
+  a.ck = reinterpret_cast<const __half*>(cross_k); a.cv = reinterpret_cast<const __half*>(cross_v);
+  a.enc_len = enc_len;
+  a.logits = logits; a.new_kv = reinterpret_cast<__half*>(new_kv);
+  a.pred = pred; a.notime = notime; a.ft = first_time; a.lt = last_time;
+  a.beam_mode = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.gridDim = dim3(pd.P);
+  cfg.blockDim = dim3(BLOCK);
+  cfg.dynamicSmemBytes = sl.smem;
+  cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel_for(pd.NT), pd, a));
   return OWSM_DEC_OK;
 }
 

@@ -154,9 +154,12 @@ def setup_dist():
     if world > 1:
         import datetime
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))  # fmt: skip
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))  # fmt: skip
+        else:  # host-only runs of the rank logic (tests)
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
     return world, rank, local
 
 
@@ -456,12 +459,17 @@ def run_reference(args, world, rank) -> dict | None:
 
 def main():
     args = parse()
+    if args.impl == "reference":
+        # the reference arm is one CPU run on rank 0; the other ranks exit 0 without work (no process group,
+        # so nobody waits on a collective while rank 0 computes)
+        world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+        res = run_reference(args, world, rank)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
     world, rank, local = setup_dist()
     try:
-        if args.impl == "reference":
-            res = run_reference(args, world, rank)
-        else:
-            res = run_ours(args, world, rank, local)
+        res = run_ours(args, world, rank, local)
         if res is not None:
             print(json.dumps(res), flush=True)
     finally:

@@ -145,6 +145,7 @@ struct Ctx {
   const int* offs;
   unsigned long long* ev;  // profiling: event stamps of this CTA (thread 0), NULL = off
   int* nev;                // shared-memory event counter
+  float* red;              // [2 * NWARP] shared-memory partial sums of a LayerNorm team
 };
 
 constexpr int NEV = 128;  // events per CTA in the profiling log
@@ -152,8 +153,8 @@ __device__ __forceinline__ void event(const Ctx& cx, int tag) {
   if (cx.ev && threadIdx.x == 0 && *cx.nev < NEV - 1) {
     long long clk;
     asm volatile("mov.u64 %0, %%clock64;" : "=l"(clk));
-    cx.ev[*cx.nev] = (globaltimer() << 8) | (unsigned)tag;
-    cx.ev[*cx.nev + 1] = (unsigned long long)clk;
+    cx.ev[*cx.nev] = globaltimer();
+    cx.ev[*cx.nev + 1] = ((unsigned long long)clk << 8) | (unsigned)tag;
     *cx.nev += 2;
   }
 }
@@ -177,13 +178,11 @@ struct Frames {
   int U, H, P;
   const int* pre;  // [U + 1] prefix sums of utterance lengths (shared memory)
   __device__ long long bound(int c) const { return c >= P ? total : (long long)c * total / P; }
-  __device__ int owner(long long f) const {  // the CTA whose range holds frame f
-    int lo = 0, hi = P - 1;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (bound(mid) <= f) lo = mid; else hi = mid - 1;
-    }
-    return lo;
+  // The CTA whose range holds frame f: the largest c with floor(c * total / P) <= f, i.e. c * total <
+  // (f + 1) * P, i.e. c = ceil((f + 1) * P / total) - 1 (one division, no search).
+  __device__ int owner(long long f) const {
+    const long long c = ((f + 1) * P + total - 1) / total - 1;
+    return (int)(c < P - 1 ? c : P - 1);
   }
   __device__ int utt_of(long long f) const {  // utterance of flat frame f
     int lo = 0, hi = U - 1;
@@ -364,43 +363,97 @@ struct Work {  // shared-memory work area, carved per stage
 // LayerNorm of the residual stream x [M][D] (eps) into B-fragment order (fp16) in shared memory. One warp
 // per token; a lane holds its D / 32 values in registers (all loads issued at once: one L2 round trip).
 constexpr int MAXV4 = 8;  // D <= 1024: float4 loads per lane
-__device__ void ln_to_frag(const PlanDev& pd, __half* bbuf) {
-  const int D = pd.D, M = pd.M, NT = pd.NT, nv4 = D / 128;
+// LayerNorm of the M rows of x into the B operand (fragment order, shared memory), padding tokens zero.
+// From 7 rows on, a warp normalises whole rows; below that a row is split over a team of 7 / M warps whose
+// partial sums meet in shared memory, so one row costs one round trip for its loads and a few hundred
+// cycles rather than a single warp's serial pass over 1024 values.
+__device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
+  const int D = pd.D, M = pd.M, NT = pd.NT, nv = D / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
     for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
-  for (int m = warp; m < M; m += NWARP) {
+  const int ts = M >= NWARP ? 1 : NWARP / M;  // warps per row
+  auto emit = [&](int m, int i, const float4& v, float mean, float rstd) {
+    const int k = i * 4;
+    *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) =
+        __floats2half2_rn((v.x - mean) * rstd, (v.y - mean) * rstd);
+    *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k + 2, NT)]) =
+        __floats2half2_rn((v.z - mean) * rstd, (v.w - mean) * rstd);
+  };
+  if (ts == 1) {
+    for (int m = warp; m < M; m += NWARP) {
+      const float4* xr = reinterpret_cast<const float4*>(pd.x + (long long)m * D);
+      float4 v[MAXV4];
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i * 32 + lane < nv) v[i] = __ldcg(xr + i * 32 + lane);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i * 32 + lane < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+      event(cx, 20);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s / D;
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i * 32 + lane < nv) {
+          const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+          q += (a * a + b * b) + (c * c + d * d);
+        }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = rsqrtf(q / D + pd.eps);
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i * 32 + lane < nv) emit(m, i * 32 + lane, v[i], mean, rstd);
+    }
+    return;
+  }
+  // teams: row m = warp / ts (warps past M * ts only join the barriers); member j takes float4s
+  // j * 32 + lane + k * ts * 32
+  const int m = warp / ts, j = warp % ts, step = ts * 32;
+  const bool on = m < M;
+  float4 v[MAXV4];
+  float s = 0.f;
+  if (on) {
     const float4* xr = reinterpret_cast<const float4*>(pd.x + (long long)m * D);
-    float4 v[MAXV4];
 #pragma unroll
-    for (int i = 0; i < MAXV4; ++i)
-      if (i < nv4) v[i] = __ldcg(xr + i * 32 + lane);
-    float s = 0.f;
+    for (int k = 0; k < MAXV4; ++k)
+      if (j * 32 + lane + k * step < nv) v[k] = __ldcg(xr + j * 32 + lane + k * step);
 #pragma unroll
-    for (int i = 0; i < MAXV4; ++i)
-      if (i < nv4) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    for (int k = 0; k < MAXV4; ++k)
+      if (j * 32 + lane + k * step < nv) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+    event(cx, 20);
 #pragma unroll
     for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mean = s / D;
-    float q = 0.f;
+    if (lane == 0) cx.red[warp] = s;
+  }
+  csync();
+  float mean = 0.f, q = 0.f;
+  if (on) {
+    float tot = 0.f;
+    for (int w = m * ts; w < m * ts + ts; ++w) tot += cx.red[w];
+    mean = tot / D;
 #pragma unroll
-    for (int i = 0; i < MAXV4; ++i)
-      if (i < nv4) {
-        const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    for (int k = 0; k < MAXV4; ++k)
+      if (j * 32 + lane + k * step < nv) {
+        const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
         q += (a * a + b * b) + (c * c + d * d);
       }
 #pragma unroll
     for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    const float rstd = rsqrtf(q / D + pd.eps);
+    if (lane == 0) cx.red[NWARP + warp] = q;
+  }
+  csync();
+  if (on) {
+    float tq = 0.f;
+    for (int w = m * ts; w < m * ts + ts; ++w) tq += cx.red[NWARP + w];
+    const float rstd = rsqrtf(tq / D + pd.eps);
 #pragma unroll
-    for (int i = 0; i < MAXV4; ++i)
-      if (i < nv4) {
-        const int k = (i * 32 + lane) * 4;
-        *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) =
-            __floats2half2_rn((v[i].x - mean) * rstd, (v[i].y - mean) * rstd);
-        *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k + 2, NT)]) =
-            __floats2half2_rn((v[i].z - mean) * rstd, (v[i].w - mean) * rstd);
-      }
+    for (int k = 0; k < MAXV4; ++k)
+      if (j * 32 + lane + k * step < nv) emit(m, j * 32 + lane + k * step, v[k], mean, rstd);
   }
 }
 
@@ -517,7 +570,7 @@ __device__ __forceinline__ void block_epilogue(const PlanDev& pd, const CallArgs
 }
 
 __device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __half* bbuf, float* stage, int cap,
-                                      int* offs_s);
+                                      int* offs_s, const Ctx& cx);
 
 // One GEMM stage on this CTA. Work items are the ring chunks of the CTA's 16-row blocks (a chunk: 16 rows x
 // up to 64 k-blocks); warp w multiplies chunks w, w + 7, ... from start to end (two accumulator chains,
@@ -533,6 +586,7 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  event(cx, 9);
   const int M = pd.M, D = pd.D;
   const bool ln = (kind == K_QKV || kind == K_CQ || kind == K_F1 || kind == K_OUT);
   const bool res = (kind == K_WO || kind == K_WCO || kind == K_F2);
@@ -565,13 +619,13 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
       }
   }
   if (ln) {
-    ln_to_frag(pd, bbuf);
+    ln_to_frag(pd, bbuf, cx);
   } else if (kind == K_WCO) {  // combine the cross-attention partials into the B operand
     // staging area: the work area after the B operand, minus a small table of segment offsets
     int* segoff = reinterpret_cast<int*>(work + pd.work_bytes) - (pd.U * pd.H + 1 + NWARP + 4);
     float* stage = reinterpret_cast<float*>(work + bbytes);
     const int cap = (int)((reinterpret_cast<uint8_t*>(segoff) - reinterpret_cast<uint8_t*>(stage)) / 4) - 64;
-    combine_cross_to_frag(pd, fr, bbuf, stage, cap, segoff);
+    combine_cross_to_frag(pd, fr, bbuf, stage, cap, segoff, cx);
   } else if (staged) {  // the whole B operand of the stage into shared memory: one L2 round trip
     const uint4* src = reinterpret_cast<const uint4*>(gsrc);
     uint4* dst = reinterpret_cast<uint4*>(bbuf);
@@ -1137,7 +1191,7 @@ __device__ void block_exclusive_scan(int* v, int n, int* warp_tot) {
 // contributors are combined in rank order (online max / rescale), normalised, and written in B-fragment
 // order (padding tokens zero). A segment larger than the staging area is read from L2 directly.
 __device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __half* bbuf, float* stage, int cap,
-                                      int* offs_s) {
+                                      int* offs_s, const Ctx& cx) {
   const int H = pd.H, Q = pd.G * pd.S, NT = pd.NT, M = pd.M;
   const int nseg = pd.U * H, row = Q * XPS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1151,6 +1205,7 @@ __device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __hal
   if (threadIdx.x == 0) offs_s[nseg] = 0;
   csync();
   block_exclusive_scan(offs_s, nseg + 1, wtot);  // offs_s[s] = dense offset, offs_s[nseg] = total
+  event(cx, 40);
   int s0 = 0;
   while (s0 < nseg) {
     // the round: segments s0 .. s1 - 1 whose dense data fits `cap` floats (at least one segment)
@@ -1171,30 +1226,69 @@ __device__ void combine_cross_to_frag(const PlanDev& pd, const Frames& fr, __hal
       }
       cp_async_wait_all();
       csync();
+      event(cx, 41);
     }
+    if (!direct) {
+      // pass 1, a thread per (segment, query): the contributors' weights exp(m_r - max) / sum_r' exp(m_r' - max)
+      // l_r' written over their max slots
+      for (int it = threadIdx.x; it < (s1 - s0) * Q; it += NTHR) {
+        const int sg = s0 + it / Q, q = it % Q;
+        const int nc = (offs_s[sg + 1] - offs_s[sg]) / row;
+        float* base = stage + (offs_s[sg] - offs_s[s0]) + q * XPS;
+        float mx = -INFINITY;
+        for (int r = 0; r < nc; ++r) mx = fmaxf(mx, base[r * row + DK]);
+        float den = 0.f;
+        for (int r = 0; r < nc; ++r) {
+          const float mr = base[r * row + DK];
+          den += mr > -INFINITY ? expf(mr - mx) * base[r * row + DK + 1] : 0.f;
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        for (int r = 0; r < nc; ++r) {
+          const float mr = base[r * row + DK];
+          base[r * row + DK] = mr > -INFINITY ? expf(mr - mx) * inv : 0.f;
+        }
+      }
+      csync();
+    }
+    // pass 2, a thread per (segment, query, pair of dims): the weighted sum in rank order
     const int items = (s1 - s0) * Q * (DK / 2);
     for (int it = threadIdx.x; it < items; it += NTHR) {
       const int dp = it % (DK / 2), q = (it / (DK / 2)) % Q, sg = s0 + it / ((DK / 2) * Q);
       const int nc = (offs_s[sg + 1] - offs_s[sg]) / row;
-      const float* base = direct ? pd.xpart + (long long)sg * pd.P * row : stage + (offs_s[sg] - offs_s[s0]);
-      float mx = -INFINITY, den = 0.f, n0 = 0.f, n1 = 0.f;
-      for (int r = 0; r < nc; ++r) {
-        const float* pr = base + r * row + q * XPS;
-        const float mr = pr[DK], lr = pr[DK + 1];
-        if (mr > -INFINITY) {
-          const float m1 = fmaxf(mx, mr);
-          const float sc = mx > -INFINITY ? expf(mx - m1) : 0.f, w = expf(mr - m1);
-          den = den * sc + w * lr;
-          n0 = n0 * sc + w * pr[2 * dp];
-          n1 = n1 * sc + w * pr[2 * dp + 1];
-          mx = m1;
+      float n0 = 0.f, n1 = 0.f;
+      if (!direct) {
+        const float* pr = stage + (offs_s[sg] - offs_s[s0]) + q * XPS;
+        for (int r = 0; r < nc; ++r, pr += row) {
+          const float w = pr[DK];
+          const float2 v = *reinterpret_cast<const float2*>(pr + 2 * dp);
+          n0 += w * v.x;
+          n1 += w * v.y;
         }
+      } else {  // straight from L2: the online form over the contributors
+        const float* base = pd.xpart + (long long)sg * pd.P * row;
+        float mx = -INFINITY, den = 0.f;
+        for (int r = 0; r < nc; ++r) {
+          const float* pr = base + r * row + q * XPS;
+          const float mr = __ldcg(pr + DK), lr = __ldcg(pr + DK + 1);
+          if (mr > -INFINITY) {
+            const float m1 = fmaxf(mx, mr);
+            const float sc = mx > -INFINITY ? expf(mx - m1) : 0.f, w = expf(mr - m1);
+            den = den * sc + w * lr;
+            n0 = n0 * sc + w * __ldcg(pr + 2 * dp);
+            n1 = n1 * sc + w * __ldcg(pr + 2 * dp + 1);
+            mx = m1;
+          }
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        n0 *= inv;
+        n1 *= inv;
       }
       const int u = sg / H, h = sg % H;
       const int m = u * Q + q;
-      *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, h * DK + 2 * dp, NT)]) = __floats2half2_rn(n0 / den, n1 / den);
+      *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, h * DK + 2 * dp, NT)]) = __floats2half2_rn(n0, n1);
     }
     csync();
+    event(cx, 42);
     s0 = s1;
   }
   for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens
@@ -1474,7 +1568,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
   int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
   if (threadIdx.x == 0) *nev = 0;
-  const Ctx cx{so, sb, offs, evlog, nev};
+  const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
   Frames fr;
   fr.total = (long long)pd.H * pre[pd.U];
   fr.U = pd.U;
@@ -2005,7 +2099,7 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
     max_blocks = std::max(max_blocks, n);
   }
   size_t off_pre = 256;
-  size_t off_sched = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  size_t off_sched = (off_pre + 4 * 1072 + 127) & ~(size_t)127;
   size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_blocks) + 127) & ~(size_t)127;
   size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
   size_t off_ring = (off_out + out_smem(M, beam > 0) + 1023) & ~(size_t)1023;
@@ -2276,7 +2370,7 @@ static int static_layout(OwsmDec* h, int R, int S, int C, int T, uint8_t* base, 
     max_blocks = std::max(max_blocks, n);
   }
   const size_t off_pre = 256;
-  const size_t off_sched = (off_pre + 4 * 1040 + 127) & ~(size_t)127;
+  const size_t off_sched = (off_pre + 4 * 1072 + 127) & ~(size_t)127;
   const size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_blocks) + 127) & ~(size_t)127;
   const size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
   const size_t off_ring = (off_out + out_smem(M, false) + 1023) & ~(size_t)1023;

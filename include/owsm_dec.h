@@ -131,6 +131,16 @@ int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int
 int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps);
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call);
 
+/* Which kernel later plans of this handle use (no counterpart in owsm-trt, which picks its kernel by GPU):
+ * 0 (default) the cluster kernel where the call shape allows it (greedy, at most 16 tokens), else the
+ * grid-stage kernel; 1 always the grid-stage kernel; 2 the cluster kernel, owsm_dec_plan failing with
+ * OWSM_DEC_ERR_LIMIT where it does not apply. Existing plans keep their kernel. */
+int owsm_dec_set_path(OwsmDec* h, int path);
+
+/* The kernel a plan runs: 1 the grid-stage kernel (eight grid-wide stages per layer), 2 the cluster
+ * kernel (three per layer). */
+int owsm_dec_plan_kernel(const OwsmDecPlan* p);
+
 /* Testing hook: the in-kernel wait limit (polls) of later calls on this handle; 0 restores the default. */
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
 

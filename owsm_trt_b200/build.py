@@ -12,7 +12,7 @@ PKG = Path(__file__).resolve().parent
 ROOT = PKG.parent
 LIB = PKG / "libowsmdec.so"
 SOURCES = [PKG / "csrc" / "decoder.cu"]
-HEADERS = [PKG / "csrc" / "ptx.cuh", ROOT / "include" / "owsm_dec.h"]
+HEADERS = [PKG / "csrc" / "ptx.cuh", PKG / "csrc" / "cluster.cuh", ROOT / "include" / "owsm_dec.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

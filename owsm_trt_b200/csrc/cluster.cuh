@@ -1,0 +1,668 @@
+// The cluster kernel: the same decoder call as decoder_kernel with three grid-wide exchanges per layer
+// instead of eight. Included by decoder.cu (it reuses that file's GEMM, attention and output-stage code).
+//
+// Layout of the call. The grid is NCL clusters of 4 CTAs (one CTA per SM). Per layer:
+//   S1  cluster (head h, row group rg): LN1 of the group's tokens -> the head's q/k/v rows (each CTA 48 of
+//       the 192 rows, exchanged through distributed shared memory) -> masked self-attention of the group's
+//       rows, split over the 4 CTAs by row or by position range, partial softmax states exchanged the same
+//       way and combined in a fixed order -> the head's slice of the out-projection (each CTA a quarter of
+//       the output features, K = 64) added into the next residual buffer.
+//   S2  the same for cross-attention: LN2 -> the head's cross-query rows -> attention over the group's
+//       utterances' encoder frames -> the head's slice of the cross-out projection.
+//   S3  cluster c < NCL3 owns F / NCL3 hidden units: LN3 of all tokens -> its FFN1 rows (+ReLU), exchanged
+//       -> its slice of FFN2 (K = F / NCL3) added into the next residual buffer.
+// The residual stream is int64 fixed point (32 fraction bits) in three rotating buffers: a stage reads
+// buffer k, adds its contributions into buffer k + 1 with integer atomics (exact, so the result does not
+// depend on their order: the call stays bit-reproducible) and zeroes buffer k + 2, which the stage before
+// read. Every CTA also adds its slice of (input residual + the stage's output bias), so each element of the
+// next buffer is x + bias + the sum of the heads' (or hidden slices') contributions.
+//
+// Exchanges inside a cluster use st.async stores into the other CTAs' shared memory, counted in bytes on
+// the receiver's mbarrier (which expects the bytes it will receive), so no cluster-wide barrier is needed
+// after start-up and the producer warp never has to take part in one. All waits are bounded.
+#pragma once
+
+namespace owsm {
+
+constexpr int CS = 4;          // CTAs per cluster
+constexpr int XQ_FLOATS = 16 * 3 * DK;  // exchange buffer: q/k/v rows of up to 16 tokens (fp32)
+constexpr int PART_ENTRIES = 64;        // partial softmax states of one stage (units x queries)
+
+// What this CTA's cluster owns in the three stages of a layer.
+struct Cl {
+  int cid, r;      // cluster index, rank in the cluster
+  int h, rg;       // S1/S2: head and row group (valid when cid < H * RG)
+  int u0, u1;      // utterances of the row group
+  int b0, Rg;      // its rows
+  int m0, Mg;      // its tokens [m0, m0 + Mg)
+  bool ffn;        // S3: cid < NCL3
+};
+
+__device__ __forceinline__ Cl cluster_view(const PlanDev& pd) {
+  Cl v;
+  v.cid = blockIdx.x / CS;
+  v.r = blockIdx.x % CS;
+  const bool heads = v.cid < pd.H * pd.RG;
+  v.h = heads ? v.cid % pd.H : 0;
+  v.rg = heads ? v.cid / pd.H : 0;
+  v.u0 = heads ? pd.U * v.rg / pd.RG : 0;
+  v.u1 = heads ? pd.U * (v.rg + 1) / pd.RG : 0;
+  v.b0 = v.u0 * pd.G;
+  v.Rg = (v.u1 - v.u0) * pd.G;
+  v.m0 = v.b0 * pd.S;
+  v.Mg = v.Rg * pd.S;
+  v.ffn = v.cid < pd.NCL3;
+  return v;
+}
+
+// Attention units of a stage inside the cluster: `items` rows (S1) or utterances (S2), each split into
+// `parts` position ranges when there are fewer items than CTAs; unit k = item * parts + part goes to
+// cluster CTA k % 4.
+__device__ __forceinline__ int unit_parts(int items) { return items >= CS ? 1 : CS / items; }
+
+// Shared-memory view of the cluster stages' work area.
+struct ClSmem {
+  __half* bbuf;   // LayerNorm output, B-fragment order (NT tiles x D)
+  float* xq;      // exchange: q/k/v (S1, [token][192]) or cross queries (S2, [token][64]) or FFN hidden
+                  // (S3, B-fragment order over the cluster's F3 hidden units)
+  float* part;    // exchange: partial softmax states [entry][XPS]
+  __half* obuf;   // attention output of the group's tokens, B-fragment order (K = 64)
+  uint8_t* attn;  // carve_attn area
+};
+
+__host__ __device__ constexpr size_t cl_bbuf_bytes(int NT, int D) { return (size_t)NT * D * 16; }
+__host__ __device__ constexpr size_t cl_work_bytes(int NT, int D, int Qmax) {
+  return cl_bbuf_bytes(NT, D) + (size_t)XQ_FLOATS * 4 + (size_t)PART_ENTRIES * XPS * 4 + (size_t)4 * NT * 256 +
+         attn_smem(Qmax) + 64;
+}
+
+__device__ __forceinline__ ClSmem carve_cl(uint8_t* work, int NT, int D) {
+  ClSmem s;
+  uint8_t* p = work;
+  s.bbuf = reinterpret_cast<__half*>(p); p += cl_bbuf_bytes(NT, D);
+  s.xq = reinterpret_cast<float*>(p); p += (size_t)XQ_FLOATS * 4;
+  s.part = reinterpret_cast<float*>(p); p += (size_t)PART_ENTRIES * XPS * 4;
+  s.obuf = reinterpret_cast<__half*>(p); p += (size_t)4 * NT * 256;
+  s.attn = p;
+  return s;
+}
+
+// ------------------------------------------------------------------------------------------------ schedule
+// Keys then values of positions p0 .. p1 - 1 (rows of 128 bytes), a chunk of at most apos positions each.
+template <class Fn>
+__device__ __forceinline__ void kv_chunks(const PlanDev& pd, const __half* kb, const __half* vb, int p0, int p1, Fn& fn) {
+  for (int j0 = p0; j0 < p1; j0 += pd.apos) {
+    const int n = p1 - j0 < pd.apos ? p1 - j0 : pd.apos;
+    fn((const void*)(kb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u);
+    fn((const void*)(vb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u);
+  }
+}
+
+// The byte ranges the producer copies for cluster stage `kind` of layer `l`, in the order the consumers use
+// them: fn(src, piece_bytes, pieces, piece_stride_bytes) per ring chunk (the pieces land back to back).
+template <class Fn>
+__device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, const int* pre, const int* offs,
+                          int kind, int l, Fn&& fn) {
+  const int D = pd.D, H = pd.H, S = pd.S, r = cl.r;
+  auto blocks = [&](int gi, int blk) {  // one whole 16-row block (K = D) with its bias tail
+    const GemmW& gw = pd.g[gi];
+    fn((const void*)(gw.w + (long long)l * gw.lstride + (long long)blk * gw.bstride), (uint32_t)gw.bstride * 16, 1, 0u);
+  };
+  // 16-row blocks rb0 .. rb0 + nb - 1 of GEMM gi, k-blocks kb0 .. kb0 + nkb - 1 of each, packed per chunk
+  auto kslices = [&](int gi, int rb0, int nb, int kb0, int nkb) {
+    const GemmW& gw = pd.g[gi];
+    const uint32_t piece = (uint32_t)nkb * 512;
+    const int per = pd.slot / (int)piece;
+    for (int b = 0; b < nb; b += per) {
+      const int n = nb - b < per ? nb - b : per;
+      fn((const void*)(gw.w + (long long)l * gw.lstride + (long long)(rb0 + b) * gw.bstride + (long long)kb0 * 32), piece,
+         n, (uint32_t)gw.bstride * 16);
+    }
+  };
+  if (kind == 1 || kind == 2) {
+    if (cl.cid >= H * pd.RG || cl.Mg == 0) return;
+    const int h = cl.h;
+    if (kind == 1) {
+      for (int j = 0; j < 3; ++j) {  // rows 48 r .. 48 r + 47 of the head's q | k | v
+        const int i = 3 * r + j, part = i / 4, sub = i % 4;
+        blocks(G_QKV, part * (D / 16) + 4 * h + sub);
+      }
+      const int parts = unit_parts(cl.Rg);
+      for (int k = r; k < cl.Rg * parts; k += CS) {
+        const int b = cl.b0 + k / parts, p = k % parts, off = offs[b];
+        const long long base = (((long long)l * pd.R + b) * H + h) * pd.C * DK;
+        kv_chunks(pd, a.kc + base, a.vc + base, off * p / parts, off * (p + 1) / parts, fn);
+      }
+      kslices(G_WO, r * (D / 64), D / 64, 4 * h, 4);
+    } else {
+      blocks(G_CQ, 4 * h + r);
+      const int ng = cl.u1 - cl.u0, parts = unit_parts(ng);
+      for (int k = r; k < ng * parts; k += CS) {
+        const int u = cl.u0 + k / parts, p = k % parts, len = pre[u + 1] - pre[u];
+        const long long base = (((long long)l * pd.U + u) * H + h) * (long long)pd.T * DK;
+        kv_chunks(pd, a.ck + base, a.cv + base, len * p / parts, len * (p + 1) / parts, fn);
+      }
+      kslices(G_WCO, r * (D / 64), D / 64, 4 * h, 4);
+    }
+    return;
+  }
+  if (kind == 3) {
+    if (!cl.ffn) return;
+    const int F3 = pd.F3, rows = F3 / CS;
+    for (int j = 0; j < rows / 16; ++j) blocks(G_F1, (cl.cid * F3 + r * rows) / 16 + j);
+    kslices(G_F2, r * (D / 64), D / 64, cl.cid * F3 / 16, F3 / 16);
+  }
+  (void)S;
+}
+
+}  // namespace owsm
+
+namespace owsm {
+
+// ------------------------------------------------------------------------------------------------ GEMM cores
+// One 16-row block (A fragments at `ash` + lane * 16, nkb k-blocks, nkb even) times the B operand at `bsh`.
+template <int NT>
+__device__ __forceinline__ void block_mma(uint32_t ash, int nkb, uint32_t bsh, float (&acc)[NT][4]) {
+  const int lane = threadIdx.x & 31;
+  float acc1[NT][4];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] = acc1[nt][e] = 0.f;
+  uint32_t bp = bsh + lane * 8;
+#pragma unroll 2
+  for (int kb = 0; kb < nkb; kb += 2) {
+    const uint4 a0 = lds128_u32(ash + kb * 512);
+    const uint4 a1 = lds128_u32(ash + (kb + 1) * 512);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint2 b0 = lds64_u32(bp + nt * 256);
+      const uint2 b1 = lds64_u32(bp + (NT + nt) * 256);
+      mma16816(acc[nt], a0, b0.x, b0.y);
+      mma16816(acc1[nt], a1, b1.x, b1.y);
+    }
+    bp += 2 * NT * 256;
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[nt][e] += acc1[nt][e];
+}
+
+// All consumer warps on one ring chunk of `nblk` blocks (block i at abase + i * astride): warp w takes
+// blocks w, w + 7, ...; epi(i, acc) per block.
+template <int NT, class Epi>
+__device__ __forceinline__ void chunk_gemm(uint32_t abase, int nblk, uint32_t astride, int nkb, uint32_t bsh, Epi&& epi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = warp; i < nblk; i += NWARP) {
+    float acc[NT][4];
+    block_mma<NT>(abase + (uint32_t)i * astride + lane * 16, nkb, bsh, acc);
+    epi(i, acc);
+  }
+}
+
+// The stage's single-block chunks j = 0 .. nch - 1 (16 rows x nkb k-blocks + a 64-byte bias tail), one warp
+// per chunk: the warp whose index is the chunk's ring slot (warps past the slot count idle), so each slot has
+// one consumer per phase. epi(j, acc, bias of rows g, g + 8).
+template <int NT, class Epi>
+__device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& epi) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
+  const int ns = ring.ns;
+  const int j0 = warp < ns ? (warp - (int)(ring.i % (uint32_t)ns) + ns) % ns : nch;
+  for (int j = j0; j < nch; j += ns) {
+    const uint8_t* slot = ring.wait_at(ring.i + j);
+    float acc[NT][4];
+    block_mma<NT>(smem_u32(slot) + lane * 16, nkb, bsh, acc);
+    const float* tail = reinterpret_cast<const float*>(slot + (size_t)nkb * 512);
+    const float bia[2] = {tail[g], tail[g + 8]};
+    ring.release_at(ring.i + j);
+    epi(j, acc, bia);
+  }
+  ring.i += nch;
+}
+
+// ------------------------------------------------------------------------------------------------ attention
+// One attention unit on all consumer warps: Q queries (s.q, fp32 [Q][64], scaled) over the cached keys and
+// values of positions p0 .. p1 - 1 (ring chunks: keys then values, apos positions per chunk), then with
+// nnew > 0 the call's own keys/values (s.knew / s.vnew [nnew][64]; query q sees new key j <= q, Q = nnew).
+// Leaves the unnormalised output in s.out, the running max / sum in s.mrun / s.lrun.
+template <int QM>
+__device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x < Q) {
+    s.mrun[threadIdx.x] = -INFINITY;
+    s.lrun[threadIdx.x] = 0.f;
+  }
+  AttnAcc<QM> acc;
+#pragma unroll
+  for (int q = 0; q < QM; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
+  csync();
+  Q1Regs qr;
+  if (QM == 1) qr = q1_load(s.q);
+  for (int j0 = p0; j0 < p1; j0 += apos) {
+    const int npos = p1 - j0 < apos ? p1 - j0 : apos;
+    const __half* kt = reinterpret_cast<const __half*>(ring.wait());
+    chunk_scores<QM>(s, qr, kt, npos, Q);
+    ring.release();
+    csync();
+    attn_softmax(s.sc, npos, Q, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
+    csync();
+    const __half* vt = reinterpret_cast<const __half*>(ring.wait());
+    attn_accum<QM>(acc, s.sc, s.alpha, vt, npos, Q);
+    ring.release();
+    csync();
+  }
+  if (nnew > 0) {  // the new tokens, causally: a warp per (query, key) dot product
+    for (int pr = warp; pr < Q * nnew; pr += NWARP) {
+      const int q = pr / nnew, j = pr % nnew;
+      float sum = s.q[q * DK + lane] * s.knew[j * DK + lane] + s.q[q * DK + lane + 32] * s.knew[j * DK + lane + 32];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) s.sc[q * APOS + j] = sum;
+    }
+    csync();
+    attn_softmax(s.sc, nnew, Q, s.mrun, s.lrun, s.alpha, [](int q, int j) { return j <= q; });
+    csync();
+#pragma unroll
+    for (int q = 0; q < QM; ++q)
+      if (q < Q) {
+        acc.o[q][0] *= s.alpha[q];
+        acc.o[q][1] *= s.alpha[q];
+      }
+    for (int j = warp; j < nnew; j += NWARP) {
+      const float2 v = make_float2(s.vnew[j * DK + 2 * lane], s.vnew[j * DK + 2 * lane + 1]);
+#pragma unroll
+      for (int q = 0; q < QM; ++q)
+        if (q < Q) {
+          const float p = s.sc[q * APOS + j];
+          acc.o[q][0] += p * v.x;
+          acc.o[q][1] += p * v.y;
+        }
+    }
+  }
+  attn_reduce<QM>(acc, Q, s.scratch, s.out);
+}
+
+// ------------------------------------------------------------------------------------------------ stages
+// Embedding into the fixed-point residual buffer 0 (this CTA's slice); buffer 1, which the first stage adds
+// into, is zeroed.
+__device__ void cl_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
+  const long long total = (long long)pd.M * pd.D;
+  const long long lo = total * c / pd.P, hi = total * (c + 1) / pd.P;
+  for (long long i = lo + threadIdx.x; i < hi; i += NTHR) {
+    const int m = (int)(i / pd.D), n = (int)(i % pd.D);
+    const int r = m / pd.S, s = m % pd.S;
+    long long t = a.tok[(long long)r * a.tok_stride + s];
+    t = t < 0 ? 0 : (t >= pd.V ? pd.V - 1 : t);
+    long long pos = (long long)cx.offs[r] + s;
+    pos = pos >= pd.max_pos ? pd.max_pos - 1 : pos;
+    pd.xf[0][i] = to_fix(__half2float(pd.emb[t * pd.D + n]) * pd.xscale + pd.pe[pos * pd.D + n]);
+    pd.xf[1][i] = 0;
+  }
+}
+
+// This CTA's slice of the next residual buffer: + input residual + the stage's output bias; and its slice
+// of the free buffer zeroed (the stage after next adds into it).
+__device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* xin, long long* xout, long long* xfree,
+                            int c) {
+  const long long total = (long long)pd.M * pd.D;
+  const long long lo = total * c / pd.P, hi = total * (c + 1) / pd.P;
+  const float* bias = pd.g[gi].b + (long long)l * pd.D;
+  for (long long i = lo + threadIdx.x; i < hi; i += NTHR) {
+    red_add_s64(xout + i, __ldcg(xin + i) + to_fix(__ldg(bias + i % pd.D)));
+    xfree[i] = 0;
+  }
+}
+
+// S1 (kind 1, self-attention) or S2 (kind 2, cross-attention) of a cluster that owns (head h, row group).
+template <int NT>
+__device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, const Cl& cl,
+                              const int* pre, int kind, int l, uint8_t* work, uint64_t* xbar, uint32_t (&ph)[2],
+                              const long long* xin, long long* xout) {
+  const int D = pd.D, H = pd.H, S = pd.S, h = cl.h, r = cl.r, Mg = cl.Mg;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const ClSmem sm = carve_cl(work, NT, D);
+  const int nq = kind == 1 ? 3 * DK : DK;  // the head's projected rows: q | k | v, or q
+  const int my = kind == 1 ? 48 : 16;      // of which this CTA computes rows my * r .. my * r + my - 1
+  const int items = kind == 1 ? cl.Rg : cl.u1 - cl.u0;
+  const int parts = unit_parts(items), nunits = items * parts;
+  const int Qu = kind == 1 ? S : pd.G * S;  // queries of a unit
+  const int mine = r < nunits ? (nunits - r + CS - 1) / CS : 0;
+  if (threadIdx.x == 0) {
+    mbar_arrive_expect_tx(&xbar[0], (uint32_t)((CS - 1) * my * Mg * 4));
+    mbar_arrive_expect_tx(&xbar[1], (uint32_t)((nunits - mine) * Qu * XPS * 4));
+  }
+  ln_rows(pd, xin, cl.m0, Mg, NT, sm.bbuf, cx);
+  csync();
+  const uint32_t xq_s = smem_u32(sm.xq), part_s = smem_u32(sm.part);
+  uint32_t rxq[CS - 1], rpart[CS - 1], rbar0[CS - 1], rbar1[CS - 1];
+#pragma unroll
+  for (int i = 0; i < CS - 1; ++i) {
+    const uint32_t dst = (uint32_t)((r + 1 + i) % CS);
+    rxq[i] = mapa_shared(xq_s, dst);
+    rpart[i] = mapa_shared(part_s, dst);
+    rbar0[i] = mapa_shared(smem_u32(&xbar[0]), dst);
+    rbar1[i] = mapa_shared(smem_u32(&xbar[1]), dst);
+  }
+  // the head's projection rows of this CTA -> every cluster CTA's exchange buffer (and the cache)
+  block_chunks<NT>(ring, my / 16, D / 16, smem_u32(sm.bbuf), [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = my * r + j * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
+        if (m >= Mg) continue;
+        const __half yh = __float2half_rn(acc[nt][e] + bia[e >> 1]);
+        const float y = __half2float(yh);  // fp16 like the projection output the reference attends with
+        const int idx = m * nq + row;
+        sm.xq[idx] = y;
+#pragma unroll
+        for (int i = 0; i < CS - 1; ++i) st_async_b32(rxq[i] + idx * 4, __float_as_uint(y), rbar0[i]);
+        if (kind == 1 && row >= DK) {  // new key / value: the cache slot and new_kv
+          const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
+          const long long cslot = ((((long long)l * pd.R + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
+          (kv ? a.vc : a.kc)[cslot] = yh;
+          a.new_kv[((((long long)(l * 2 + kv) * pd.R + b) * H + h) * S + s) * DK + d] = yh;
+        }
+      }
+  });
+  csync();
+  if (!mbar_wait_cluster(&xbar[0], ph[0], pd.max_spin)) {
+    ring.dead = true;
+    atomicExch(pd.err, E_ERR_TIMEOUT);
+  }
+  ph[0] ^= 1u;
+  // this CTA's attention units -> their partial softmax states into every cluster CTA's table
+  const AttnSmem as = carve_attn(sm.attn, pd.Qmax);
+  for (int k = r; k < nunits; k += CS) {
+    const int item = k / parts, p = k % parts;
+    int p0, p1, nnew = 0;
+    if (kind == 1) {
+      const int b = cl.b0 + item, off = cx.offs[b];
+      p0 = off * p / parts;
+      p1 = off * (p + 1) / parts;
+      nnew = (p == parts - 1) ? S : 0;
+      for (int idx = threadIdx.x; idx < S * DK; idx += NTHR) {
+        const int q = idx / DK, d = idx % DK, ml = item * S + q;
+        as.q[idx] = sm.xq[ml * nq + d] * 0.125f;
+        as.knew[idx] = sm.xq[ml * nq + DK + d];
+        as.vnew[idx] = sm.xq[ml * nq + 2 * DK + d];
+      }
+    } else {
+      const int u = cl.u0 + item, len = pre[u + 1] - pre[u];
+      p0 = len * p / parts;
+      p1 = len * (p + 1) / parts;
+      for (int idx = threadIdx.x; idx < Qu * DK; idx += NTHR) {
+        const int q = idx / DK, d = idx % DK;
+        as.q[idx] = sm.xq[(item * Qu + q) * nq + d] * 0.125f;
+      }
+    }
+    if (Qu == 1) attn_unit<1>(as, ring, Qu, p0, p1, pd.apos, nnew);
+    else attn_unit<MAXQ>(as, ring, Qu, p0, p1, pd.apos, nnew);
+    for (int idx = threadIdx.x; idx < Qu * (XPS / 4); idx += NTHR) {
+      const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
+      float4 v;
+      if (c4 < DK / 4) v = lds128f(&as.out[q * DK + c4 * 4]);
+      else v = make_float4(as.mrun[q], as.lrun[q], 0.f, 0.f);
+      const int off = (k * Qu + q) * XPS + c4 * 4;
+      sts128f(&sm.part[off], v);
+      const uint4 w = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
+#pragma unroll
+      for (int i = 0; i < CS - 1; ++i) st_async_v4(rpart[i] + off * 4, w, rbar1[i]);
+    }
+    csync();
+  }
+  if (!mbar_wait_cluster(&xbar[1], ph[1], pd.max_spin)) {
+    ring.dead = true;
+    atomicExch(pd.err, E_ERR_TIMEOUT);
+  }
+  ph[1] ^= 1u;
+  // every token of the group: its units' parts combined in part order -> the out-projection's B operand
+  for (int idx = threadIdx.x; idx < NT * 8 * (DK / 2); idx += NTHR) {
+    const int m = idx / (DK / 2), dp = idx % (DK / 2);
+    float n0 = 0.f, n1 = 0.f;
+    if (m < Mg) {
+      const int item = m / Qu, q = m % Qu;
+      const float* e0 = sm.part + ((size_t)(item * parts) * Qu + q) * XPS;
+      const size_t step = (size_t)Qu * XPS;
+      float mx = -INFINITY;
+      for (int p = 0; p < parts; ++p) mx = fmaxf(mx, e0[p * step + DK]);
+      float den = 0.f;
+      for (int p = 0; p < parts; ++p) {
+        const float mp = e0[p * step + DK];
+        if (mp > -INFINITY) {
+          const float w = expf(mp - mx);
+          den += w * e0[p * step + DK + 1];
+          n0 += w * e0[p * step + 2 * dp];
+          n1 += w * e0[p * step + 2 * dp + 1];
+        }
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      n0 *= inv;
+      n1 *= inv;
+    }
+    *reinterpret_cast<__half2*>(&sm.obuf[bfrag_idx(m, 2 * dp, NT)]) = __floats2half2_rn(n0, n1);
+  }
+  csync();
+  // the head's slice of the out-projection: output rows (D / 4) r .. , k-blocks 4 h .. 4 h + 3
+  const int nb = D / 64, per = pd.slot / 2048;
+  for (int bb = 0; bb < nb; bb += per) {
+    const int n = nb - bb < per ? nb - bb : per;
+    const uint8_t* slot = ring.wait();
+    chunk_gemm<NT>(smem_u32(slot), n, 2048u, 4, smem_u32(sm.obuf), [&](int i, const float (&acc)[NT][4]) {
+      const int rb = r * nb + bb + i;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int nn = rb * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
+          if (m < Mg) red_add_s64(xout + (long long)(cl.m0 + m) * D + nn, to_fix(acc[nt][e]));
+        }
+    });
+    ring.release();
+  }
+}
+
+// S3: FFN1 rows of this cluster's hidden slice (+ReLU), exchanged as B fragments; FFN2 slice -> residual.
+template <int NT>
+__device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const Cl& cl, uint8_t* work,
+                             uint64_t* xbar, uint32_t (&ph)[2], const long long* xin, long long* xout) {
+  const int D = pd.D, M = pd.M, r = cl.r, F3 = pd.F3, rows = F3 / CS, nkb3 = F3 / 16;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const ClSmem sm = carve_cl(work, NT, D);
+  __half* hb = reinterpret_cast<__half*>(sm.xq);  // B fragments over the F3 hidden units (nkb3 k-blocks)
+  const int kb_mine = rows / 16;                   // this CTA's k-blocks: r * kb_mine ..
+  const uint32_t my_bytes = (uint32_t)kb_mine * NT * 256;
+  if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar[0], (CS - 1) * my_bytes);
+  ln_rows(pd, xin, 0, M, NT, sm.bbuf, cx);
+  csync();
+  block_chunks<NT>(ring, rows / 16, D / 16, smem_u32(sm.bbuf), [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int k = r * rows + j * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
+        const float y = m < M ? fmaxf(acc[nt][e] + bia[e >> 1], 0.f) : 0.f;
+        hb[bfrag_idx(m, k, NT)] = __float2half_rn(y);
+      }
+  });
+  csync();
+  const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;
+  const uint32_t bar0 = smem_u32(&xbar[0]);
+  for (int i = threadIdx.x; i < (int)(my_bytes / 16); i += NTHR) {
+    const uint4 v = lds128_u32(mine_s + i * 16);
+#pragma unroll
+    for (int q = 1; q < CS; ++q) {
+      const uint32_t dst = (uint32_t)((r + q) % CS);
+      st_async_v4(mapa_shared(mine_s + i * 16, dst), v, mapa_shared(bar0, dst));
+    }
+  }
+  if (!mbar_wait_cluster(&xbar[0], ph[0], pd.max_spin)) {
+    ring.dead = true;
+    atomicExch(pd.err, E_ERR_TIMEOUT);
+  }
+  ph[0] ^= 1u;
+  const int nb = D / 64, piece = nkb3 * 512, per = pd.slot / piece;
+  for (int bb = 0; bb < nb; bb += per) {
+    const int n = nb - bb < per ? nb - bb : per;
+    const uint8_t* slot = ring.wait();
+    chunk_gemm<NT>(smem_u32(slot), n, (uint32_t)piece, nkb3, smem_u32(hb), [&](int i, const float (&acc)[NT][4]) {
+      const int rb = r * nb + bb + i;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int nn = rb * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
+          if (m < M) red_add_s64(xout + (long long)m * D + nn, to_fix(acc[nt][e]));
+        }
+    });
+    ring.release();
+  }
+}
+
+}  // namespace owsm
+
+namespace owsm {
+
+// The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output.
+template <int NT>
+__global__ void __launch_bounds__(BLOCK, 1)
+    decoder_cl_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + MAXSLOT;
+  uint64_t* xbar = empty + MAXSLOT;  // the two exchange barriers of a stage
+  int* pre = reinterpret_cast<int*>(smem + pd.off_pre);
+  uint8_t* ringdata = smem + pd.off_ring;
+  uint8_t* work = smem + pd.off_work;
+  const int c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int L = pd.L, n_stages = 3 * L + 2;
+  int* so = reinterpret_cast<int*>(smem + pd.off_sched);
+  int* sb = so + NGEMM + 1;
+  int* offs = reinterpret_cast<int*>(smem + pd.off_rows);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < pd.nslot; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NWARP);
+    }
+    mbar_init(&xbar[0], 1);
+    mbar_init(&xbar[1], 1);
+    fence_barrier_init();
+    pre[0] = 0;
+    for (int u = 0; u < pd.U; ++u) pre[u + 1] = pre[u] + utt_len(pd, a, u);
+    so[0] = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) so[gi + 1] = so[gi] + (pd.goff[gi][c + 1] - pd.goff[gi][c]);
+  }
+  for (int r = threadIdx.x; r < pd.R; r += BLOCK) offs[r] = row_off_global(pd, a, r);
+  __syncthreads();
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const int base = pd.goff[gi][c];
+    for (int i = threadIdx.x; i < so[gi + 1] - so[gi]; i += BLOCK) sb[so[gi] + i] = pd.gblk[gi][base + i];
+  }
+  // every CTA of the cluster has initialised its barriers before any CTA sends to them
+  cluster_sync_all();
+  unsigned long long* evlog = pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
+  int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
+  if (threadIdx.x == 0) *nev = 0;
+  __syncthreads();
+  const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
+  Frames fr;  // (the output stage's GEMM helpers take it; the cluster stages do not split frames this way)
+  fr.total = (long long)pd.H * pre[pd.U];
+  fr.U = pd.U;
+  fr.H = pd.H;
+  fr.P = (int)(fr.total < pd.P ? fr.total : pd.P);
+  fr.pre = pre;
+  const Cl cl = cluster_view(pd);
+
+  if (warp == NWARP) {  // producer
+    if (lane == 0) {
+      uint32_t i = 0;
+      bool dead = false;
+      auto put = [&](const void* src, uint32_t piece, int pieces, uint32_t stride, uint64_t pol) {
+        if (dead) return;
+        const int s = i % pd.nslot;
+        if (!mbar_wait(&empty[s], ((i / pd.nslot) & 1) ^ 1, pd.max_spin)) {
+          dead = true;
+          atomicExch(pd.err, E_ERR_TIMEOUT);
+          return;
+        }
+        if (i >= (uint32_t)pd.inflight) {
+          const uint32_t j = i - pd.inflight;
+          if (!mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, pd.max_spin)) {
+            dead = true;
+            atomicExch(pd.err, E_ERR_TIMEOUT);
+            return;
+          }
+        }
+        mbar_arrive_expect_tx(&full[s], piece * (uint32_t)pieces);
+        for (int q = 0; q < pieces; ++q)
+          bulk_g2s(ringdata + (size_t)s * pd.sstride + (size_t)q * piece,
+                   reinterpret_cast<const uint8_t*>(src) + (size_t)q * stride, piece, &full[s], pol);
+        ++i;
+      };
+      const uint64_t first = policy_evict_first();
+      for (int g = 1; g < n_stages && !dead; ++g) {
+        if (g == n_stages - 1) {  // output stage: the grid kernel's block schedule
+          for_chunks(pd, a, fr, cx, 8 * L + 1, c, [&](const void* src, uint32_t bytes) { put(src, bytes, 1, 0u, first); });
+        } else {
+          const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;
+          cl_chunks(pd, a, cl, pre, offs, kind, l,
+                    [&](const void* src, uint32_t piece, int pieces, uint32_t stride) { put(src, piece, pieces, stride, first); });
+        }
+      }
+      const uint32_t from = i > (uint32_t)pd.nslot ? i - pd.nslot : 0;
+      for (uint32_t j = from; j < i; ++j) mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, DEFAULT_SPIN);
+    }
+    return;
+  }
+
+  Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
+  OutState os = carve_out(smem + pd.off_out, pd.M, false);
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    os.amax[m] = -INFINITY;
+    os.aidx[m] = 0x7fffffff;
+  }
+  int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
+  uint32_t ph[2] = {0u, 0u};
+  bool dead = false;
+  for (int g = 0; g < n_stages; ++g) {
+    unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (ts && threadIdx.x == 0) ts[0] = globaltimer();
+    if (g == 0) {
+      cl_embed(pd, a, cx, c);
+    } else if (g < n_stages - 1) {
+      const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;
+      const long long* xin = pd.xf[(g - 1) % 3];
+      long long* xout = pd.xf[g % 3];
+      long long* xfree = pd.xf[(g + 1) % 3];
+      cl_residual(pd, kind == 1 ? G_WO : (kind == 2 ? G_WCO : G_F2), l, xin, xout, xfree, c);
+      if (kind < 3) {
+        if (cl.cid < pd.H * pd.RG && cl.Mg > 0) cl_attn_stage<NT>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);
+      } else if (cl.ffn) {
+        cl_ffn_stage<NT>(pd, ring, cx, cl, work, xbar, ph, xin, xout);
+      }
+      __threadfence();
+    } else {
+      gemm_stage<NT>(pd, a, ring, cx, fr, K_OUT, 0, c, work, os);
+      csync();
+      if (a.pred) argmax_finish(pd, a, c, os, flag, work);
+    }
+    if (ts && threadIdx.x == 0) ts[1] = globaltimer();
+    if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead);
+    if (ts && threadIdx.x == 0) {
+      ts[2] = globaltimer();
+      ts[3] = ring.waited;
+    }
+    ring.waited = 0;
+  }
+  csync();
+  if (threadIdx.x == 0) {
+    if (atom_acq_rel_add(&pd.ctr[1], 1) == (uint32_t)(pd.P - 1)) {
+      atomicExch(&pd.ctr[1], 0u);
+      atomicExch(&pd.ctr[0], 0u);
+    }
+  }
+}
+
+}  // namespace owsm

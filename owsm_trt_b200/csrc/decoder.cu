@@ -95,6 +95,10 @@ struct PlanDev {
   int inflight;             // bulk copies in flight per CTA (ring slots may hold more, finished)
   int stage_b;              // largest non-LayerNorm B operand staged in shared memory (bytes)
   int work_bytes;           // size of the work area
+  const long long* xfix;    // cluster kernel: the fixed-point residual stream the output stage normalises
+  int cl;                   // 1: the cluster kernel runs this plan
+  int RG, NCL3, F3;         // cluster kernel: row groups per head, clusters of the FFN stage, hidden units each
+  long long* xf[3];         // cluster kernel: rotating fixed-point residual buffers [M][D]
 };
 
 struct CallArgs {
@@ -363,12 +367,22 @@ struct Work {  // shared-memory work area, carved per stage
 // LayerNorm of the residual stream x [M][D] (eps) into B-fragment order (fp16) in shared memory. One warp
 // per token; a lane holds its D / 32 values in registers (all loads issued at once: one L2 round trip).
 constexpr int MAXV4 = 8;  // D <= 1024: float4 loads per lane
-// LayerNorm of the M rows of x into the B operand (fragment order, shared memory), padding tokens zero.
+// Four consecutive values of a residual-stream row: fp32, or int64 fixed point (32 fraction bits).
+__device__ __forceinline__ float4 load4(const float* row, int i) { return __ldcg(reinterpret_cast<const float4*>(row) + i); }
+__device__ __forceinline__ float4 load4(const long long* row, int i) {
+  const longlong2 a = __ldcg(reinterpret_cast<const longlong2*>(row) + 2 * i);
+  const longlong2 b = __ldcg(reinterpret_cast<const longlong2*>(row) + 2 * i + 1);
+  return make_float4(from_fix(a.x), from_fix(a.y), from_fix(b.x), from_fix(b.y));
+}
+
+// LayerNorm of rows m0 .. m0 + M - 1 of the residual stream into the B operand (fragment order over NT
+// tiles of 8 tokens, shared memory), padding tokens zero.
 // From 7 rows on, a warp normalises whole rows; below that a row is split over a team of 7 / M warps whose
 // partial sums meet in shared memory, so one row costs one round trip for its loads and a few hundred
 // cycles rather than a single warp's serial pass over 1024 values.
-__device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
-  const int D = pd.D, M = pd.M, NT = pd.NT, nv = D / 4;
+template <class T>
+__device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __half* bbuf, const Ctx& cx) {
+  const int D = pd.D, nv = D / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
     for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
@@ -382,11 +396,11 @@ __device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
   };
   if (ts == 1) {
     for (int m = warp; m < M; m += NWARP) {
-      const float4* xr = reinterpret_cast<const float4*>(pd.x + (long long)m * D);
+      const T* xr = x + (long long)(m0 + m) * D;
       float4 v[MAXV4];
 #pragma unroll
       for (int i = 0; i < MAXV4; ++i)
-        if (i * 32 + lane < nv) v[i] = __ldcg(xr + i * 32 + lane);
+        if (i * 32 + lane < nv) v[i] = load4(xr, i * 32 + lane);
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < MAXV4; ++i)
@@ -418,10 +432,10 @@ __device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
   float4 v[MAXV4];
   float s = 0.f;
   if (on) {
-    const float4* xr = reinterpret_cast<const float4*>(pd.x + (long long)m * D);
+    const T* xr = x + (long long)(m0 + m) * D;
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
-      if (j * 32 + lane + k * step < nv) v[k] = __ldcg(xr + j * 32 + lane + k * step);
+      if (j * 32 + lane + k * step < nv) v[k] = load4(xr, j * 32 + lane + k * step);
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
       if (j * 32 + lane + k * step < nv) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
@@ -455,6 +469,13 @@ __device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
     for (int k = 0; k < MAXV4; ++k)
       if (j * 32 + lane + k * step < nv) emit(m, j * 32 + lane + k * step, v[k], mean, rstd);
   }
+}
+
+// The B operand of a LayerNorm GEMM stage over all M tokens: from the fp32 residual stream, or from the
+// fixed-point one of the cluster kernel when the plan names it.
+__device__ void ln_to_frag(const PlanDev& pd, __half* bbuf, const Ctx& cx) {
+  if (pd.xfix) ln_rows(pd, pd.xfix, 0, pd.M, pd.NT, bbuf, cx);
+  else ln_rows(pd, pd.x, 0, pd.M, pd.NT, bbuf, cx);
 }
 
 // Per-token running results of the output stage (shared memory). The CTA-level arrays hold the stage's
@@ -1745,6 +1766,8 @@ __global__ void place_bias_kernel(const float* __restrict__ b, int N, uint4* __r
 
 }  // namespace owsm
 
+#include "cluster.cuh"
+
 // ================================================================================================ host / C ABI
 using namespace owsm;
 
@@ -1786,6 +1809,7 @@ struct OwsmDec {
   float* pe = nullptr;
   int* err = nullptr;  // device error word
   uint32_t max_spin = DEFAULT_SPIN;
+  int path = 0;  // 0: cluster kernel where it applies, 1: always the grid-stage kernel, 2: cluster kernel or fail
   ~OwsmDec() {
     int cur = 0;
     cudaGetDevice(&cur);
@@ -1906,6 +1930,10 @@ KernelFn kernel_for(int NT) {
   }
 }
 
+KernelFn cl_kernel_for(int NT) { return NT == 1 ? decoder_cl_kernel<1> : decoder_cl_kernel<2>; }
+
+KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT) : kernel_for(pd.NT); }
+
 
 }  // namespace
 
@@ -2020,7 +2048,11 @@ int owsm_dec_create(const OwsmDecDims* dims, const OwsmDecWeights* w, int device
 
 void owsm_dec_destroy(OwsmDec* h) { delete h; }
 
-int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out) {
+}  // extern "C"
+
+// The plan of a call shape; with allow_cl the cluster kernel where the shape allows it.
+static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, bool allow_cl,
+                     OwsmDecPlan** out) {
   if (!h || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
   *out = nullptr;
   const OwsmDecDims& d = h->dims;
@@ -2056,6 +2088,40 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
     delete p;
     return code;
   };
+  cudaDeviceProp prop0;
+  CUDA_TRY(cudaGetDeviceProperties(&prop0, h->device));
+  // The cluster kernel: greedy calls of up to 16 tokens. Clusters of 4 CTAs, as many as fit one per SM;
+  // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
+  // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
+  if (allow_cl && !beam && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
+    KernelFn kf = cl_kernel_for(pd.NT);
+    CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(BLOCK);
+    cfg.dynamicSmemBytes = prop0.sharedMemPerBlockOptin;
+    cfg.gridDim = dim3(CS);
+    int ncl = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveClusters(&ncl, (void*)kf, &cfg));
+    ncl = std::min(ncl, h->programs / CS);
+    int ncl3 = 0;
+    for (int q = 1; q <= ncl; ++q)
+      if ((d.F / 64) % q == 0 && (size_t)(d.F / q / 16) * pd.NT * 256 <= (size_t)XQ_FLOATS * 4) ncl3 = q;
+    if (ncl >= d.H && ncl3 > 0) {
+      pd.cl = 1;
+      pd.P = ncl * CS;
+      pd.RG = std::max(1, std::min(ncl / d.H, U));
+      pd.NCL3 = ncl3;
+      pd.F3 = d.F / ncl3;
+    }
+  }
+  if (allow_cl && h->path == 2 && !pd.cl) return bail(fail(OWSM_DEC_ERR_LIMIT, "the cluster kernel does not take this call"));
   int rc;
   int64_t* tot = &p->scratch_bytes;
   // schedule
@@ -2077,7 +2143,13 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.oB, (size_t)NT * 8 * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.hB, (size_t)NT * 8 * F, tot))) return bail(rc);
-  if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * XPS, tot))) return bail(rc);
+  if (pd.cl) {
+    for (int i = 0; i < 3; ++i)
+      if ((rc = dev_alloc(p->allocs, &pd.xf[i], (size_t)M * D, tot))) return bail(rc);
+    pd.xfix = pd.xf[(3 * d.L) % 3];
+  } else if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * XPS, tot))) {
+    return bail(rc);
+  }
   if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
@@ -2139,14 +2211,18 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   // 32 KB slots while at least 4 fit (up to 6); else 16 KB slots while 4 fit; else the larger of the two
   // that leaves at least 2 slots
   size_t slot = SLOT, work = work_for(SLOT);
-  if (slots_left(work, SLOT) < 4) {
+  if (pd.cl) {  // stage buffers of the cluster kernel; its output stage as the grid kernel's; 32 KB slots
+    work = std::max(cl_work_bytes(NT, D, pd.Qmax), (size_t)NT * (D / 16) * 256 + 16);
+    work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);
+    if (slots_left(work, SLOT) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small for the cluster kernel"));
+  } else if (slots_left(work, SLOT) < 4) {
     const size_t w16 = work_for(SLOT / 2);
     if (slots_left(w16, SLOT / 2) >= 4 || slots_left(work, SLOT) < 2) slot = SLOT / 2, work = w16;
   }
   if (slots_left(work, slot) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small"));
   // staging for the cross-attention partials of the cross-out stage: 16 KB more when that leaves the ring as
   // it is (segments that do not fit are read from L2)
-  {
+  if (!pd.cl) {
     const size_t wco = (size_t)NT * D * 16 + 4 * (size_t)(U * d.H + 16) + 256 + 16384;
     if (slots_left(std::max(work, wco), slot) >= std::min<size_t>(slots_left(work, slot), 4)) work = std::max(work, wco);
   }
@@ -2165,12 +2241,22 @@ int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int 
   pd.work_bytes = (int)work;
   p->smem = (size_t)pd.off_work + work;
   // the attribute is per function: set it to the device maximum once, so plans of other sizes coexist
-  CUDA_TRY(cudaFuncSetAttribute(kernel_for(pd.NT), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+  CUDA_TRY(cudaFuncSetAttribute(plan_kernel(pd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
   int per_sm = 0;
-  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for(pd.NT), BLOCK, p->smem));
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan_kernel(pd), BLOCK, p->smem));
   if (per_sm < 1) return bail(fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM"));
   *out = p;
   return OWSM_DEC_OK;
+}
+
+extern "C" {
+
+int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out) {
+  if (!h) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  const int rc = plan_impl(h, R, S, C, T, rows_per_utt, beam, h->path != 1, out);
+  // a call the cluster kernel cannot lay out (shared memory, clusters) runs on the grid-stage kernel
+  if (rc == OWSM_DEC_ERR_LIMIT && h->path == 0) return plan_impl(h, R, S, C, T, rows_per_utt, beam, false, out);
+  return rc;
 }
 
 void owsm_dec_plan_destroy(OwsmDecPlan* p) { delete p; }
@@ -2179,16 +2265,20 @@ static int launch(OwsmDecPlan* p, void* stream, const CallArgs& a) {
   DeviceGuard guard(p->h->device);
   p->pd.max_spin = p->h->max_spin;
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = CS;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.gridDim = dim3(p->pd.P);
   cfg.blockDim = dim3(BLOCK);
   cfg.dynamicSmemBytes = p->smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  CUDA_TRY(cudaLaunchKernelEx(&cfg, kernel_for(p->pd.NT), p->pd, a));
+  cfg.numAttrs = p->pd.cl ? 2 : 1;
+  CUDA_TRY(cudaLaunchKernelEx(&cfg, plan_kernel(p->pd), p->pd, a));
   return OWSM_DEC_OK;
 }
 
@@ -2278,7 +2368,19 @@ int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps) {
 
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
-  return 8 * p->pd.L + 2 + (beam_call ? 3 : 0);
+  return p->pd.cl ? 3 * p->pd.L + 2 : 8 * p->pd.L + 2 + (beam_call ? 3 : 0);
+}
+
+int owsm_dec_set_path(OwsmDec* h, int path) {
+  if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
+  if (path < 0 || path > 2) return fail(OWSM_DEC_ERR_ARG, "path must be 0, 1 or 2");
+  h->path = path;
+  return OWSM_DEC_OK;
+}
+
+int owsm_dec_plan_kernel(const OwsmDecPlan* p) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  return p->pd.cl ? 2 : 1;
 }
 
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls) {

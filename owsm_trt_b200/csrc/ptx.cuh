@@ -180,6 +180,63 @@ __device__ __forceinline__ void sts128f(void* p, float4 v) {
                : "memory");
 }
 
+// ---------------------------------------------------------------- thread-block clusters
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// The address of this CTA's shared variable at `addr` in the shared memory of cluster CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+// Stores into another cluster CTA's shared memory that count their bytes on that CTA's mbarrier (the
+// receiver announces the bytes it expects with mbar_arrive_expect_tx and waits on the phase).
+__device__ __forceinline__ void st_async_b32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr), "r"(v),
+               "r"(rbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, uint4 v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+               "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
+               : "memory");
+}
+
+// Wait (bounded) for a phase of this CTA's mbarrier that other cluster CTAs complete: acquire at cluster
+// scope, so their stores are visible afterwards.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, uint32_t max_polls) {
+  for (uint32_t i = 0; i < max_polls; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+// All threads of all CTAs of the cluster (used once, at kernel start, before the warps take their roles).
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Fixed-point residual stream: int64 with 32 fraction bits; integer adds are exact, so the sum of a
+// stage's contributions does not depend on the order in which they land.
+__device__ __forceinline__ void red_add_s64(long long* p, long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * 4294967296.0f); }
+__device__ __forceinline__ float from_fix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
+
 // 16-byte asynchronous global -> shared copy through L2 only (data other CTAs wrote this call).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");

@@ -161,6 +161,18 @@ class B200Decoder:
                 _lib.lib().owsm_dec_plan_reset(p)
             raise RuntimeError("the decoder kernel timed out at a grid barrier (were all its CTAs resident?)")
 
+    def set_path(self, path: int) -> None:
+        """Which kernel later calls use: 0 the cluster kernel where the call allows it (default), 1 the
+        grid-stage kernel, 2 the cluster kernel or an error. Drops the cached plans."""
+        _lib.check(_lib.lib().owsm_dec_set_path(self._h, int(path)), "owsm_dec_set_path")
+        for p in self._plans.values():
+            _lib.lib().owsm_dec_plan_destroy(p)
+        self._plans.clear()
+
+    def plan_kernel(self, run) -> str:
+        """"cluster" or "grid": the kernel behind a step_fn / beam_fn closure."""
+        return "cluster" if _lib.lib().owsm_dec_plan_kernel(run.plan) == 2 else "grid"
+
     def set_max_spin(self, polls: int) -> None:
         """Testing hook: the in-kernel wait limit of later calls (0: the default)."""
         _lib.check(_lib.lib().owsm_dec_set_max_spin(self._h, polls), "owsm_dec_set_max_spin")
@@ -226,7 +238,7 @@ class B200Decoder:
         run.plan = plan
         run.beam = False
         run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, ntm, enc_len)
-        run.programs = self.programs
+        run.programs = self._plan_info(plan)[0]
         run.kernel = self
         return run
 

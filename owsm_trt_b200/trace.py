@@ -15,7 +15,10 @@ from . import _lib
 KINDS = ["QKV", "SATT", "WO", "CQ", "XATT", "WCO", "F1", "F2"]
 
 
-def stage_names(L: int, beam: bool) -> list[str]:
+def stage_names(L: int, beam: bool, cluster: bool = False) -> list[str]:
+    """Stage names of a call: the grid-stage kernel's eight per layer, or the cluster kernel's three."""
+    if cluster:
+        return ["EMBED"] + [("S1", "S2", "S3")[i % 3] for i in range(3 * L)] + ["OUT"]
     names = ["EMBED"] + [KINDS[i % 8] for i in range(8 * L)] + ["OUT"]
     return names + (["SELECT", "REORD_A", "REORD_B"] if beam else [])
 
@@ -24,8 +27,9 @@ def profile(kernel, run) -> torch.Tensor:
     """Stamps [stages, programs, 4] (start, end, barrier exit, ns waiting for ring slots) of one call of `run`."""
     lib = _lib.lib()
     n = lib.owsm_dec_plan_stages(run.plan, int(run.beam))
+    P = kernel._plan_info(run.plan)[0]
     # stage stamps [n, P, 4], then an event log of 128 stamps per CTA
-    ts = torch.zeros(n * kernel.programs * 4 + kernel.programs * 128, dtype=torch.int64, device=kernel.device)
+    ts = torch.zeros(n * P * 4 + P * 128, dtype=torch.int64, device=kernel.device)
     _lib.check(lib.owsm_dec_plan_trace(run.plan, ts.data_ptr()), "owsm_dec_plan_trace")
     try:
         run()
@@ -34,15 +38,15 @@ def profile(kernel, run) -> torch.Tensor:
         _lib.check(lib.owsm_dec_plan_trace(run.plan, None), "owsm_dec_plan_trace")
     kernel.check()
     ts = ts.cpu()
-    stages = ts[: n * kernel.programs * 4].view(n, kernel.programs, 4)
-    stages.events = ts[n * kernel.programs * 4 :].view(kernel.programs, 128)
+    stages = ts[: n * P * 4].view(n, P, 4)
+    stages.events = ts[n * P * 4 :].view(P, 128)
     return stages
 
 
 def summary(ts: torch.Tensor, L: int, beam: bool = False) -> dict[str, dict[str, float]]:
     """Per stage kind, in microseconds: span (barrier release to barrier release), work (slowest CTA's stage
     time), wait (mean barrier time), ring (the most a CTA waited for its data in the stage), count."""
-    names = stage_names(L, beam)
+    names = stage_names(L, beam, cluster=ts.shape[0] == 3 * L + 2)
     t = ts.double()
     start, end, exit_ = t[..., 0], t[..., 1], t[..., 2]
     t0 = start.min()

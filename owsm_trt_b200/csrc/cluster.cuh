@@ -315,7 +315,8 @@ __device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* x
 }
 
 // S1 (kind 1, self-attention) or S2 (kind 2, cross-attention) of a cluster that owns (head h, row group).
-template <int NT>
+// QM: compile-time bound of the queries of an attention unit (1 for one-token calls without row sharing).
+template <int NT, int QM>
 __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, const Cl& cl,
                               const int* pre, int kind, int l, uint8_t* work, uint64_t* xbar, uint32_t (&ph)[2],
                               const long long* xin, long long* xout) {
@@ -334,6 +335,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
   }
   ln_rows(pd, xin, cl.m0, Mg, NT, sm.bbuf, cx);
   csync();
+  event(cx, 51);
   const uint32_t xq_s = smem_u32(sm.xq), part_s = smem_u32(sm.part);
   uint32_t rxq[CS - 1], rpart[CS - 1], rbar0[CS - 1], rbar1[CS - 1];
 #pragma unroll
@@ -367,11 +369,13 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       }
   });
   csync();
+  event(cx, 52);
   if (!mbar_wait_cluster(&xbar[0], ph[0], pd.max_spin)) {
     ring.dead = true;
     atomicExch(pd.err, E_ERR_TIMEOUT);
   }
   ph[0] ^= 1u;
+  event(cx, 53);
   // this CTA's attention units -> their partial softmax states into every cluster CTA's table
   const AttnSmem as = carve_attn(sm.attn, pd.Qmax);
   for (int k = r; k < nunits; k += CS) {
@@ -397,8 +401,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         as.q[idx] = sm.xq[(item * Qu + q) * nq + d] * 0.125f;
       }
     }
-    if (Qu == 1) attn_unit<1>(as, ring, Qu, p0, p1, pd.apos, nnew);
-    else attn_unit<MAXQ>(as, ring, Qu, p0, p1, pd.apos, nnew);
+    attn_unit<QM>(as, ring, Qu, p0, p1, pd.apos, nnew);
     for (int idx = threadIdx.x; idx < Qu * (XPS / 4); idx += NTHR) {
       const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
       float4 v;
@@ -411,12 +414,14 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       for (int i = 0; i < CS - 1; ++i) st_async_v4(rpart[i] + off * 4, w, rbar1[i]);
     }
     csync();
+    event(cx, 54);
   }
   if (!mbar_wait_cluster(&xbar[1], ph[1], pd.max_spin)) {
     ring.dead = true;
     atomicExch(pd.err, E_ERR_TIMEOUT);
   }
   ph[1] ^= 1u;
+  event(cx, 55);
   // every token of the group: its units' parts combined in part order -> the out-projection's B operand
   for (int idx = threadIdx.x; idx < NT * 8 * (DK / 2); idx += NTHR) {
     const int m = idx / (DK / 2), dp = idx % (DK / 2);
@@ -444,6 +449,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
     *reinterpret_cast<__half2*>(&sm.obuf[bfrag_idx(m, 2 * dp, NT)]) = __floats2half2_rn(n0, n1);
   }
   csync();
+  event(cx, 56);
   // the head's slice of the out-projection: output rows (D / 4) r .. , k-blocks 4 h .. 4 h + 3
   const int nb = D / 64, per = pd.slot / 2048;
   for (int bb = 0; bb < nb; bb += per) {
@@ -476,6 +482,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
   if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar[0], (CS - 1) * my_bytes);
   ln_rows(pd, xin, 0, M, NT, sm.bbuf, cx);
   csync();
+  event(cx, 60);
   block_chunks<NT>(ring, rows / 16, D / 16, smem_u32(sm.bbuf), [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
@@ -487,6 +494,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
       }
   });
   csync();
+  event(cx, 61);
   const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;
   const uint32_t bar0 = smem_u32(&xbar[0]);
   for (int i = threadIdx.x; i < (int)(my_bytes / 16); i += NTHR) {
@@ -502,6 +510,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
     atomicExch(pd.err, E_ERR_TIMEOUT);
   }
   ph[0] ^= 1u;
+  event(cx, 63);
   const int nb = D / 64, piece = nkb3 * 512, per = pd.slot / piece;
   for (int bb = 0; bb < nb; bb += per) {
     const int n = nb - bb < per ? nb - bb : per;
@@ -524,8 +533,69 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
 
 namespace owsm {
 
-// The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output.
+// The output stage of the cluster kernel (greedy calls): final LayerNorm of the fixed-point residual,
+// this CTA's vocab blocks (the grid kernel's block schedule), logits out and the running argmax per token
+// (first index on ties; timestamp ids left out for flagged rows), merged over the warps into os.amax/aidx.
 template <int NT>
+__device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, uint8_t* work,
+                             OutState& os) {
+  const int M = pd.M, V = pd.V;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  __half* bbuf = reinterpret_cast<__half*>(work);
+  ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx);
+  csync();
+  float best[NT][2];
+  int besti[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) best[nt][0] = best[nt][1] = -INFINITY, besti[nt][0] = besti[nt][1] = 0x7fffffff;
+  const int b0 = cx.so[G_OUT];
+  block_chunks<NT>(ring, cx.so[G_OUT + 1] - b0, pd.D / 16, smem_u32(bbuf),
+                   [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
+                     const int rb = cx.sb[b0 + j];
+#pragma unroll
+                     for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                       for (int e = 0; e < 4; ++e) {
+                         const int n = rb * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
+                         if (m >= M || n >= V) continue;
+                         const float y = acc[nt][e] + bia[e >> 1];
+                         a.logits[(long long)m * V + n] = y;
+                         const float ya = (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ? -INFINITY : y;
+                         merge_best(best[nt][e & 1], besti[nt][e & 1], ya, n);
+                       }
+                   });
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best[nt][s2], o);
+        const int oi = __shfl_xor_sync(0xffffffffu, besti[nt][s2], o);
+        merge_best(best[nt][s2], besti[nt][s2], ov, oi);
+      }
+      const int m = nt * 8 + 2 * t + s2;
+      if (g == 0 && m < M) {
+        os.wamax[warp * M + m] = best[nt][s2];
+        os.waidx[warp * M + m] = besti[nt][s2];
+      }
+    }
+  csync();
+  for (int m = threadIdx.x; m < M; m += NTHR) {
+    float bv = os.amax[m];
+    int bi = os.aidx[m];
+    for (int w = 0; w < NWARP; ++w) merge_best(bv, bi, os.wamax[w * M + m], os.waidx[w * M + m]);
+    os.amax[m] = bv;
+    os.aidx[m] = bi;
+  }
+  csync();
+}
+
+// The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output.
+// Only the ring position, the exchange parities and the error flag live in registers across stages; the
+// rest of the per-CTA state is rebuilt inside each stage from shared memory and the launch parameters, which
+// keeps the register allocation of the stage code free of state it does not use.
+template <int NT, int QM>
 __global__ void __launch_bounds__(BLOCK, 1)
     decoder_cl_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -567,16 +637,16 @@ __global__ void __launch_bounds__(BLOCK, 1)
   if (threadIdx.x == 0) *nev = 0;
   __syncthreads();
   const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
-  Frames fr;  // (the output stage's GEMM helpers take it; the cluster stages do not split frames this way)
-  fr.total = (long long)pd.H * pre[pd.U];
-  fr.U = pd.U;
-  fr.H = pd.H;
-  fr.P = (int)(fr.total < pd.P ? fr.total : pd.P);
-  fr.pre = pre;
-  const Cl cl = cluster_view(pd);
 
   if (warp == NWARP) {  // producer
     if (lane == 0) {
+      Frames fr;  // (unused by the output stage's schedule; for_chunks takes one)
+      fr.total = 0;
+      fr.U = pd.U;
+      fr.H = pd.H;
+      fr.P = 1;
+      fr.pre = pre;
+      const Cl cl = cluster_view(pd);
       uint32_t i = 0;
       bool dead = false;
       auto put = [&](const void* src, uint32_t piece, int pieces, uint32_t stride, uint64_t pol) {
@@ -617,18 +687,17 @@ __global__ void __launch_bounds__(BLOCK, 1)
     return;
   }
 
-  Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
-  OutState os = carve_out(smem + pd.off_out, pd.M, false);
-  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
-    os.amax[m] = -INFINITY;
-    os.aidx[m] = 0x7fffffff;
+  if (threadIdx.x < pd.M) {  // the output stage's running argmax
+    OutState os = carve_out(smem + pd.off_out, pd.M, false);
+    os.amax[threadIdx.x] = -INFINITY;
+    os.aidx[threadIdx.x] = 0x7fffffff;
   }
-  int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
-  uint32_t ph[2] = {0u, 0u};
+  uint32_t ring_i = 0, ph[2] = {0u, 0u};
   bool dead = false;
   for (int g = 0; g < n_stages; ++g) {
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
+    Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, ring_i, pd.max_spin, pd.err, dead, 0ull, pd.ts != nullptr};
     if (g == 0) {
       cl_embed(pd, a, cx, c);
     } else if (g < n_stages - 1) {
@@ -637,24 +706,30 @@ __global__ void __launch_bounds__(BLOCK, 1)
       long long* xout = pd.xf[g % 3];
       long long* xfree = pd.xf[(g + 1) % 3];
       cl_residual(pd, kind == 1 ? G_WO : (kind == 2 ? G_WCO : G_F2), l, xin, xout, xfree, c);
+      event(cx, 50);
+      const Cl cl = cluster_view(pd);
       if (kind < 3) {
-        if (cl.cid < pd.H * pd.RG && cl.Mg > 0) cl_attn_stage<NT>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);
+        if (cl.cid < pd.H * pd.RG && cl.Mg > 0)
+          cl_attn_stage<NT, QM>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);
       } else if (cl.ffn) {
         cl_ffn_stage<NT>(pd, ring, cx, cl, work, xbar, ph, xin, xout);
       }
+      event(cx, 57);
       __threadfence();
     } else {
-      gemm_stage<NT>(pd, a, ring, cx, fr, K_OUT, 0, c, work, os);
-      csync();
+      OutState os = carve_out(smem + pd.off_out, pd.M, false);
+      int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
+      cl_out_stage<NT>(pd, a, ring, cx, work, os);
       if (a.pred) argmax_finish(pd, a, c, os, flag, work);
     }
+    ring_i = ring.i;
+    dead = ring.dead;
     if (ts && threadIdx.x == 0) ts[1] = globaltimer();
     if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead);
     if (ts && threadIdx.x == 0) {
       ts[2] = globaltimer();
       ts[3] = ring.waited;
     }
-    ring.waited = 0;
   }
   csync();
   if (threadIdx.x == 0) {

@@ -1930,9 +1930,12 @@ KernelFn kernel_for(int NT) {
   }
 }
 
-KernelFn cl_kernel_for(int NT) { return NT == 1 ? decoder_cl_kernel<1> : decoder_cl_kernel<2>; }
+KernelFn cl_kernel_for(int NT, int Qmax) {
+  if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1> : decoder_cl_kernel<2, 1>;
+  return NT == 1 ? decoder_cl_kernel<1, MAXQ> : decoder_cl_kernel<2, MAXQ>;
+}
 
-KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT) : kernel_for(pd.NT); }
+KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax) : kernel_for(pd.NT); }
 
 
 }  // namespace
@@ -2094,7 +2097,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
   // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
   if (allow_cl && !beam && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
-    KernelFn kf = cl_kernel_for(pd.NT);
+    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax);
     CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];

@@ -222,65 +222,167 @@ __device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& e
 }
 
 // ------------------------------------------------------------------------------------------------ attention
-// One attention unit on all consumer warps: Q queries (s.q, fp32 [Q][64], scaled) over the cached keys and
-// values of positions p0 .. p1 - 1 (ring chunks: keys then values, apos positions per chunk), then with
-// nnew > 0 the call's own keys/values (s.knew / s.vnew [nnew][64]; query q sees new key j <= q, Q = nnew).
-// Leaves the unnormalised output in s.out, the running max / sum in s.mrun / s.lrun.
+// Online-softmax state of one warp for up to QM queries: running max and sum (warp-uniform) and two output
+// dims per lane (2 lane, 2 lane + 1).
+template <int QM>
+struct WarpSoftmax {
+  float m[QM], l[QM], o0[QM], o1[QM];
+};
+
+// One step of 8 key positions for one warp: lane (group g = lane / 4, quarter) scores position g over the
+// 16 dims of its quarter (rotated by g, so the 8 rows of a step spread over the banks), the 4 lanes of a
+// group add up, then every lane updates the state and accumulates the 8 value rows' dims 2 lane, 2 lane + 1.
+// K / V rows: fp16 (`kh`, `vh`, 64 halves per row) or fp32 (`kf`, `vf`); n valid positions (<= 8); query q
+// sees position i of the step when causal_base < 0 or causal_base + i <= q.
+template <int QM, bool F32>
+__device__ __forceinline__ void warp_step(WarpSoftmax<QM>& st, const float* qs, int Q, const void* kp, const void* vp,
+                                          int n, int causal_base) {
+  const int lane = threadIdx.x & 31, g = lane >> 2, part = ((lane & 3) + g) & 3;
+  float kv[16];
+  if (g < n) {
+    if (F32) {
+      const float* kr = reinterpret_cast<const float*>(kp) + g * DK + part * 16;
+#pragma unroll
+      for (int i = 0; i < 16; i += 4) {
+        const float4 v = lds128f(kr + i);
+        kv[i] = v.x; kv[i + 1] = v.y; kv[i + 2] = v.z; kv[i + 3] = v.w;
+      }
+    } else {
+      const uint32_t ka = smem_u32(reinterpret_cast<const __half*>(kp) + g * DK + part * 16);
+      const uint4 k0 = lds128_u32(ka), k1 = lds128_u32(ka + 16);
+      const __half2* h0 = reinterpret_cast<const __half2*>(&k0);
+      const __half2* h1 = reinterpret_cast<const __half2*>(&k1);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f0 = __half22float2(h0[e]), f1 = __half22float2(h1[e]);
+        kv[2 * e] = f0.x; kv[2 * e + 1] = f0.y; kv[8 + 2 * e] = f1.x; kv[9 + 2 * e] = f1.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) kv[i] = 0.f;
+  }
+  // this step's value dims of the lane: rows 0 .. n - 1
+  float2 vv[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if (i < n) {
+      if (F32) vv[i] = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vp) + i * DK + 2 * lane);
+      else {
+        uint32_t raw;
+        asm volatile("ld.shared.u32 %0, [%1];" : "=r"(raw) : "r"(smem_u32(reinterpret_cast<const __half*>(vp) + i * DK + 2 * lane)));
+        vv[i] = __half22float2(*reinterpret_cast<__half2*>(&raw));
+      }
+    } else {
+      vv[i] = make_float2(0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < QM; ++q) {
+    if (q >= Q) break;
+    const float* qq = qs + q * DK + part * 16;
+    float sc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; i += 4) {
+      const float4 a = lds128f(qq + i);
+      sc += a.x * kv[i] + a.y * kv[i + 1] + a.z * kv[i + 2] + a.w * kv[i + 3];
+    }
+    sc += __shfl_xor_sync(0xffffffffu, sc, 1);
+    sc += __shfl_xor_sync(0xffffffffu, sc, 2);
+    const bool ok = g < n && (causal_base < 0 || causal_base + g <= q);
+    if (!ok) sc = -INFINITY;
+    float mx = sc;
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+    const float mnew = fmaxf(st.m[q], mx);
+    if (mnew == -INFINITY) continue;  // nothing visible yet
+    const float al = st.m[q] > -INFINITY ? expf(st.m[q] - mnew) : 0.f;
+    const float p = ok ? expf(sc - mnew) : 0.f;
+    float ps = p;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    st.l[q] = st.l[q] * al + ps;
+    float a0 = st.o0[q] * al, a1 = st.o1[q] * al;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pi = __shfl_sync(0xffffffffu, p, i * 4);
+      a0 += pi * vv[i].x;
+      a1 += pi * vv[i].y;
+    }
+    st.o0[q] = a0;
+    st.o1[q] = a1;
+    st.m[q] = mnew;
+  }
+}
+
+// One attention unit on all consumer warps, split-K inside the CTA: Q queries (s.q, fp32 [Q][64], scaled)
+// over the cached keys/values of positions p0 .. p1 - 1 (ring chunks: keys then values, apos positions per
+// chunk; warp w takes the steps of 8 positions w, w + 7, ... of each chunk and keeps its own online-softmax
+// state, so no block barrier is needed per chunk), then with nnew > 0 the call's own keys/values (s.knew /
+// s.vnew [nnew][64], fp32; query q sees new key j <= q, Q = nnew) on the warp with the least chunk work.
+// The warps' states are merged once: s.out (unnormalised), s.mrun, s.lrun per query.
 template <int QM>
 __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x < Q) {
-    s.mrun[threadIdx.x] = -INFINITY;
-    s.lrun[threadIdx.x] = 0.f;
-  }
-  AttnAcc<QM> acc;
+  WarpSoftmax<QM> st;
 #pragma unroll
-  for (int q = 0; q < QM; ++q) acc.o[q][0] = acc.o[q][1] = 0.f;
-  csync();
-  Q1Regs qr;
-  if (QM == 1) qr = q1_load(s.q);
+  for (int q = 0; q < QM; ++q) st.m[q] = -INFINITY, st.l[q] = 0.f, st.o0[q] = 0.f, st.o1[q] = 0.f;
+  csync();  // the queries (and new keys / values) are in shared memory
+  int last_steps = 0;
   for (int j0 = p0; j0 < p1; j0 += apos) {
     const int npos = p1 - j0 < apos ? p1 - j0 : apos;
-    const __half* kt = reinterpret_cast<const __half*>(ring.wait());
-    chunk_scores<QM>(s, qr, kt, npos, Q);
-    ring.release();
-    csync();
-    attn_softmax(s.sc, npos, Q, s.mrun, s.lrun, s.alpha, [](int, int) { return true; });
-    csync();
-    const __half* vt = reinterpret_cast<const __half*>(ring.wait());
-    attn_accum<QM>(acc, s.sc, s.alpha, vt, npos, Q);
-    ring.release();
-    csync();
-  }
-  if (nnew > 0) {  // the new tokens, causally: a warp per (query, key) dot product
-    for (int pr = warp; pr < Q * nnew; pr += NWARP) {
-      const int q = pr / nnew, j = pr % nnew;
-      float sum = s.q[q * DK + lane] * s.knew[j * DK + lane] + s.q[q * DK + lane + 32] * s.knew[j * DK + lane + 32];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      if (lane == 0) s.sc[q * APOS + j] = sum;
+    const __half* kt = reinterpret_cast<const __half*>(ring.wait_at(ring.i));
+    const __half* vt = reinterpret_cast<const __half*>(ring.wait_at(ring.i + 1));
+    const int nsteps = (npos + 7) >> 3;
+    for (int t = warp; t < nsteps; t += NWARP) {
+      const int n = npos - t * 8 < 8 ? npos - t * 8 : 8;
+      warp_step<QM, false>(st, s.q, Q, kt + (size_t)t * 8 * DK, vt + (size_t)t * 8 * DK, n, -1);
     }
-    csync();
-    attn_softmax(s.sc, nnew, Q, s.mrun, s.lrun, s.alpha, [](int q, int j) { return j <= q; });
-    csync();
+    last_steps = nsteps;
+    __syncwarp();
+    ring.release();  // keys
+    ring.release();  // values
+  }
+  if (nnew > 0 && warp == (last_steps % NWARP)) {  // a warp with no more chunk steps than the others
+    for (int j = 0; j < nnew; j += 8)
+      warp_step<QM, true>(st, s.q, Q, s.knew + (size_t)j * DK, s.vnew + (size_t)j * DK, nnew - j < 8 ? nnew - j : 8, j);
+  }
+  // merge the warps: per warp m, l (sc area) and its output dims (scratch)
+  float* wm = s.sc;
+  float* wl = s.sc + NWARP * QM;
 #pragma unroll
-    for (int q = 0; q < QM; ++q)
-      if (q < Q) {
-        acc.o[q][0] *= s.alpha[q];
-        acc.o[q][1] *= s.alpha[q];
-      }
-    for (int j = warp; j < nnew; j += NWARP) {
-      const float2 v = make_float2(s.vnew[j * DK + 2 * lane], s.vnew[j * DK + 2 * lane + 1]);
-#pragma unroll
-      for (int q = 0; q < QM; ++q)
-        if (q < Q) {
-          const float p = s.sc[q * APOS + j];
-          acc.o[q][0] += p * v.x;
-          acc.o[q][1] += p * v.y;
+  for (int q = 0; q < QM; ++q) {
+    if (q >= Q) break;
+    if (lane == 0) {
+      wm[warp * QM + q] = st.m[q];
+      wl[warp * QM + q] = st.l[q];
+    }
+    *reinterpret_cast<float2*>(&s.scratch[(warp * Q + q) * DK + 2 * lane]) = make_float2(st.o0[q], st.o1[q]);
+  }
+  csync();
+  for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
+    const int q = idx / DK, d = idx % DK;
+    float mx = -INFINITY;
+    for (int w = 0; w < NWARP; ++w) mx = fmaxf(mx, wm[w * QM + q]);
+    float o = 0.f, l = 0.f;
+    if (mx > -INFINITY)
+      for (int w = 0; w < NWARP; ++w) {
+        const float mw = wm[w * QM + q];
+        if (mw > -INFINITY) {
+          const float f = expf(mw - mx);
+          o += f * s.scratch[(w * Q + q) * DK + d];
+          l += f * wl[w * QM + q];
         }
+      }
+    s.out[idx] = o;
+    if (d == 0) {
+      s.mrun[q] = mx;
+      s.lrun[q] = l;
     }
   }
-  attn_reduce<QM>(acc, Q, s.scratch, s.out);
+  csync();
 }
 
 // ------------------------------------------------------------------------------------------------ stages

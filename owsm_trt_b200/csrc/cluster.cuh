@@ -693,11 +693,81 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
   csync();
 }
 
-// The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output.
+// The output stage of a beam call: final LayerNorm, this CTA's vocab blocks, logits out, and per token the
+// running max / sum of exp (log-softmax partials) and top-K over this CTA's ids, first per warp (a 16-row
+// tile at a time, as the grid kernel does), then merged over the warps into os.rmax / rsum / topv / topi.
+template <int NT>
+__device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, uint8_t* work,
+                                  OutState& os) {
+  const int M = pd.M, V = pd.V;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  __half* bbuf = reinterpret_cast<__half*>(work);
+  ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx);
+  for (int m = lane; m < M; m += 32) {
+    os.wrmax[warp * M + m] = -INFINITY;
+    os.wrsum[warp * M + m] = 0.f;
+    for (int j = 0; j < KTOP; ++j) {
+      os.wtopv[((size_t)warp * M + m) * KTOP + j] = -INFINITY;
+      os.wtopi[((size_t)warp * M + m) * KTOP + j] = 0x7fffffff;
+    }
+  }
+  csync();
+  const int b0 = cx.so[G_OUT];
+  block_chunks<NT>(ring, cx.so[G_OUT + 1] - b0, pd.D / 16, smem_u32(bbuf),
+                   [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
+                     const int rb = cx.sb[b0 + j];
+                     float* tile = os.wtile + (size_t)warp * 16 * M;
+#pragma unroll
+                     for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                       for (int e = 0; e < 4; ++e) {
+                         const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
+                         if (m >= M) continue;
+                         const float y = acc[nt][e] + bia[e >> 1];
+                         if (n < V) a.logits[(long long)m * V + n] = y;
+                         tile[row * M + m] = (n < V) ? y : -INFINITY;
+                       }
+                     __syncwarp();
+                     beam_merge_block(os, warp, lane, M, rb);
+                     __syncwarp();
+                   });
+  csync();
+  for (int m = threadIdx.x; m < M; m += NTHR) {
+    float mx = os.rmax[m];
+    for (int w = 0; w < NWARP; ++w) mx = fmaxf(mx, os.wrmax[w * M + m]);
+    float sm = (os.rmax[m] > -INFINITY) ? os.rsum[m] * expf(os.rmax[m] - mx) : 0.f;
+    for (int w = 0; w < NWARP; ++w) {
+      const float wm = os.wrmax[w * M + m];
+      if (wm > -INFINITY) sm += os.wrsum[w * M + m] * expf(wm - mx);
+    }
+    os.rmax[m] = mx;
+    os.rsum[m] = sm;
+    float* tv = os.topv + m * KTOP;
+    int* ti = os.topi + m * KTOP;
+    for (int w = 0; w < NWARP; ++w)
+      for (int e = 0; e < KTOP; ++e) {
+        const float y = os.wtopv[((size_t)w * M + m) * KTOP + e];
+        const int n = os.wtopi[((size_t)w * M + m) * KTOP + e];
+        if (!(y > tv[KTOP - 1] || (y == tv[KTOP - 1] && n < ti[KTOP - 1]))) continue;
+        int jj = KTOP - 1;
+        while (jj > 0 && (y > tv[jj - 1] || (y == tv[jj - 1] && n < ti[jj - 1]))) {
+          tv[jj] = tv[jj - 1];
+          ti[jj] = ti[jj - 1];
+          --jj;
+        }
+        tv[jj] = y;
+        ti[jj] = n;
+      }
+  }
+  csync();
+}
+
+// The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output;
+// beam calls (BEAM): 3 L + 2 select, 3 L + 3 and 3 L + 4 the two halves of the cache reorder.
 // Only the ring position, the exchange parities and the error flag live in registers across stages; the
 // rest of the per-CTA state is rebuilt inside each stage from shared memory and the launch parameters, which
 // keeps the register allocation of the stage code free of state it does not use.
-template <int NT, int QM>
+template <int NT, int QM, bool BEAM>
 __global__ void __launch_bounds__(BLOCK, 1)
     decoder_cl_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -709,7 +779,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   uint8_t* work = smem + pd.off_work;
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int L = pd.L, n_stages = 3 * L + 2;
+  const int L = pd.L, n_out = 3 * L + 1, n_stages = n_out + 1 + (BEAM ? 3 : 0);
   int* so = reinterpret_cast<int*>(smem + pd.off_sched);
   int* sb = so + NGEMM + 1;
   int* offs = reinterpret_cast<int*>(smem + pd.off_rows);
@@ -774,8 +844,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
         ++i;
       };
       const uint64_t first = policy_evict_first();
-      for (int g = 1; g < n_stages && !dead; ++g) {
-        if (g == n_stages - 1) {  // output stage: the grid kernel's block schedule
+      for (int g = 1; g <= n_out && !dead; ++g) {
+        if (g == n_out) {  // output stage: the grid kernel's block schedule
           for_chunks(pd, a, fr, cx, 8 * L + 1, c, [&](const void* src, uint32_t bytes) { put(src, bytes, 1, 0u, first); });
         } else {
           const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;
@@ -789,10 +859,16 @@ __global__ void __launch_bounds__(BLOCK, 1)
     return;
   }
 
-  if (threadIdx.x < pd.M) {  // the output stage's running argmax
-    OutState os = carve_out(smem + pd.off_out, pd.M, false);
+  if (threadIdx.x < pd.M) {  // the output stage's running argmax / log-softmax partials and top-K
+    OutState os = carve_out(smem + pd.off_out, pd.M, BEAM);
     os.amax[threadIdx.x] = -INFINITY;
     os.aidx[threadIdx.x] = 0x7fffffff;
+    os.rmax[threadIdx.x] = -INFINITY;
+    os.rsum[threadIdx.x] = 0.f;
+    for (int j = 0; j < KTOP; ++j) {
+      os.topv[threadIdx.x * KTOP + j] = -INFINITY;
+      os.topi[threadIdx.x * KTOP + j] = 0x7fffffff;
+    }
   }
   uint32_t ring_i = 0, ph[2] = {0u, 0u};
   bool dead = false;
@@ -802,7 +878,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
     Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, ring_i, pd.max_spin, pd.err, dead, 0ull, pd.ts != nullptr};
     if (g == 0) {
       cl_embed(pd, a, cx, c);
-    } else if (g < n_stages - 1) {
+    } else if (g < n_out) {
       const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;
       const long long* xin = pd.xf[(g - 1) % 3];
       long long* xout = pd.xf[g % 3];
@@ -818,11 +894,19 @@ __global__ void __launch_bounds__(BLOCK, 1)
       }
       event(cx, 57);
       __threadfence();
-    } else {
-      OutState os = carve_out(smem + pd.off_out, pd.M, false);
-      int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
-      cl_out_stage<NT>(pd, a, ring, cx, work, os);
-      if (a.pred) argmax_finish(pd, a, c, os, flag, work);
+    } else if (g == n_out) {
+      OutState os = carve_out(smem + pd.off_out, pd.M, BEAM);
+      if (BEAM) {
+        cl_out_stage_beam<NT>(pd, a, ring, cx, work, os);
+        beam_partials(pd, c, os);
+      } else {
+        int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
+        cl_out_stage<NT>(pd, a, ring, cx, work, os);
+        if (a.pred) argmax_finish(pd, a, c, os, flag, work);
+      }
+    } else if (BEAM) {
+      if (g == n_out + 1) select_stage(pd, a, c, work);
+      else reorder_stage(pd, a, cx, c, g == n_out + 2);
     }
     ring_i = ring.i;
     dead = ring.dead;

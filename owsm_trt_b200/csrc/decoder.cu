@@ -1930,12 +1930,13 @@ KernelFn kernel_for(int NT) {
   }
 }
 
-KernelFn cl_kernel_for(int NT, int Qmax) {
-  if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1> : decoder_cl_kernel<2, 1>;
-  return NT == 1 ? decoder_cl_kernel<1, MAXQ> : decoder_cl_kernel<2, MAXQ>;
+KernelFn cl_kernel_for(int NT, int Qmax, bool beam) {
+  if (beam) return NT == 1 ? decoder_cl_kernel<1, MAXQ, true> : decoder_cl_kernel<2, MAXQ, true>;
+  if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false> : decoder_cl_kernel<2, 1, false>;
+  return NT == 1 ? decoder_cl_kernel<1, MAXQ, false> : decoder_cl_kernel<2, MAXQ, false>;
 }
 
-KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax) : kernel_for(pd.NT); }
+KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax, pd.beam > 0) : kernel_for(pd.NT); }
 
 
 }  // namespace
@@ -2096,8 +2097,8 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   // The cluster kernel: greedy calls of up to 16 tokens. Clusters of 4 CTAs, as many as fit one per SM;
   // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
   // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
-  if (allow_cl && !beam && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
-    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax);
+  if (allow_cl && (!beam || pd.Qmax > 1) && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
+    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax, beam > 0);
     CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
@@ -2217,6 +2218,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   if (pd.cl) {  // stage buffers of the cluster kernel; its output stage as the grid kernel's; 32 KB slots
     work = std::max(cl_work_bytes(NT, D, pd.Qmax), (size_t)NT * (D / 16) * 256 + 16);
     work = std::max(work, sizeof(float) * 2 * (size_t)pd.P * M);
+    if (beam) work = std::max(work, select_smem(beam, pd.P));
     if (slots_left(work, SLOT) < 2) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small for the cluster kernel"));
   } else if (slots_left(work, SLOT) < 4) {
     const size_t w16 = work_for(SLOT / 2);
@@ -2371,7 +2373,7 @@ int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps) {
 
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
-  return p->pd.cl ? 3 * p->pd.L + 2 : 8 * p->pd.L + 2 + (beam_call ? 3 : 0);
+  return (p->pd.cl ? 3 * p->pd.L + 2 : 8 * p->pd.L + 2) + (beam_call ? 3 : 0);
 }
 
 int owsm_dec_set_path(OwsmDec* h, int path) {

@@ -18,8 +18,9 @@ KINDS = ["QKV", "SATT", "WO", "CQ", "XATT", "WCO", "F1", "F2"]
 def stage_names(L: int, beam: bool, cluster: bool = False) -> list[str]:
     """Stage names of a call: the grid-stage kernel's eight per layer, or the cluster kernel's three."""
     if cluster:
-        return ["EMBED"] + [("S1", "S2", "S3")[i % 3] for i in range(3 * L)] + ["OUT"]
-    names = ["EMBED"] + [KINDS[i % 8] for i in range(8 * L)] + ["OUT"]
+        names = ["EMBED"] + [("S1", "S2", "S3")[i % 3] for i in range(3 * L)] + ["OUT"]
+    else:
+        names = ["EMBED"] + [KINDS[i % 8] for i in range(8 * L)] + ["OUT"]
     return names + (["SELECT", "REORD_A", "REORD_B"] if beam else [])
 
 
@@ -46,7 +47,7 @@ def profile(kernel, run) -> torch.Tensor:
 def summary(ts: torch.Tensor, L: int, beam: bool = False) -> dict[str, dict[str, float]]:
     """Per stage kind, in microseconds: span (barrier release to barrier release), work (slowest CTA's stage
     time), wait (mean barrier time), ring (the most a CTA waited for its data in the stage), count."""
-    names = stage_names(L, beam, cluster=ts.shape[0] == 3 * L + 2)
+    names = stage_names(L, beam, cluster=ts.shape[0] == 3 * L + 2 + (3 if beam else 0))
     t = ts.double()
     start, end, exit_ = t[..., 0], t[..., 1], t[..., 2]
     t0 = start.min()

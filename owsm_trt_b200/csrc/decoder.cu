@@ -25,6 +25,7 @@
 #include <cmath>
 #include <cstdio>
 #include <atomic>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -1810,6 +1811,11 @@ struct OwsmDec {
   int* err = nullptr;  // device error word
   uint32_t max_spin = DEFAULT_SPIN;
   int path = 0;  // 0: cluster kernel where it applies, 1: always the grid-stage kernel, 2: cluster kernel or fail
+  // Profiling aid: with OWSM_DEC_NO_COOP set when the handle is made, cluster-kernel calls are launched
+  // without the cooperative attribute (the profiler rejects cooperative cluster launches). The grid-wide
+  // barrier then relies on all CTAs being resident, which holds when the call runs alone (one CTA per SM,
+  // at most the resident cluster count); if they were not, its bounded waits report a timeout.
+  bool coop = std::getenv("OWSM_DEC_NO_COOP") == nullptr;
   ~OwsmDec() {
     int cur = 0;
     cudaGetDevice(&cur);
@@ -1930,9 +1936,12 @@ KernelFn kernel_for(int NT) {
   }
 }
 
+// One instantiation per (token tiles, bound on the queries of an attention unit, beam): the per-query state
+// of the attention code lives in registers, so a tighter bound leaves more registers to the rest.
 KernelFn cl_kernel_for(int NT, int Qmax, bool beam) {
-  if (beam) return NT == 1 ? decoder_cl_kernel<1, MAXQ, true> : decoder_cl_kernel<2, MAXQ, true>;
+  if (beam) return NT == 1 ? decoder_cl_kernel<1, 8, true> : decoder_cl_kernel<2, 8, true>;  // beam <= 8
   if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false> : decoder_cl_kernel<2, 1, false>;
+  if (Qmax <= 8) return NT == 1 ? decoder_cl_kernel<1, 8, false> : decoder_cl_kernel<2, 8, false>;
   return NT == 1 ? decoder_cl_kernel<1, MAXQ, false> : decoder_cl_kernel<2, MAXQ, false>;
 }
 
@@ -2281,8 +2290,8 @@ static int launch(OwsmDecPlan* p, void* stream, const CallArgs& a) {
   cfg.blockDim = dim3(BLOCK);
   cfg.dynamicSmemBytes = p->smem;
   cfg.stream = reinterpret_cast<cudaStream_t>(stream);
-  cfg.attrs = attr;
-  cfg.numAttrs = p->pd.cl ? 2 : 1;
+  cfg.attrs = p->pd.cl && !p->h->coop ? attr + 1 : attr;
+  cfg.numAttrs = p->pd.cl ? (p->h->coop ? 2 : 1) : 1;
   CUDA_TRY(cudaLaunchKernelEx(&cfg, plan_kernel(p->pd), p->pd, a));
   return OWSM_DEC_OK;
 }

@@ -71,3 +71,48 @@ def summary(ts: torch.Tensor, L: int, beam: bool = False) -> dict[str, dict[str,
             d[k] = round(d[k] / d["count"], 3)
     out["_total_us"] = {"count": 1, "span_us": round(float(end[-1].max() - t0) / 1e3, 2), "work_us": 0.0, "wait_us": 0.0}
     return out
+
+
+def main() -> None:
+    """``python -m owsm_trt_b200.trace [--batch B] [--path 0|1]``: the stage table of one greedy call of the
+    1B-shaped decoder (seeded weights, the benchmark's synthetic encoder lengths, cache position 100)."""
+    import argparse
+    import json
+    import sys
+    from pathlib import Path
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--path", type=int, default=0, help="0: cluster kernel where it applies, 1: grid-stage kernel")
+    args = ap.parse_args()
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
+    import bench
+    from .decoder import B200Decoder
+    from .synthetic import MEDIUM_1B, decoder_state_dict
+
+    d, dev, B = MEDIUM_1B, torch.device("cuda", 0), args.batch
+    sd = decoder_state_dict(d, 0, False)
+    k = B200Decoder.from_state_dict(sd, d.H, dev)
+    k.set_path(args.path)
+    ck, cv, enc_len, prefix, kc, vc = bench.make_workload(d, sd, dev, B, 5)
+    tok = prefix[:, -1:].to(dev).contiguous()
+    off = torch.full((B,), 100, dtype=torch.long, device=dev)
+    logits = torch.zeros(B, 1, d.V, device=dev)
+    new_kv = torch.zeros(d.L, 2, B, d.H, 1, d.dk, device=dev, dtype=torch.float16)
+    run = k.step_fn(tok, off, kc, vc, ck, cv, logits, new_kv, pred=tok, enc_len=enc_len.to(dev))
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        run()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    s = summary(profile(k, run), d.L)
+    print(json.dumps({"kernel": k.plan_kernel(run), "batch": B, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
+                      "stages": s}, indent=1))  # fmt: skip
+
+
+if __name__ == "__main__":
+    main()

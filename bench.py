@@ -64,8 +64,8 @@ def peaks() -> tuple[float, str]:
 
 def profiled_traffic(batch: int) -> int | None:
     """DRAM bytes (read + write) of one decoder launch of this workload, from the committed ncu summary of
-    the same command (profiles/decoder_kernel_b16_full.md); None for other batch sizes or if absent."""
-    p = Path(__file__).resolve().parent / "profiles" / "decoder_kernel_b16_full.md"
+    the same command (profiles/decoder_cl_kernel_b16_full.md); None for other batch sizes or if absent."""
+    p = Path(__file__).resolve().parent / "profiles" / "decoder_cl_kernel_b16_full.md"
     if batch != BATCH or not p.exists():
         return None
     m = re.search(r"^traffic_bytes_per_launch:\s*(\d+)", p.read_text(), re.M)

@@ -25,6 +25,7 @@
 namespace owsm {
 
 constexpr int CS = 4;          // CTAs per cluster
+constexpr float kLog2e = 1.4426950408889634f;  // log2(e): the wide attention steps work in the log2 domain
 constexpr int XQ_FLOATS = 16 * 3 * DK;  // exchange buffer: q/k/v rows of up to 16 tokens (fp32)
 constexpr int PART_ENTRIES = 64;        // partial softmax states of one stage (units x queries)
 
@@ -317,37 +318,153 @@ __device__ __forceinline__ void warp_step(WarpSoftmax<QM>& st, const float* qs, 
   }
 }
 
+// One step of up to 32 key positions for one warp, for long position ranges: lane i holds the whole key
+// row of position i (64 dims in 32 half2 registers, its 16-byte pieces rotated by the lane so the 32 rows
+// spread over the banks) and scores it against each query in the log2 domain; the warp's max and sum run
+// over shuffles; the probabilities go through the warp's 32-float buffer, and lane l adds up output dims
+// 2 l, 2 l + 1 over the step's value rows, 8 rows per round. Same visibility rule as warp_step.
+template <int QM, bool F32>
+__device__ __forceinline__ void warp_step32(WarpSoftmax<QM>& st, const float* qs, int Q, const void* kp, const void* vp,
+                                            int n, int causal_base, float* pbuf) {
+  const int lane = threadIdx.x & 31;
+  uint32_t kr[32];
+  if (lane < n) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int pc = (c + lane) & 7;
+      if (F32) {
+        const float* kf = reinterpret_cast<const float*>(kp) + lane * DK + pc * 8;
+        const float4 u = lds128f(kf), w = lds128f(kf + 4);
+        kr[4 * c] = pack_half2(u.x, u.y); kr[4 * c + 1] = pack_half2(u.z, u.w);
+        kr[4 * c + 2] = pack_half2(w.x, w.y); kr[4 * c + 3] = pack_half2(w.z, w.w);
+      } else {
+        const uint4 u = lds128_u32(smem_u32(reinterpret_cast<const __half*>(kp) + lane * DK + pc * 8));
+        kr[4 * c] = u.x; kr[4 * c + 1] = u.y; kr[4 * c + 2] = u.z; kr[4 * c + 3] = u.w;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) kr[i] = 0u;
+  }
+#pragma unroll
+  for (int q = 0; q < QM; ++q) {
+    if (q >= Q) break;
+    const float* qq = qs + q * DK;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int pc = (c + lane) & 7;
+      const float4 a = lds128f(qq + pc * 8), b = lds128f(qq + pc * 8 + 4);
+      const float2 k0 = unpack_half2(kr[4 * c]), k1 = unpack_half2(kr[4 * c + 1]);
+      const float2 k2 = unpack_half2(kr[4 * c + 2]), k3 = unpack_half2(kr[4 * c + 3]);
+      s0 = fmaf(a.x, k0.x, fmaf(a.y, k0.y, s0));
+      s1 = fmaf(a.z, k1.x, fmaf(a.w, k1.y, s1));
+      s2 = fmaf(b.x, k2.x, fmaf(b.y, k2.y, s2));
+      s3 = fmaf(b.z, k3.x, fmaf(b.w, k3.y, s3));
+    }
+    const bool ok = lane < n && (causal_base < 0 || causal_base + lane <= q);
+    const float sc = ok ? ((s0 + s1) + (s2 + s3)) * kLog2e : -INFINITY;  // log2 domain
+    float mx = sc;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mnew = fmaxf(st.m[q], mx);
+    if (mnew == -INFINITY) continue;
+    const float al = st.m[q] > -INFINITY ? exp2f(st.m[q] - mnew) : 0.f;
+    const float p = ok ? exp2f(sc - mnew) : 0.f;
+    float ps = p;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    st.l[q] = st.l[q] * al + ps;
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(smem_u32(pbuf + lane)), "f"(p) : "memory");
+    __syncwarp();
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+    {
+      // 8 value rows per round, loads issued together; rows past n have p = 0 and are not read
+#pragma unroll 1
+      for (int i0 = 0; i0 < n; i0 += 8) {
+        float pv[8];
+        float2 vv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int i = i0 + e;
+          pv[e] = i < n ? lds32f(pbuf + i) : 0.f;
+          if (F32) {
+            vv[e] = i < n ? *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vp) + i * DK + 2 * lane) : make_float2(0.f, 0.f);
+          } else {
+            uint32_t r0 = 0u;
+            if (i < n) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r0) : "r"(smem_u32(reinterpret_cast<const __half*>(vp) + i * DK + 2 * lane)));
+            vv[e] = unpack_half2(r0);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) {
+          a0 = fmaf(pv[e], vv[e].x, a0); a1 = fmaf(pv[e], vv[e].y, a1);
+          b0 = fmaf(pv[e + 1], vv[e + 1].x, b0); b1 = fmaf(pv[e + 1], vv[e + 1].y, b1);
+        }
+      }
+    }
+    __syncwarp();
+    st.o0[q] = st.o0[q] * al + (a0 + b0);
+    st.o1[q] = st.o1[q] * al + (a1 + b1);
+    st.m[q] = mnew;
+  }
+}
+
+
 // One attention unit on all consumer warps, split-K inside the CTA: Q queries (s.q, fp32 [Q][64], scaled)
 // over the cached keys/values of positions p0 .. p1 - 1 (ring chunks: keys then values, apos positions per
 // chunk; warp w takes the steps of 8 positions w, w + 7, ... of each chunk and keeps its own online-softmax
 // state, so no block barrier is needed per chunk), then with nnew > 0 the call's own keys/values (s.knew /
 // s.vnew [nnew][64], fp32; query q sees new key j <= q, Q = nnew) on the warp with the least chunk work.
 // The warps' states are merged once: s.out (unnormalised), s.mrun, s.lrun per query.
-template <int QM>
+template <int QM, bool WIDE>
 __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // long ranges of one query: steps of 32 positions (log2 domain); otherwise steps of 8 (the wide step's
+  // registers would crowd the per-query state of several queries)
+  const bool wide = WIDE && QM == 1 && p1 - p0 >= 256;
   WarpSoftmax<QM> st;
 #pragma unroll
   for (int q = 0; q < QM; ++q) st.m[q] = -INFINITY, st.l[q] = 0.f, st.o0[q] = 0.f, st.o1[q] = 0.f;
+  float* pbuf = s.sc + 2 * NWARP * QM + warp * 32;  // this warp's probabilities of a wide step
   csync();  // the queries (and new keys / values) are in shared memory
   int last_steps = 0;
   for (int j0 = p0; j0 < p1; j0 += apos) {
     const int npos = p1 - j0 < apos ? p1 - j0 : apos;
     const __half* kt = reinterpret_cast<const __half*>(ring.wait_at(ring.i));
     const __half* vt = reinterpret_cast<const __half*>(ring.wait_at(ring.i + 1));
-    const int nsteps = (npos + 7) >> 3;
-    for (int t = warp; t < nsteps; t += NWARP) {
-      const int n = npos - t * 8 < 8 ? npos - t * 8 : 8;
-      warp_step<QM, false>(st, s.q, Q, kt + (size_t)t * 8 * DK, vt + (size_t)t * 8 * DK, n, -1);
+    if constexpr (WIDE && QM == 1) {
+      if (wide) {
+      // steps numbered across the whole unit (chunks hold whole steps), so the warps stay balanced when a
+      // chunk's step count is not a multiple of the warp count
+      const int nsteps = (npos + 31) >> 5, sbase = (j0 - p0) >> 5;
+      for (int t = (warp - sbase % NWARP + NWARP) % NWARP; t < nsteps; t += NWARP) {
+        const int n = npos - t * 32 < 32 ? npos - t * 32 : 32;
+        warp_step32<QM, false>(st, s.q, Q, kt + (size_t)t * 32 * DK, vt + (size_t)t * 32 * DK, n, -1, pbuf);
+      }
+      last_steps = sbase + nsteps;
+      }
     }
-    last_steps = nsteps;
+    if (!wide) {
+      const int nsteps = (npos + 7) >> 3;
+      for (int t = warp; t < nsteps; t += NWARP) {
+        const int n = npos - t * 8 < 8 ? npos - t * 8 : 8;
+        warp_step<QM, false>(st, s.q, Q, kt + (size_t)t * 8 * DK, vt + (size_t)t * 8 * DK, n, -1);
+      }
+      last_steps = nsteps;
+    }
     __syncwarp();
     ring.release();  // keys
     ring.release();  // values
   }
   if (nnew > 0 && warp == (last_steps % NWARP)) {  // a warp with no more chunk steps than the others
-    for (int j = 0; j < nnew; j += 8)
-      warp_step<QM, true>(st, s.q, Q, s.knew + (size_t)j * DK, s.vnew + (size_t)j * DK, nnew - j < 8 ? nnew - j : 8, j);
+    if constexpr (WIDE && QM == 1) {
+      if (wide) warp_step32<QM, true>(st, s.q, Q, s.knew, s.vnew, nnew, 0, pbuf);  // nnew <= 16
+    }
+    if (!wide) {
+      for (int j = 0; j < nnew; j += 8)
+        warp_step<QM, true>(st, s.q, Q, s.knew + (size_t)j * DK, s.vnew + (size_t)j * DK, nnew - j < 8 ? nnew - j : 8, j);
+    }
   }
   // merge the warps: per warp m, l (sc area) and its output dims (scratch)
   float* wm = s.sc;
@@ -371,14 +488,14 @@ __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, 
       for (int w = 0; w < NWARP; ++w) {
         const float mw = wm[w * QM + q];
         if (mw > -INFINITY) {
-          const float f = expf(mw - mx);
+          const float f = wide ? exp2f(mw - mx) : expf(mw - mx);
           o += f * s.scratch[(w * Q + q) * DK + d];
           l += f * wl[w * QM + q];
         }
       }
     s.out[idx] = o;
     if (d == 0) {
-      s.mrun[q] = mx;
+      s.mrun[q] = wide ? mx / kLog2e : mx;  // the partial's max in natural-log units
       s.lrun[q] = l;
     }
   }
@@ -418,7 +535,7 @@ __device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* x
 
 // S1 (kind 1, self-attention) or S2 (kind 2, cross-attention) of a cluster that owns (head h, row group).
 // QM: compile-time bound of the queries of an attention unit (1 for one-token calls without row sharing).
-template <int NT, int QM>
+template <int NT, int QM, bool WIDE>
 __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, const Cl& cl,
                               const int* pre, int kind, int l, uint8_t* work, uint64_t* xbar, uint32_t (&ph)[2],
                               const long long* xin, long long* xout) {
@@ -439,15 +556,9 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
   csync();
   event(cx, 51);
   const uint32_t xq_s = smem_u32(sm.xq), part_s = smem_u32(sm.part);
-  uint32_t rxq[CS - 1], rpart[CS - 1], rbar0[CS - 1], rbar1[CS - 1];
-#pragma unroll
-  for (int i = 0; i < CS - 1; ++i) {
-    const uint32_t dst = (uint32_t)((r + 1 + i) % CS);
-    rxq[i] = mapa_shared(xq_s, dst);
-    rpart[i] = mapa_shared(part_s, dst);
-    rbar0[i] = mapa_shared(smem_u32(&xbar[0]), dst);
-    rbar1[i] = mapa_shared(smem_u32(&xbar[1]), dst);
-  }
+  const uint32_t bar0_s = smem_u32(&xbar[0]), bar1_s = smem_u32(&xbar[1]);
+  // (the other CTAs' addresses are mapped where they are used: keeping them live through the stage costs
+  // registers the attention code needs)
   // the head's projection rows of this CTA -> every cluster CTA's exchange buffer (and the cache)
   block_chunks<NT>(ring, my / 16, D / 16, smem_u32(sm.bbuf), [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
 #pragma unroll
@@ -461,7 +572,10 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         const int idx = m * nq + row;
         sm.xq[idx] = y;
 #pragma unroll
-        for (int i = 0; i < CS - 1; ++i) st_async_b32(rxq[i] + idx * 4, __float_as_uint(y), rbar0[i]);
+        for (int i = 1; i < CS; ++i) {
+          const uint32_t dst = (uint32_t)((r + i) % CS);
+          st_async_b32(mapa_shared(xq_s + idx * 4, dst), __float_as_uint(y), mapa_shared(bar0_s, dst));
+        }
         if (kind == 1 && row >= DK) {  // new key / value: the cache slot and new_kv
           const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
           const long long cslot = ((((long long)l * pd.R + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
@@ -503,7 +617,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         as.q[idx] = sm.xq[(item * Qu + q) * nq + d] * 0.125f;
       }
     }
-    attn_unit<QM>(as, ring, Qu, p0, p1, pd.apos, nnew);
+    attn_unit<QM, WIDE>(as, ring, Qu, p0, p1, pd.apos, nnew);
     for (int idx = threadIdx.x; idx < Qu * (XPS / 4); idx += NTHR) {
       const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
       float4 v;
@@ -513,7 +627,10 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       sts128f(&sm.part[off], v);
       const uint4 w = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
 #pragma unroll
-      for (int i = 0; i < CS - 1; ++i) st_async_v4(rpart[i] + off * 4, w, rbar1[i]);
+      for (int i = 1; i < CS; ++i) {
+        const uint32_t dst = (uint32_t)((r + i) % CS);
+        st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
+      }
     }
     csync();
     event(cx, 54);
@@ -763,11 +880,12 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
 }
 
 // The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output;
-// beam calls (BEAM): 3 L + 2 select, 3 L + 3 and 3 L + 4 the two halves of the cache reorder.
+// beam calls (BEAM): 3 L + 2 select, 3 L + 3 and 3 L + 4 the two halves of the cache reorder. WIDE:
+// one-query attention units of at least 256 positions take steps of 32 positions.
 // Only the ring position, the exchange parities and the error flag live in registers across stages; the
 // rest of the per-CTA state is rebuilt inside each stage from shared memory and the launch parameters, which
 // keeps the register allocation of the stage code free of state it does not use.
-template <int NT, int QM, bool BEAM>
+template <int NT, int QM, bool BEAM, bool WIDE>
 __global__ void __launch_bounds__(BLOCK, 1)
     decoder_cl_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -888,7 +1006,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       const Cl cl = cluster_view(pd);
       if (kind < 3) {
         if (cl.cid < pd.H * pd.RG && cl.Mg > 0)
-          cl_attn_stage<NT, QM>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);
+          cl_attn_stage<NT, QM, WIDE>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);
       } else if (cl.ffn) {
         cl_ffn_stage<NT>(pd, ring, cx, cl, work, xbar, ph, xin, xout);
       }

@@ -99,6 +99,7 @@ struct PlanDev {
   const long long* xfix;    // cluster kernel: the fixed-point residual stream the output stage normalises
   int cl;                   // 1: the cluster kernel runs this plan
   int RG, NCL3, F3;         // cluster kernel: row groups per head, clusters of the FFN stage, hidden units each
+  int wide;                 // cluster kernel: one-query attention units of >= 256 positions take steps of 32
   long long* xf[3];         // cluster kernel: rotating fixed-point residual buffers [M][D]
 };
 
@@ -1938,14 +1939,17 @@ KernelFn kernel_for(int NT) {
 
 // One instantiation per (token tiles, bound on the queries of an attention unit, beam): the per-query state
 // of the attention code lives in registers, so a tighter bound leaves more registers to the rest.
-KernelFn cl_kernel_for(int NT, int Qmax, bool beam) {
-  if (beam) return NT == 1 ? decoder_cl_kernel<1, 8, true> : decoder_cl_kernel<2, 8, true>;  // beam <= 8
-  if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false> : decoder_cl_kernel<2, 1, false>;
-  if (Qmax <= 8) return NT == 1 ? decoder_cl_kernel<1, 8, false> : decoder_cl_kernel<2, 8, false>;
-  return NT == 1 ? decoder_cl_kernel<1, MAXQ, false> : decoder_cl_kernel<2, MAXQ, false>;
+KernelFn cl_kernel_for(int NT, int Qmax, bool beam, bool wide) {
+  if (beam) return NT == 1 ? decoder_cl_kernel<1, 8, true, false> : decoder_cl_kernel<2, 8, true, false>;  // beam <= 8
+  if (Qmax == 1 && wide) return NT == 1 ? decoder_cl_kernel<1, 1, false, true> : decoder_cl_kernel<2, 1, false, true>;
+  if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false, false> : decoder_cl_kernel<2, 1, false, false>;
+  if (Qmax <= 8) return NT == 1 ? decoder_cl_kernel<1, 8, false, false> : decoder_cl_kernel<2, 8, false, false>;
+  return NT == 1 ? decoder_cl_kernel<1, MAXQ, false, false> : decoder_cl_kernel<2, MAXQ, false, false>;
 }
 
-KernelFn plan_kernel(const PlanDev& pd) { return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax, pd.beam > 0) : kernel_for(pd.NT); }
+KernelFn plan_kernel(const PlanDev& pd) {
+  return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax, pd.beam > 0, pd.wide != 0) : kernel_for(pd.NT);
+}
 
 
 }  // namespace
@@ -2107,7 +2111,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
   // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
   if (allow_cl && (!beam || pd.Qmax > 1) && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
-    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax, beam > 0);
+    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax, beam > 0, false);
     CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
@@ -2132,6 +2136,9 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
       pd.RG = std::max(1, std::min(ncl / d.H, U));
       pd.NCL3 = ncl3;
       pd.F3 = d.F / ncl3;
+      // one-query calls whose cross-attention units reach 256 frames: the kernel with wide attention steps
+      const int ngm = (U + pd.RG - 1) / pd.RG, parts = ngm >= CS ? 1 : CS / ngm;
+      pd.wide = pd.Qmax == 1 && T / parts >= 256;
     }
   }
   if (allow_cl && h->path == 2 && !pd.cl) return bail(fail(OWSM_DEC_ERR_LIMIT, "the cluster kernel does not take this call"));

@@ -235,7 +235,11 @@ __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * 4294967296.0f); }
-__device__ __forceinline__ float from_fix(long long v) { return __ll2float_rn(v) * 2.3283064365386963e-10f; }
+// (high word as a 32-bit integer plus the low word scaled: two fast 32-bit conversions rather than one
+// 64-bit one, which is much slower; same value to within a rounding of the low word's contribution)
+__device__ __forceinline__ float from_fix(long long v) {
+  return (float)(int)(v >> 32) + (float)(unsigned)(v & 0xffffffffll) * 2.3283064365386963e-10f;
+}
 
 // 16-byte asynchronous global -> shared copy through L2 only (data other CTAs wrote this call).
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {

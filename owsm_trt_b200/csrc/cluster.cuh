@@ -131,7 +131,7 @@ __device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, co
       const int parts = unit_parts(cl.Rg);
       for (int k = r; k < cl.Rg * parts; k += CS) {
         const int b = cl.b0 + k / parts, p = k % parts, off = offs[b];
-        const long long base = (((long long)l * pd.R + b) * H + h) * pd.C * DK;
+        const long long base = (((long long)l * pd.Rs + b) * H + h) * pd.C * DK;
         kv_chunks(pd, a.kc + base, a.vc + base, off * p / parts, off * (p + 1) / parts, fn);
       }
       kslices(G_WO, r * (D / 64), D / 64, 4 * h, 4);
@@ -140,7 +140,7 @@ __device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, co
       const int ng = cl.u1 - cl.u0, parts = unit_parts(ng);
       for (int k = r; k < ng * parts; k += CS) {
         const int u = cl.u0 + k / parts, p = k % parts, len = pre[u + 1] - pre[u];
-        const long long base = (((long long)l * pd.U + u) * H + h) * (long long)pd.T * DK;
+        const long long base = (((long long)l * pd.Us + u) * H + h) * (long long)pd.T * DK;
         kv_chunks(pd, a.ck + base, a.cv + base, len * p / parts, len * (p + 1) / parts, fn);
       }
       kslices(G_WCO, r * (D / 64), D / 64, 4 * h, 4);
@@ -162,32 +162,56 @@ namespace owsm {
 
 // ------------------------------------------------------------------------------------------------ GEMM cores
 // One 16-row block (A fragments at `ash` + lane * 16, nkb k-blocks, nkb even) times the B operand at `bsh`.
+// The dependent mma chain, not the loads, sets a block's time, so the k-blocks go round four accumulator
+// chains when nkb is a multiple of 4 (two otherwise).
 template <int NT>
 __device__ __forceinline__ void block_mma(uint32_t ash, int nkb, uint32_t bsh, float (&acc)[NT][4]) {
   const int lane = threadIdx.x & 31;
-  float acc1[NT][4];
+  float a1[NT][4], a2[NT][4], a3[NT][4];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] = acc1[nt][e] = 0.f;
+    for (int e = 0; e < 4; ++e) acc[nt][e] = a1[nt][e] = a2[nt][e] = a3[nt][e] = 0.f;
   uint32_t bp = bsh + lane * 8;
-#pragma unroll 2
-  for (int kb = 0; kb < nkb; kb += 2) {
-    const uint4 a0 = lds128_u32(ash + kb * 512);
-    const uint4 a1 = lds128_u32(ash + (kb + 1) * 512);
+  if ((nkb & 3) == 0) {
+#pragma unroll 1
+    for (int kb = 0; kb < nkb; kb += 4) {
+      const uint4 x0 = lds128_u32(ash + kb * 512);
+      const uint4 x1 = lds128_u32(ash + (kb + 1) * 512);
+      const uint4 x2 = lds128_u32(ash + (kb + 2) * 512);
+      const uint4 x3 = lds128_u32(ash + (kb + 3) * 512);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-      const uint2 b0 = lds64_u32(bp + nt * 256);
-      const uint2 b1 = lds64_u32(bp + (NT + nt) * 256);
-      mma16816(acc[nt], a0, b0.x, b0.y);
-      mma16816(acc1[nt], a1, b1.x, b1.y);
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 b0 = lds64_u32(bp + nt * 256);
+        const uint2 b1 = lds64_u32(bp + (NT + nt) * 256);
+        const uint2 b2 = lds64_u32(bp + (2 * NT + nt) * 256);
+        const uint2 b3 = lds64_u32(bp + (3 * NT + nt) * 256);
+        mma16816(acc[nt], x0, b0.x, b0.y);
+        mma16816(a1[nt], x1, b1.x, b1.y);
+        mma16816(a2[nt], x2, b2.x, b2.y);
+        mma16816(a3[nt], x3, b3.x, b3.y);
+      }
+      bp += 4 * NT * 256;
     }
-    bp += 2 * NT * 256;
+  } else {
+#pragma unroll 2
+    for (int kb = 0; kb < nkb; kb += 2) {
+      const uint4 x0 = lds128_u32(ash + kb * 512);
+      const uint4 x1 = lds128_u32(ash + (kb + 1) * 512);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const uint2 b0 = lds64_u32(bp + nt * 256);
+        const uint2 b1 = lds64_u32(bp + (NT + nt) * 256);
+        mma16816(acc[nt], x0, b0.x, b0.y);
+        mma16816(a1[nt], x1, b1.x, b1.y);
+      }
+      bp += 2 * NT * 256;
+    }
   }
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[nt][e] += acc1[nt][e];
+    for (int e = 0; e < 4; ++e) acc[nt][e] += (a1[nt][e] + a2[nt][e]) + a3[nt][e];
 }
 
 // All consumer warps on one ring chunk of `nblk` blocks (block i at abase + i * astride): warp w takes
@@ -578,9 +602,9 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         }
         if (kind == 1 && row >= DK) {  // new key / value: the cache slot and new_kv
           const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
-          const long long cslot = ((((long long)l * pd.R + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
+          const long long cslot = ((((long long)l * pd.Rs + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
           (kv ? a.vc : a.kc)[cslot] = yh;
-          a.new_kv[((((long long)(l * 2 + kv) * pd.R + b) * H + h) * S + s) * DK + d] = yh;
+          a.new_kv[((((long long)(l * 2 + kv) * pd.Rs + b) * H + h) * S + s) * DK + d] = yh;
         }
       }
   });
@@ -763,6 +787,7 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
   __half* bbuf = reinterpret_cast<__half*>(work);
   ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx);
   csync();
+  event(cx, 70);
   float best[NT][2];
   int besti[NT][2];
 #pragma unroll
@@ -783,6 +808,7 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
                          merge_best(best[nt][e & 1], besti[nt][e & 1], ya, n);
                        }
                    });
+  event(cx, 71);
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1020,6 +1046,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       } else {
         int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
         cl_out_stage<NT>(pd, a, ring, cx, work, os);
+        event(cx, 72);
         if (a.pred) argmax_finish(pd, a, c, os, flag, work);
       }
     } else if (BEAM) {

@@ -44,7 +44,8 @@ constexpr int BLOCK = NTHR + 32;       // + producer warp
 constexpr int SLOT = 32768;            // ring slot bytes
 constexpr int MAXSLOT = 8;
 constexpr int MAXNT = 8;               // n-tiles of 8 tokens: M <= 64 tokens per call
-constexpr int MAXQ = 16;               // queries of one attention unit
+constexpr int MAXQ = 32;               // queries of one attention unit (grid-stage kernel)
+constexpr int CLQ = 16;                // queries of one attention unit (cluster kernel)
 constexpr int KTOP = 8;                // largest beam
 constexpr int APOS = SLOT / (DK * 2);  // attention positions per chunk (256)
 constexpr uint32_t DEFAULT_SPIN = 1u << 22;
@@ -100,6 +101,8 @@ struct PlanDev {
   int cl;                   // 1: the cluster kernel runs this plan
   int RG, NCL3, F3;         // cluster kernel: row groups per head, clusters of the FFN stage, hidden units each
   int wide;                 // cluster kernel: one-query attention units of >= 256 positions take steps of 32
+  int Rs, Us;               // cluster kernel: rows / utterances of the caller's buffers (layer strides of the
+                            // caches, new_kv and cross K/V), more than R / U when the call is a row slice
   long long* xf[3];         // cluster kernel: rotating fixed-point residual buffers [M][D]
 };
 
@@ -1833,7 +1836,12 @@ struct OwsmDecPlan {
   size_t smem = 0;
   int64_t scratch_bytes = 0;
   int beam = 0;
+  // a call of more than 16 tokens on the cluster kernel: consecutive row slices of whole utterances, one
+  // cluster-kernel launch each on the same stream (first row of each)
+  std::vector<OwsmDecPlan*> subs;
+  std::vector<int> sub_r0;
   ~OwsmDecPlan() {
+    for (OwsmDecPlan* q : subs) delete q;
     int cur = 0;
     cudaGetDevice(&cur);
     cudaSetDevice(h->device);
@@ -1944,7 +1952,7 @@ KernelFn cl_kernel_for(int NT, int Qmax, bool beam, bool wide) {
   if (Qmax == 1 && wide) return NT == 1 ? decoder_cl_kernel<1, 1, false, true> : decoder_cl_kernel<2, 1, false, true>;
   if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false, false> : decoder_cl_kernel<2, 1, false, false>;
   if (Qmax <= 8) return NT == 1 ? decoder_cl_kernel<1, 8, false, false> : decoder_cl_kernel<2, 8, false, false>;
-  return NT == 1 ? decoder_cl_kernel<1, MAXQ, false, false> : decoder_cl_kernel<2, MAXQ, false, false>;
+  return NT == 1 ? decoder_cl_kernel<1, CLQ, false, false> : decoder_cl_kernel<2, CLQ, false, false>;
 }
 
 KernelFn plan_kernel(const PlanDev& pd) {
@@ -2078,7 +2086,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   if (R % G) return fail(OWSM_DEC_ERR_ARG, "rows must be a multiple of rows_per_utt");
   const int M = R * S;
   if (M > MAXNT * 8) return fail(OWSM_DEC_ERR_LIMIT, "at most 64 tokens (rows x window) per call");
-  if (S > MAXQ || G * S > MAXQ) return fail(OWSM_DEC_ERR_LIMIT, "rows_per_utt x window must be <= 16");
+  if (S > MAXQ || G * S > MAXQ) return fail(OWSM_DEC_ERR_LIMIT, "rows_per_utt x window must be <= 32");
   if (beam) {
     if (beam < 1 || beam > KTOP || S != 1 || R % beam || G != beam)
       return fail(OWSM_DEC_ERR_LIMIT, "beam calls: S = 1, beam <= 8, rows = batch x beam, rows_per_utt = beam");
@@ -2094,6 +2102,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   pd.L = d.L; pd.D = d.D; pd.H = d.H; pd.F = d.F; pd.V = d.V; pd.max_pos = d.max_pos;
   pd.eps = d.eps; pd.xscale = d.xscale;
   pd.R = R; pd.S = S; pd.M = M; pd.NT = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; pd.C = C; pd.T = T; pd.G = G; pd.U = U; pd.beam = beam;
+  pd.Rs = R; pd.Us = U;
   pd.P = h->programs;
   pd.max_spin = h->max_spin;
   pd.emb = h->emb;
@@ -2110,7 +2119,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   // The cluster kernel: greedy calls of up to 16 tokens. Clusters of 4 CTAs, as many as fit one per SM;
   // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
   // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
-  if (allow_cl && (!beam || pd.Qmax > 1) && M <= 16 && d.D % 64 == 0 && d.F % 64 == 0) {
+  if (allow_cl && (!beam || pd.Qmax > 1) && M <= 16 && pd.Qmax <= CLQ && d.D % 64 == 0 && d.F % 64 == 0) {
     KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax, beam > 0, false);
     CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
     cudaLaunchConfig_t cfg = {};
@@ -2273,7 +2282,39 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
 extern "C" {
 
 int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out) {
-  if (!h) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  if (!h || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  const int G = rows_per_utt < 1 ? 1 : rows_per_utt;
+  // more than 16 tokens, greedy: row slices of whole utterances on the cluster kernel (each slice <= 16
+  // tokens), launched one after another; the grid-stage kernel if that cannot be laid out
+  if (h->path != 1 && !beam && R >= 1 && S >= 1 && R * S > 16 && R * S <= MAXNT * 8 && R % G == 0 && G * S <= 16) {
+    const int per = (16 / (S * G)) * G;  // rows per slice
+    OwsmDecPlan* p = new OwsmDecPlan();
+    p->h = h;
+    int rc = OWSM_DEC_OK;
+    for (int r0 = 0; r0 < R && rc == OWSM_DEC_OK; r0 += per) {
+      OwsmDecPlan* q = nullptr;
+      rc = plan_impl(h, std::min(per, R - r0), S, C, T, G, 0, true, &q);
+      if (rc == OWSM_DEC_OK && !q->pd.cl) rc = OWSM_DEC_ERR_LIMIT;
+      if (rc == OWSM_DEC_OK) {
+        q->pd.Rs = R;
+        q->pd.Us = R / G;
+        p->subs.push_back(q);
+        p->sub_r0.push_back(r0);
+        p->scratch_bytes += q->scratch_bytes;
+      } else if (q) {
+        delete q;
+      }
+    }
+    if (rc == OWSM_DEC_OK) {
+      p->pd = p->subs[0]->pd;  // (for the info calls: programs, ring slots, kernel)
+      p->pd.R = R;
+      p->pd.M = R * S;
+      *out = p;
+      return OWSM_DEC_OK;
+    }
+    delete p;
+    if (h->path == 2) return rc;
+  }
   const int rc = plan_impl(h, R, S, C, T, rows_per_utt, beam, h->path != 1, out);
   // a call the cluster kernel cannot lay out (shared memory, clusters) runs on the grid-stage kernel
   if (rc == OWSM_DEC_ERR_LIMIT && h->path == 0) return plan_impl(h, R, S, C, T, rows_per_utt, beam, false, out);
@@ -2318,6 +2359,21 @@ int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t t
                   int first_time, int last_time) {
   int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
   if (rc) return rc;
+  if (!p->subs.empty()) {  // row slices: the same buffers, offset to each slice's first row
+    const PlanDev& d0 = p->subs[0]->pd;
+    const long long H = d0.H, C = d0.C, T = d0.T, S = d0.S, V = d0.V, G = d0.G;
+    for (size_t i = 0; i < p->subs.size(); ++i) {
+      const long long r0 = p->sub_r0[i], u0 = r0 / G;
+      rc = owsm_dec_step(p->subs[i], stream, tokens + r0 * tok_stride, tok_stride, offset + r0 * off_stride, off_stride,
+                         reinterpret_cast<__half*>(self_k) + r0 * H * C * DK, reinterpret_cast<__half*>(self_v) + r0 * H * C * DK,
+                         reinterpret_cast<const __half*>(cross_k) + u0 * H * T * DK,
+                         reinterpret_cast<const __half*>(cross_v) + u0 * H * T * DK, enc_len ? enc_len + u0 : nullptr,
+                         logits + r0 * S * V, reinterpret_cast<__half*>(new_kv) + r0 * H * S * DK, pred ? pred + r0 * S : nullptr,
+                         notime ? notime + r0 : nullptr, first_time, last_time);
+      if (rc) return rc;
+    }
+    return OWSM_DEC_OK;
+  }
   CallArgs a{};
   a.tok = tokens; a.tok_stride = tok_stride;
   a.off = offset; a.off_stride = off_stride;
@@ -2365,6 +2421,11 @@ int owsm_dec_get_error(OwsmDec* h) {
 
 int owsm_dec_plan_reset(OwsmDecPlan* p) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  for (OwsmDecPlan* q : p->subs) {
+    const int rc = owsm_dec_plan_reset(q);
+    if (rc) return rc;
+  }
+  if (!p->subs.empty()) return OWSM_DEC_OK;
   DeviceGuard guard(p->h->device);
   CUDA_TRY(cudaDeviceSynchronize());
   CUDA_TRY(cudaMemset(p->pd.ctr, 0, 8 * sizeof(uint32_t)));
@@ -2382,6 +2443,7 @@ int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int
 
 int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  if (!p->subs.empty()) return owsm_dec_plan_trace(p->subs[0], stamps);  // a sliced call: its first slice
   DeviceGuard guard(p->h->device);
   p->pd.ts = reinterpret_cast<unsigned long long*>(stamps);
   return OWSM_DEC_OK;

@@ -108,7 +108,7 @@ def test_rows_per_utt_equals_duplicated_cross(kern, sd):
     assert (shared[0].cpu() - lo).abs().max().item() < 0.02 * lo.abs().max().item()
 
 
-@pytest.mark.parametrize("R,S", [(1, 1), (2, 5), (1, 16), (8, 8), (64, 1), (16, 4)])
+@pytest.mark.parametrize("R,S", [(1, 1), (2, 5), (1, 16), (8, 8), (64, 1), (16, 4), (1, 32), (2, 32)])
 def test_step_shapes_match_oracle(kern, sd, R, S):
     """Rows x window shapes up to the kernel's 64 tokens, against the oracle (reference: test_step_matches_decoder)."""
     d = TEST_CFG
@@ -120,6 +120,36 @@ def test_step_shapes_match_oracle(kern, sd, R, S):
     torch.testing.assert_close(new_kv.float().cpu(), kvo, atol=0.05, rtol=0.02)
     _check_cache(kc.to(DEV), vc.to(DEV), kc2, vc2, new_kv, offset)
     _argmax_ok(lo, logits, pred)
+
+
+@pytest.mark.parametrize("R,S", [(1, 1), (16, 1), (2, 5), (32, 1), (8, 8)])
+def test_kernel_choice_and_agreement(sd, R, S):
+    """Calls of up to 16 tokens run on the cluster kernel, larger ones as row slices of it; the cluster and
+    grid-stage kernels agree on the same call (logits and new K/V within the oracle tolerances)."""
+    _gpu()
+    from owsm_trt_b200.decoder import B200Decoder
+
+    d = TEST_CFG
+    C, T = 64, 37
+    tokens, offset, kc, vc, ck, cv = cases.step_inputs(d, R, S, C, T, 77 + R * 10 + S)
+    outs = {}
+    for path in (0, 1):
+        k = B200Decoder.from_state_dict(sd, d.H, DEV)
+        k.set_path(path)
+        logits = torch.zeros(R, S, d.V, device=DEV)
+        new_kv = torch.zeros(d.L, 2, R, d.H, S, d.dk, device=DEV, dtype=torch.float16)
+        kc2, vc2 = kc.clone().to(DEV), vc.clone().to(DEV)
+        pred = torch.zeros(R, S, dtype=torch.long, device=DEV)
+        run = k.step_fn(tokens.to(DEV), offset.to(DEV), kc2, vc2, ck.to(DEV), cv.to(DEV), logits, new_kv, pred=pred)
+        run()
+        torch.cuda.synchronize()
+        k.check()
+        outs[path] = (k.plan_kernel(run), logits.cpu(), new_kv.float().cpu())
+        k.close()
+    assert outs[0][0] == "cluster" and outs[1][0] == "grid"
+    lg0, lg1 = outs[0][1], outs[1][1]
+    assert (lg0 - lg1).abs().max().item() < 0.02 * lg1.abs().max().item()
+    torch.testing.assert_close(outs[0][2], outs[1][2], atol=0.05, rtol=0.02)
 
 
 def test_masked_lengths_match_oracle(kern, sd):
@@ -331,10 +361,10 @@ def test_medium_step_matches_reference_golden():
 
 
 @pytest.mark.slow
-@pytest.mark.parametrize("R,S", [(16, 4), (64, 1), (1, 16), (15, 1)])
+@pytest.mark.parametrize("R,S", [(16, 4), (64, 1), (1, 16), (15, 1), (1, 32)])
 def test_medium_row_counts_plan_and_run(R, S):
-    """Every row count the benchmarks use on the 1B-shaped model (prefill of 16 x 4, 64 rows, a 16-token
-    window, 15 beam rows) gets a plan within shared memory and runs: finite logits, argmax bit-exact
+    """Every row count the benchmarks use on the 1B-shaped model (prefill of 16 x 4, 64 rows, 16- and
+    32-token windows, 15 beam rows) gets a plan within shared memory and runs: finite logits, argmax bit-exact
     against them, the cache written at each row's offset."""
     from owsm_trt_b200.synthetic import MEDIUM_1B
 

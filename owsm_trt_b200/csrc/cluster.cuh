@@ -72,9 +72,13 @@ struct ClSmem {
 };
 
 __host__ __device__ constexpr size_t cl_bbuf_bytes(int NT, int D) { return (size_t)NT * D * 16; }
+// The attention area doubles as the split-k partial sums of block_chunks (a warp's NT x 4 floats per lane).
+__host__ __device__ constexpr size_t cl_attn_bytes(int NT, int Qmax) {
+  return attn_smem(Qmax) > (size_t)NWARP * NT * 512 ? attn_smem(Qmax) : (size_t)NWARP * NT * 512;
+}
 __host__ __device__ constexpr size_t cl_work_bytes(int NT, int D, int Qmax) {
   return cl_bbuf_bytes(NT, D) + (size_t)XQ_FLOATS * 4 + (size_t)PART_ENTRIES * XPS * 4 + (size_t)4 * NT * 256 +
-         attn_smem(Qmax) + 64;
+         cl_attn_bytes(NT, Qmax) + 64;
 }
 
 __device__ __forceinline__ ClSmem carve_cl(uint8_t* work, int NT, int D) {
@@ -229,10 +233,51 @@ __device__ __forceinline__ void chunk_gemm(uint32_t abase, int nblk, uint32_t as
 // The stage's single-block chunks j = 0 .. nch - 1 (16 rows x nkb k-blocks + a 64-byte bias tail), one warp
 // per chunk: the warp whose index is the chunk's ring slot (warps past the slot count idle), so each slot has
 // one consumer per phase. epi(j, acc, bias of rows g, g + 8).
+// With at most half as many chunks as warps (and `red`, a shared-memory area of NWARP x NT x 512 bytes,
+// given), a chunk's k-blocks are split over a team of NWARP / nch warps instead: a block's dependent mma
+// chain, not the data, sets its time, so a team finishes it in a fraction of one warp's time. The team's
+// other warps leave their partial sums in `red` and the first warp adds them up (in warp order) and runs epi.
 template <int NT, class Epi>
-__device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& epi) {
+__device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& epi, float* red = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
   const int ns = ring.ns;
+  if (red != nullptr && nch > 0 && 2 * nch <= NWARP && nch <= ns) {
+    const int ts = NWARP / nch, j = warp / ts, w = warp % ts;
+    if (j < nch) {
+      // whole groups of 4 k-blocks where nkb allows (block_mma's four-chain form), else pairs
+      const int u = (nkb & 3) == 0 ? 4 : 2, units = nkb / u, k0 = u * (units * w / ts), k1 = u * (units * (w + 1) / ts);
+      const uint8_t* slot = ring.wait_at(ring.i + j);
+      float acc[NT][4];
+      block_mma<NT>(smem_u32(slot) + lane * 16 + (uint32_t)k0 * 512, k1 - k0, bsh + (uint32_t)k0 * NT * 256, acc);
+      float bia[2] = {0.f, 0.f};
+      if (w == 0) {
+        const float* tail = reinterpret_cast<const float*>(slot + (size_t)nkb * 512);
+        bia[0] = tail[g];
+        bia[1] = tail[g + 8];
+      }
+      ring.release_at(ring.i + j, w == 0 ? NWARP - ts + 1 : 1);
+      float* mine = red + (warp * 32 + lane) * (NT * 4);
+      if (w > 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sts128f(mine + nt * 4, make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
+      }
+      asm volatile("bar.sync %0, %1;" ::"r"(2 + j), "r"(ts * 32) : "memory");
+      if (w == 0) {
+        for (int o = 1; o < ts; ++o)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            const float4 p = lds128f(mine + (o * 32) * (NT * 4) + nt * 4);
+            acc[nt][0] += p.x;
+            acc[nt][1] += p.y;
+            acc[nt][2] += p.z;
+            acc[nt][3] += p.w;
+          }
+        epi(j, acc, bia);
+      }
+    }
+    ring.i += nch;
+    return;
+  }
   const int j0 = warp < ns ? (warp - (int)(ring.i % (uint32_t)ns) + ns) % ns : nch;
   for (int j = j0; j < nch; j += ns) {
     const uint8_t* slot = ring.wait_at(ring.i + j);
@@ -342,14 +387,28 @@ __device__ __forceinline__ void warp_step(WarpSoftmax<QM>& st, const float* qs, 
   }
 }
 
-// One step of up to 32 key positions for one warp, for long position ranges: lane i holds the whole key
-// row of position i (64 dims in 32 half2 registers, its 16-byte pieces rotated by the lane so the 32 rows
-// spread over the banks) and scores it against each query in the log2 domain; the warp's max and sum run
-// over shuffles; the probabilities go through the warp's 32-float buffer, and lane l adds up output dims
-// 2 l, 2 l + 1 over the step's value rows, 8 rows per round. Same visibility rule as warp_step.
-template <int QM, bool F32>
-__device__ __forceinline__ void warp_step32(WarpSoftmax<QM>& st, const float* qs, int Q, const void* kp, const void* vp,
-                                            int n, int causal_base, float* pbuf) {
+// Warp-wide maximum of a float (one instruction on sm_100a).
+__device__ __forceinline__ float warp_max(float v) {
+  float r;
+  asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// The permuted query layout of the wide steps: the two 16-byte halves of dims 8 c .. 8 c + 7 at float
+// offsets 4 c and 32 + 4 c, so the lanes of a quarter warp, which read different chunks c of one half, hit
+// different banks.
+__device__ __forceinline__ int qperm(int d) { return ((d >> 2) & 1) * 32 + (d >> 3) * 4 + (d & 3); }
+
+// One step of up to 32 key positions for one warp and one query, for long position ranges: lane i holds the
+// whole key row of position i (64 dims in 32 half2 registers, its 16-byte pieces rotated by the lane so the
+// rows of a quarter warp spread over the banks) and scores it against the query (permuted layout `qp`) in
+// the log2 domain; the warp's max is one redux, the running sum of probabilities stays per lane (st.l, added
+// up over the warp once the unit is done); the probabilities go through the warp's 32-float buffer and lane
+// l adds up output dims 2 l, 2 l + 1 over the step's value rows, 8 rows per round. The query sees position
+// i when causal_base < 0 or causal_base + i <= 0.
+template <bool F32>
+__device__ __forceinline__ void warp_step32(WarpSoftmax<1>& st, const float* qp, const void* kp, const void* vp, int n,
+                                            int causal_base, float* pbuf) {
   const int lane = threadIdx.x & 31;
   uint32_t kr[32];
   if (lane < n) {
@@ -370,68 +429,55 @@ __device__ __forceinline__ void warp_step32(WarpSoftmax<QM>& st, const float* qs
 #pragma unroll
     for (int i = 0; i < 32; ++i) kr[i] = 0u;
   }
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-  for (int q = 0; q < QM; ++q) {
-    if (q >= Q) break;
-    const float* qq = qs + q * DK;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      const int pc = (c + lane) & 7;
-      const float4 a = lds128f(qq + pc * 8), b = lds128f(qq + pc * 8 + 4);
-      const float2 k0 = unpack_half2(kr[4 * c]), k1 = unpack_half2(kr[4 * c + 1]);
-      const float2 k2 = unpack_half2(kr[4 * c + 2]), k3 = unpack_half2(kr[4 * c + 3]);
-      s0 = fmaf(a.x, k0.x, fmaf(a.y, k0.y, s0));
-      s1 = fmaf(a.z, k1.x, fmaf(a.w, k1.y, s1));
-      s2 = fmaf(b.x, k2.x, fmaf(b.y, k2.y, s2));
-      s3 = fmaf(b.z, k3.x, fmaf(b.w, k3.y, s3));
-    }
-    const bool ok = lane < n && (causal_base < 0 || causal_base + lane <= q);
-    const float sc = ok ? ((s0 + s1) + (s2 + s3)) * kLog2e : -INFINITY;  // log2 domain
-    float mx = sc;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float mnew = fmaxf(st.m[q], mx);
-    if (mnew == -INFINITY) continue;
-    const float al = st.m[q] > -INFINITY ? exp2f(st.m[q] - mnew) : 0.f;
-    const float p = ok ? exp2f(sc - mnew) : 0.f;
-    float ps = p;
-#pragma unroll
-    for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-    st.l[q] = st.l[q] * al + ps;
-    asm volatile("st.shared.f32 [%0], %1;" ::"r"(smem_u32(pbuf + lane)), "f"(p) : "memory");
-    __syncwarp();
-    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
-    {
-      // 8 value rows per round, loads issued together; rows past n have p = 0 and are not read
+  for (int c = 0; c < 8; ++c) {
+    const int pc = (c + lane) & 7;
+    const float4 a = lds128f(qp + pc * 4), b = lds128f(qp + 32 + pc * 4);
+    const float2 k0 = unpack_half2(kr[4 * c]), k1 = unpack_half2(kr[4 * c + 1]);
+    const float2 k2 = unpack_half2(kr[4 * c + 2]), k3 = unpack_half2(kr[4 * c + 3]);
+    s0 = fmaf(a.x, k0.x, fmaf(a.y, k0.y, s0));
+    s1 = fmaf(a.z, k1.x, fmaf(a.w, k1.y, s1));
+    s2 = fmaf(b.x, k2.x, fmaf(b.y, k2.y, s2));
+    s3 = fmaf(b.z, k3.x, fmaf(b.w, k3.y, s3));
+  }
+  const bool ok = lane < n && (causal_base < 0 || causal_base + lane <= 0);
+  const float sc = ok ? ((s0 + s1) + (s2 + s3)) * kLog2e : -INFINITY;  // log2 domain
+  const float mnew = fmaxf(st.m[0], warp_max(sc));
+  if (mnew == -INFINITY) return;
+  const float al = exp2f(st.m[0] - mnew);  // 0 while nothing was visible (m = -inf)
+  const float p = ok ? exp2f(sc - mnew) : 0.f;
+  st.l[0] = st.l[0] * al + p;
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(smem_u32(pbuf + lane)), "f"(p) : "memory");
+  __syncwarp();
+  float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  // 8 value rows per round, loads issued together; rows past n have p = 0 and are not read
 #pragma unroll 1
-      for (int i0 = 0; i0 < n; i0 += 8) {
-        float pv[8];
-        float2 vv[8];
+  for (int i0 = 0; i0 < n; i0 += 8) {
+    const float4 pa = lds128f(pbuf + i0), pb = lds128f(pbuf + i0 + 4);
+    const float pv[8] = {pa.x, pa.y, pa.z, pa.w, pb.x, pb.y, pb.z, pb.w};
+    float2 vv[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int i = i0 + e;
-          pv[e] = i < n ? lds32f(pbuf + i) : 0.f;
-          if (F32) {
-            vv[e] = i < n ? *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vp) + i * DK + 2 * lane) : make_float2(0.f, 0.f);
-          } else {
-            uint32_t r0 = 0u;
-            if (i < n) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r0) : "r"(smem_u32(reinterpret_cast<const __half*>(vp) + i * DK + 2 * lane)));
-            vv[e] = unpack_half2(r0);
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          a0 = fmaf(pv[e], vv[e].x, a0); a1 = fmaf(pv[e], vv[e].y, a1);
-          b0 = fmaf(pv[e + 1], vv[e + 1].x, b0); b1 = fmaf(pv[e + 1], vv[e + 1].y, b1);
-        }
+    for (int e = 0; e < 8; ++e) {
+      const int i = i0 + e;
+      if (F32) {
+        vv[e] = i < n ? *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(vp) + i * DK + 2 * lane) : make_float2(0.f, 0.f);
+      } else {
+        uint32_t r0 = 0u;
+        if (i < n) asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r0) : "r"(smem_u32(reinterpret_cast<const __half*>(vp) + i * DK + 2 * lane)));
+        vv[e] = unpack_half2(r0);
       }
     }
-    __syncwarp();
-    st.o0[q] = st.o0[q] * al + (a0 + b0);
-    st.o1[q] = st.o1[q] * al + (a1 + b1);
-    st.m[q] = mnew;
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      a0 = fmaf(pv[e], vv[e].x, a0); a1 = fmaf(pv[e], vv[e].y, a1);
+      b0 = fmaf(pv[e + 1], vv[e + 1].x, b0); b1 = fmaf(pv[e + 1], vv[e + 1].y, b1);
+    }
   }
+  __syncwarp();
+  st.o0[0] = st.o0[0] * al + (a0 + b0);
+  st.o1[0] = st.o1[0] * al + (a1 + b1);
+  st.m[0] = mnew;
 }
 
 
@@ -440,9 +486,10 @@ __device__ __forceinline__ void warp_step32(WarpSoftmax<QM>& st, const float* qs
 // chunk; warp w takes the steps of 8 positions w, w + 7, ... of each chunk and keeps its own online-softmax
 // state, so no block barrier is needed per chunk), then with nnew > 0 the call's own keys/values (s.knew /
 // s.vnew [nnew][64], fp32; query q sees new key j <= q, Q = nnew) on the warp with the least chunk work.
-// The warps' states are merged once: s.out (unnormalised), s.mrun, s.lrun per query.
+// The warps' states are merged once: s.out (unnormalised), s.mrun, s.lrun per query. Wide units (WIDE, one
+// query) read the query from s.out in the permuted layout of qperm, which the caller writes beside s.q.
 template <int QM, bool WIDE>
-__device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew) {
+__device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew, const Ctx& cx) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // long ranges of one query: steps of 32 positions (log2 domain); otherwise steps of 8 (the wide step's
   // registers would crowd the per-query state of several queries)
@@ -450,8 +497,11 @@ __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, 
   WarpSoftmax<QM> st;
 #pragma unroll
   for (int q = 0; q < QM; ++q) st.m[q] = -INFINITY, st.l[q] = 0.f, st.o0[q] = 0.f, st.o1[q] = 0.f;
-  float* pbuf = s.sc + 2 * NWARP * QM + warp * 32;  // this warp's probabilities of a wide step
+  // this warp's probabilities of a wide step (after the merge's per-warp m, l; 16-byte aligned: the step
+  // reads them with 128-bit loads)
+  float* pbuf = s.sc + ((2 * NWARP * QM + 3) & ~3) + warp * 32;
   csync();  // the queries (and new keys / values) are in shared memory
+  event(cx, 80);
   int last_steps = 0;
   for (int j0 = p0; j0 < p1; j0 += apos) {
     const int npos = p1 - j0 < apos ? p1 - j0 : apos;
@@ -464,7 +514,7 @@ __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, 
       const int nsteps = (npos + 31) >> 5, sbase = (j0 - p0) >> 5;
       for (int t = (warp - sbase % NWARP + NWARP) % NWARP; t < nsteps; t += NWARP) {
         const int n = npos - t * 32 < 32 ? npos - t * 32 : 32;
-        warp_step32<QM, false>(st, s.q, Q, kt + (size_t)t * 32 * DK, vt + (size_t)t * 32 * DK, n, -1, pbuf);
+        warp_step32<false>(st, s.out, kt + (size_t)t * 32 * DK, vt + (size_t)t * 32 * DK, n, -1, pbuf);
       }
       last_steps = sbase + nsteps;
       }
@@ -481,13 +531,21 @@ __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, 
     ring.release();  // keys
     ring.release();  // values
   }
+  event(cx, 81);
   if (nnew > 0 && warp == (last_steps % NWARP)) {  // a warp with no more chunk steps than the others
     if constexpr (WIDE && QM == 1) {
-      if (wide) warp_step32<QM, true>(st, s.q, Q, s.knew, s.vnew, nnew, 0, pbuf);  // nnew <= 16
+      if (wide) warp_step32<true>(st, s.out, s.knew, s.vnew, nnew, 0, pbuf);  // nnew = 1 (one query)
     }
     if (!wide) {
       for (int j = 0; j < nnew; j += 8)
         warp_step<QM, true>(st, s.q, Q, s.knew + (size_t)j * DK, s.vnew + (size_t)j * DK, nnew - j < 8 ? nnew - j : 8, j);
+    }
+  }
+  event(cx, 82);
+  if constexpr (WIDE && QM == 1) {
+    if (wide) {  // the lanes' running sums -> the warp's
+#pragma unroll
+      for (int o = 16; o; o >>= 1) st.l[0] += __shfl_xor_sync(0xffffffffu, st.l[0], o);
     }
   }
   // merge the warps: per warp m, l (sc area) and its output dims (scratch)
@@ -557,11 +615,54 @@ __device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* x
   }
 }
 
+// LayerNorm of tokens 0 .. M - 1 (residual rows m0 ..) into the B operand at bbuf, the same on every CTA of
+// the cluster. From CL_LN_SPLIT tokens on, each CTA normalises a quarter of them (a row costs the loads'
+// round trips, not bandwidth, so four CTAs finish in about the time of one quarter) and stores their
+// fragments into the other CTAs' bbuf through st.async on the exchange barrier xb; the CTAs' tokens are
+// disjoint, so each B operand is the one a single CTA would have made. Ends with the operand complete.
+// The LayerNorm itself runs out of line: inlined into every stage of the cluster kernel, its 32 registers of
+// row values pushed the kernel's allocation into spills across the GEMM and attention loops (a called copy
+// measured about 7% faster at batch 1 and 19% at batch 16; the grid-stage kernel keeps it inline, where the
+// call measured slower).
+__device__ __noinline__ void cl_ln_call(const PlanDev& pd, const long long* x, int m0, int M, int NT, __half* bbuf,
+                                        const Ctx& cx, int r0, int r1) {
+  ln_rows(pd, x, m0, M, NT, bbuf, cx, r0, r1);
+}
+
+constexpr int CL_LN_SPLIT = 8;
+__device__ void cl_ln_rows(const PlanDev& pd, const long long* x, int m0, int M, int NT, __half* bbuf, const Ctx& cx,
+                           int r, uint64_t* xb, uint32_t& ph, Ring& ring) {
+  const bool split = M >= CL_LN_SPLIT;
+  const int D = pd.D, r0 = split ? M * r / CS : 0, r1 = split ? M * (r + 1) / CS : M;
+  if (split && threadIdx.x == 0) mbar_arrive_expect_tx(xb, (uint32_t)((M - (r1 - r0)) * D * 2));
+  cl_ln_call(pd, x, m0, M, NT, bbuf, cx, r0, r1);
+  csync();
+  if (!split) return;
+  // a token's fragments: per k-block 32 contiguous bytes, k-blocks NT * 256 bytes apart
+  const uint32_t b_s = smem_u32(bbuf), xb_s = smem_u32(xb);
+  const int per_row = D / 8;  // 16-byte pieces of a token
+  for (int i = threadIdx.x; i < (r1 - r0) * per_row; i += NTHR) {
+    const int m = r0 + i / per_row, c = i % per_row;
+    const uint32_t off = (uint32_t)((((c >> 1) * NT + (m >> 3)) * 32 + (m & 7) * 4) * 8 + (c & 1) * 16);
+    const uint4 v = lds128_u32(b_s + off);
+#pragma unroll
+    for (int q = 1; q < CS; ++q) {
+      const uint32_t dst = (uint32_t)((r + q) % CS);
+      st_async_v4(mapa_shared(b_s + off, dst), v, mapa_shared(xb_s, dst));
+    }
+  }
+  if (!mbar_wait_cluster(xb, ph, pd.max_spin)) {
+    ring.dead = true;
+    atomicExch(pd.err, E_ERR_TIMEOUT);
+  }
+  ph ^= 1u;
+}
+
 // S1 (kind 1, self-attention) or S2 (kind 2, cross-attention) of a cluster that owns (head h, row group).
 // QM: compile-time bound of the queries of an attention unit (1 for one-token calls without row sharing).
 template <int NT, int QM, bool WIDE>
 __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, const Cl& cl,
-                              const int* pre, int kind, int l, uint8_t* work, uint64_t* xbar, uint32_t (&ph)[2],
+                              const int* pre, int kind, int l, uint8_t* work, uint64_t* xbar, uint32_t (&ph)[3],
                               const long long* xin, long long* xout) {
   const int D = pd.D, H = pd.H, S = pd.S, h = cl.h, r = cl.r, Mg = cl.Mg;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
@@ -576,8 +677,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
     mbar_arrive_expect_tx(&xbar[0], (uint32_t)((CS - 1) * my * Mg * 4));
     mbar_arrive_expect_tx(&xbar[1], (uint32_t)((nunits - mine) * Qu * XPS * 4));
   }
-  ln_rows(pd, xin, cl.m0, Mg, NT, sm.bbuf, cx);
-  csync();
+  cl_ln_rows(pd, xin, cl.m0, Mg, NT, sm.bbuf, cx, r, &xbar[2], ph[2], ring);
   event(cx, 51);
   const uint32_t xq_s = smem_u32(sm.xq), part_s = smem_u32(sm.part);
   const uint32_t bar0_s = smem_u32(&xbar[0]), bar1_s = smem_u32(&xbar[1]);
@@ -607,7 +707,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
           a.new_kv[((((long long)(l * 2 + kv) * pd.Rs + b) * H + h) * S + s) * DK + d] = yh;
         }
       }
-  });
+  }, reinterpret_cast<float*>(sm.attn));
   csync();
   event(cx, 52);
   if (!mbar_wait_cluster(&xbar[0], ph[0], pd.max_spin)) {
@@ -629,6 +729,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       for (int idx = threadIdx.x; idx < S * DK; idx += NTHR) {
         const int q = idx / DK, d = idx % DK, ml = item * S + q;
         as.q[idx] = sm.xq[ml * nq + d] * 0.125f;
+        if (QM == 1 && WIDE) as.out[qperm(d)] = as.q[idx];  // the wide steps' copy (s.out until the merge)
         as.knew[idx] = sm.xq[ml * nq + DK + d];
         as.vnew[idx] = sm.xq[ml * nq + 2 * DK + d];
       }
@@ -639,9 +740,10 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       for (int idx = threadIdx.x; idx < Qu * DK; idx += NTHR) {
         const int q = idx / DK, d = idx % DK;
         as.q[idx] = sm.xq[(item * Qu + q) * nq + d] * 0.125f;
+        if (QM == 1 && WIDE) as.out[qperm(d)] = as.q[idx];
       }
     }
-    attn_unit<QM, WIDE>(as, ring, Qu, p0, p1, pd.apos, nnew);
+    attn_unit<QM, WIDE>(as, ring, Qu, p0, p1, pd.apos, nnew, cx);
     for (int idx = threadIdx.x; idx < Qu * (XPS / 4); idx += NTHR) {
       const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
       float4 v;
@@ -715,7 +817,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
 // S3: FFN1 rows of this cluster's hidden slice (+ReLU), exchanged as B fragments; FFN2 slice -> residual.
 template <int NT>
 __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const Cl& cl, uint8_t* work,
-                             uint64_t* xbar, uint32_t (&ph)[2], const long long* xin, long long* xout) {
+                             uint64_t* xbar, uint32_t (&ph)[3], const long long* xin, long long* xout) {
   const int D = pd.D, M = pd.M, r = cl.r, F3 = pd.F3, rows = F3 / CS, nkb3 = F3 / 16;
   const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const ClSmem sm = carve_cl(work, NT, D);
@@ -723,8 +825,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
   const int kb_mine = rows / 16;                   // this CTA's k-blocks: r * kb_mine ..
   const uint32_t my_bytes = (uint32_t)kb_mine * NT * 256;
   if (threadIdx.x == 0) mbar_arrive_expect_tx(&xbar[0], (CS - 1) * my_bytes);
-  ln_rows(pd, xin, 0, M, NT, sm.bbuf, cx);
-  csync();
+  cl_ln_rows(pd, xin, 0, M, NT, sm.bbuf, cx, r, &xbar[2], ph[2], ring);
   event(cx, 60);
   block_chunks<NT>(ring, rows / 16, D / 16, smem_u32(sm.bbuf), [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
 #pragma unroll
@@ -735,7 +836,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
         const float y = m < M ? fmaxf(acc[nt][e] + bia[e >> 1], 0.f) : 0.f;
         hb[bfrag_idx(m, k, NT)] = __float2half_rn(y);
       }
-  });
+  }, reinterpret_cast<float*>(sm.attn));
   csync();
   event(cx, 61);
   const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;
@@ -781,12 +882,11 @@ namespace owsm {
 // (first index on ties; timestamp ids left out for flagged rows), merged over the warps into os.amax/aidx.
 template <int NT>
 __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, uint8_t* work,
-                             OutState& os) {
+                             OutState& os, uint64_t* xb, uint32_t& ph) {
   const int M = pd.M, V = pd.V;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   __half* bbuf = reinterpret_cast<__half*>(work);
-  ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx);
-  csync();
+  cl_ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx, (int)(blockIdx.x % CS), xb, ph, ring);
   event(cx, 70);
   float best[NT][2];
   int besti[NT][2];
@@ -841,11 +941,11 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
 // tile at a time, as the grid kernel does), then merged over the warps into os.rmax / rsum / topv / topi.
 template <int NT>
 __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, uint8_t* work,
-                                  OutState& os) {
+                                  OutState& os, uint64_t* xb, uint32_t& ph) {
   const int M = pd.M, V = pd.V;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   __half* bbuf = reinterpret_cast<__half*>(work);
-  ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx);
+  cl_ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx, (int)(blockIdx.x % CS), xb, ph, ring);
   for (int m = lane; m < M; m += 32) {
     os.wrmax[warp * M + m] = -INFINITY;
     os.wrsum[warp * M + m] = 0.f;
@@ -917,7 +1017,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAXSLOT;
-  uint64_t* xbar = empty + MAXSLOT;  // the two exchange barriers of a stage
+  uint64_t* xbar = empty + MAXSLOT;  // the exchange barriers of a stage (two) and of its LayerNorm
   int* pre = reinterpret_cast<int*>(smem + pd.off_pre);
   uint8_t* ringdata = smem + pd.off_ring;
   uint8_t* work = smem + pd.off_work;
@@ -934,6 +1034,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
     }
     mbar_init(&xbar[0], 1);
     mbar_init(&xbar[1], 1);
+    mbar_init(&xbar[2], 1);
     fence_barrier_init();
     pre[0] = 0;
     for (int u = 0; u < pd.U; ++u) pre[u + 1] = pre[u] + utt_len(pd, a, u);
@@ -1014,7 +1115,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       os.topi[threadIdx.x * KTOP + j] = 0x7fffffff;
     }
   }
-  uint32_t ring_i = 0, ph[2] = {0u, 0u};
+  uint32_t ring_i = 0, ph[3] = {0u, 0u, 0u};
   bool dead = false;
   for (int g = 0; g < n_stages; ++g) {
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
@@ -1041,11 +1142,11 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (g == n_out) {
       OutState os = carve_out(smem + pd.off_out, pd.M, BEAM);
       if (BEAM) {
-        cl_out_stage_beam<NT>(pd, a, ring, cx, work, os);
+        cl_out_stage_beam<NT>(pd, a, ring, cx, work, os, &xbar[2], ph[2]);
         beam_partials(pd, c, os);
       } else {
         int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
-        cl_out_stage<NT>(pd, a, ring, cx, work, os);
+        cl_out_stage<NT>(pd, a, ring, cx, work, os, &xbar[2], ph[2]);
         event(cx, 72);
         if (a.pred) argmax_finish(pd, a, c, os, flag, work);
       }

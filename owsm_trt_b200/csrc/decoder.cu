@@ -339,9 +339,9 @@ struct Ring {
     if (timing) waited += globaltimer() - t0;
     return data + (size_t)s * stride;
   }
-  __device__ void release_at(uint32_t idx) {
+  __device__ void release_at(uint32_t idx, int cnt = NWARP) {  // cnt: this warp's share of the NWARP arrivals
     __syncwarp();
-    if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(&empty[idx % ns], NWARP);
+    if ((threadIdx.x & 31) == 0) mbar_arrive_cnt(&empty[idx % ns], cnt);
   }
 };
 
@@ -385,13 +385,17 @@ __device__ __forceinline__ float4 load4(const long long* row, int i) {
 // From 7 rows on, a warp normalises whole rows; below that a row is split over a team of 7 / M warps whose
 // partial sums meet in shared memory, so one row costs one round trip for its loads and a few hundred
 // cycles rather than a single warp's serial pass over 1024 values.
+// r0 .. r1 - 1 (default: all M) are the tokens this call normalises; the padding is zeroed either way.
 template <class T>
-__device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __half* bbuf, const Ctx& cx) {
+__device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __half* bbuf, const Ctx& cx,
+                        int r0 = 0, int r1 = -1) {
   const int D = pd.D, nv = D / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
     for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
-  const int ts = M >= NWARP ? 1 : NWARP / M;  // warps per row
+  if (r1 < 0) r1 = M;
+  const int Mc = r1 - r0;
+  const int ts = Mc >= NWARP ? 1 : NWARP / Mc;  // warps per row
   auto emit = [&](int m, int i, const float4& v, float mean, float rstd) {
     const int k = i * 4;
     *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k, NT)]) =
@@ -400,7 +404,7 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
         __floats2half2_rn((v.z - mean) * rstd, (v.w - mean) * rstd);
   };
   if (ts == 1) {
-    for (int m = warp; m < M; m += NWARP) {
+    for (int m = r0 + warp; m < r1; m += NWARP) {
       const T* xr = x + (long long)(m0 + m) * D;
       float4 v[MAXV4];
 #pragma unroll
@@ -432,8 +436,8 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
   }
   // teams: row m = warp / ts (warps past M * ts only join the barriers); member j takes float4s
   // j * 32 + lane + k * ts * 32
-  const int m = warp / ts, j = warp % ts, step = ts * 32;
-  const bool on = m < M;
+  const int mt = warp / ts, m = r0 + mt, j = warp % ts, step = ts * 32;
+  const bool on = mt < Mc;
   float4 v[MAXV4];
   float s = 0.f;
   if (on) {
@@ -453,7 +457,7 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
   float mean = 0.f, q = 0.f;
   if (on) {
     float tot = 0.f;
-    for (int w = m * ts; w < m * ts + ts; ++w) tot += cx.red[w];
+    for (int w = mt * ts; w < mt * ts + ts; ++w) tot += cx.red[w];
     mean = tot / D;
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
@@ -468,7 +472,7 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
   csync();
   if (on) {
     float tq = 0.f;
-    for (int w = m * ts; w < m * ts + ts; ++w) tq += cx.red[NWARP + w];
+    for (int w = mt * ts; w < mt * ts + ts; ++w) tq += cx.red[NWARP + w];
     const float rstd = rsqrtf(tq / D + pd.eps);
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)

@@ -84,6 +84,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", type=int, default=0, help="0: cluster kernel where it applies, 1: grid-stage kernel")
+    ap.add_argument("--events", type=int, nargs="*", default=[], help="CTAs whose event log to print")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
     import bench
@@ -109,9 +110,28 @@ def main() -> None:
         run()
     e1.record()
     torch.cuda.synchronize(dev)
-    s = summary(profile(k, run), d.L)
+    ts = profile(k, run)
+    s = summary(ts, d.L)
     print(json.dumps({"kernel": k.plan_kernel(run), "batch": B, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
                       "stages": s}, indent=1))  # fmt: skip
+    for c in args.events:
+        print(json.dumps({"cta": c, "events": event_log(ts, c)}))
+
+
+def event_log(ts: torch.Tensor, c: int) -> list[list[float]]:
+    """CTA c's event log as [tag, µs since the kernel's first stage start] in the order recorded (the first 64
+    events of the call: tag 20 a LayerNorm row's loads issued, 50-57 the steps of an attention stage, 60-63 of
+    an FFN stage, 70-72 of the output stage, 80-82 inside an attention unit: queries ready, cached positions
+    done, new positions done)."""
+    ev = ts.events[c]
+    t0 = int(ts[0, :, 0].min())
+    out = []
+    for i in range(0, ev.numel() - 1, 2):
+        t, tag = int(ev[i]), int(ev[i + 1]) & 0xFF
+        if t == 0:
+            break
+        out.append([tag, round((t - t0) / 1e3, 3)])
+    return out
 
 
 if __name__ == "__main__":

@@ -164,6 +164,22 @@ def test_masked_lengths_match_oracle(kern, sd):
     assert (logits.cpu() - lo).abs().max().item() < 0.02 * lo.abs().max().item()
 
 
+@pytest.mark.parametrize("masked", [False, True])
+def test_wide_steps_match_oracle(kern, sd, masked):
+    """32 one-token rows over 300 encoder frames: with 4 heads the cluster kernel gives each cross-attention
+    unit a whole utterance, so units of 256 frames or more take the wide (32-position) steps and shorter
+    masked ones the 8-position steps, both within the oracle tolerance."""
+    d = TEST_CFG
+    R, C, T = 32, 64, 300
+    tokens, offset, kc, vc, ck, cv = cases.step_inputs(d, R, 1, C, T, 66)
+    lens = [300, 256, 299, 255, 1, 40, 280, 150] * 4 if masked else None
+    el = None if lens is None else torch.tensor(lens)
+    lo, _ = ref.decoder_step(sd, d.H, tokens, offset, kc.float(), vc.float(), ck.float(), cv.float(), enc_len=el)
+    logits, _, _, _, pred = _run_step(kern, d, tokens, offset, kc.to(DEV), vc.to(DEV), ck, cv, enc_len=lens)
+    assert (logits.cpu() - lo).abs().max().item() < 0.02 * lo.abs().max().item()
+    assert torch.equal(pred.cpu(), ref.argmax_first(logits.cpu()))
+
+
 def test_argmax_without_timestamps(kern):
     """Rows flagged <notimestamps> get the argmax over the other ids (megakernel_ring's NOTIME)."""
     d = TEST_CFG

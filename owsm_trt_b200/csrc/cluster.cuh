@@ -1138,7 +1138,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
         cl_ffn_stage<NT>(pd, ring, cx, cl, work, xbar, ph, xin, xout);
       }
       event(cx, 57);
-      __threadfence();
+      // (no per-thread fence: the grid barrier's release by thread 0 after the CTA barrier publishes the
+      // stage's writes, as in the grid-stage kernel)
     } else if (g == n_out) {
       OutState os = carve_out(smem + pd.off_out, pd.M, BEAM);
       if (BEAM) {

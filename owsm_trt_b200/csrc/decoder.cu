@@ -391,8 +391,10 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
                         int r0 = 0, int r1 = -1) {
   const int D = pd.D, nv = D / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  event(cx, 21);
   for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
     for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
+  event(cx, 22);
   if (r1 < 0) r1 = M;
   const int Mc = r1 - r0;
   const int ts = Mc >= NWARP ? 1 : NWARP / Mc;  // warps per row
@@ -454,6 +456,7 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
     if (lane == 0) cx.red[warp] = s;
   }
   csync();
+  event(cx, 23);
   float mean = 0.f, q = 0.f;
   if (on) {
     float tot = 0.f;

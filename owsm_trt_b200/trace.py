@@ -120,7 +120,8 @@ def main() -> None:
 
 def event_log(ts: torch.Tensor, c: int) -> list[list[float]]:
     """CTA c's event log as [tag, µs since the kernel's first stage start] in the order recorded (the first 64
-    events of the call: tag 20 a LayerNorm row's loads issued, 50-57 the steps of an attention stage, 60-63 of
+    events of the call: tags 21, 22, 20, 23 inside a LayerNorm (entry, padding zeroed, a row's loads done,
+    a team's first barrier passed), 50-57 the steps of an attention stage, 60-63 of
     an FFN stage, 70-72 of the output stage, 80-82 inside an attention unit: queries ready, cached positions
     done, new positions done)."""
     ev = ts.events[c]

@@ -624,9 +624,11 @@ __device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* x
 // row values pushed the kernel's allocation into spills across the GEMM and attention loops (a called copy
 // measured about 7% faster at batch 1 and 19% at batch 16; the grid-stage kernel keeps it inline, where the
 // call measured slower).
+// The padding tokens' fragments are left as they are: a GEMM's output column m depends on B column m alone,
+// and every epilogue of this kernel drops the columns of padding tokens.
 __device__ __noinline__ void cl_ln_call(const PlanDev& pd, const long long* x, int m0, int M, int NT, __half* bbuf,
                                         const Ctx& cx, int r0, int r1) {
-  ln_rows(pd, x, m0, M, NT, bbuf, cx, r0, r1);
+  ln_rows(pd, x, m0, M, NT, bbuf, cx, r0, r1, false);
 }
 
 constexpr int CL_LN_SPLIT = 8;

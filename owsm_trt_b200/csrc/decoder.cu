@@ -173,11 +173,12 @@ __device__ __forceinline__ int utt_len(const PlanDev& pd, const CallArgs& a, int
   return t < 1 ? 1 : (t > pd.T ? pd.T : t);
 }
 
-// Half index of element (token m, feature k) in B-fragment order with NT n-tiles.
-__device__ __forceinline__ long long bfrag_idx(int m, int k, int NT) {
-  int kb = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
-  int reg = kk >> 3, t = (kk & 7) >> 1, e = kk & 1;
-  return ((((long long)kb * NT + nt) * 32 + (g * 4 + t)) * 4) + reg * 2 + e;
+// Half index of element (token m, feature k) in B-fragment order with NT n-tiles (32-bit: every B operand,
+// in shared or global memory, holds far fewer than 2^31 halves).
+__device__ __forceinline__ int bfrag_idx(int m, int k, int NT) {
+  const int kb = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
+  const int reg = kk >> 3, t = (kk & 7) >> 1, e = kk & 1;
+  return (((kb * NT + nt) * 32 + (g * 4 + t)) * 4) + reg * 2 + e;
 }
 
 // The frame-space partition of cross-attention: frames of all (utterance, head) segments in a row,
@@ -380,20 +381,27 @@ __device__ __forceinline__ float4 load4(const long long* row, int i) {
   return make_float4(from_fix(a.x), from_fix(a.y), from_fix(b.x), from_fix(b.y));
 }
 
+// Zero fragments for the padding tokens M .. NT * 8 - 1 of a B operand over D features.
+__device__ __forceinline__ void zero_pad_tokens(__half* bbuf, int M, int NT, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int m = M + warp; m < NT * 8; m += NWARP)
+    for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
+}
+
 // LayerNorm of rows m0 .. m0 + M - 1 of the residual stream into the B operand (fragment order over NT
 // tiles of 8 tokens, shared memory), padding tokens zero.
 // From 7 rows on, a warp normalises whole rows; below that a row is split over a team of 7 / M warps whose
 // partial sums meet in shared memory, so one row costs one round trip for its loads and a few hundred
 // cycles rather than a single warp's serial pass over 1024 values.
 // r0 .. r1 - 1 (default: all M) are the tokens this call normalises; the padding is zeroed either way.
+// pad = false: the caller keeps the padding tokens' fragments zero itself.
 template <class T>
 __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __half* bbuf, const Ctx& cx,
-                        int r0 = 0, int r1 = -1) {
+                        int r0 = 0, int r1 = -1, bool pad = true) {
   const int D = pd.D, nv = D / 4;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   event(cx, 21);
-  for (int m = M + warp; m < NT * 8; m += NWARP)  // padding tokens: zero fragments
-    for (int k = lane * 2; k < D; k += 64) *reinterpret_cast<uint32_t*>(&bbuf[bfrag_idx(m, k, NT)]) = 0u;
+  if (pad) zero_pad_tokens(bbuf, M, NT, D);
   event(cx, 22);
   if (r1 < 0) r1 = M;
   const int Mc = r1 - r0;

@@ -413,6 +413,20 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
     *reinterpret_cast<__half2*>(&bbuf[bfrag_idx(m, k + 2, NT)]) =
         __floats2half2_rn((v.z - mean) * rstd, (v.w - mean) * rstd);
   };
+  // One pass of statistics: the sum and the sum of squares in fp64 (a float's square is exact in double,
+  // so E[x^2] - mean^2 keeps full fp32 accuracy), one shuffle round and, for a team, one barrier.
+  auto moments = [&](const float4& u, double& s1, double& s2) {
+    s1 += ((double)u.x + (double)u.y) + ((double)u.z + (double)u.w);
+    s2 = fma((double)u.x, (double)u.x, s2);
+    s2 = fma((double)u.y, (double)u.y, s2);
+    s2 = fma((double)u.z, (double)u.z, s2);
+    s2 = fma((double)u.w, (double)u.w, s2);
+  };
+  auto finish = [&](double s1, double s2, float& mean, float& rstd) {
+    const double mu = s1 / D, var = fmax(s2 / D - mu * mu, 0.0);
+    mean = (float)mu;
+    rstd = rsqrtf((float)var + pd.eps);
+  };
   if (ts == 1) {
     for (int m = r0 + warp; m < r1; m += NWARP) {
       const T* xr = x + (long long)(m0 + m) * D;
@@ -420,71 +434,60 @@ __device__ void ln_rows(const PlanDev& pd, const T* x, int m0, int M, int NT, __
 #pragma unroll
       for (int i = 0; i < MAXV4; ++i)
         if (i * 32 + lane < nv) v[i] = load4(xr, i * 32 + lane);
-      float s = 0.f;
+      double s1 = 0.0, s2 = 0.0;
 #pragma unroll
       for (int i = 0; i < MAXV4; ++i)
-        if (i * 32 + lane < nv) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+        if (i * 32 + lane < nv) moments(v[i], s1, s2);
       event(cx, 20);
 #pragma unroll
-      for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      const float mean = s / D;
-      float q = 0.f;
-#pragma unroll
-      for (int i = 0; i < MAXV4; ++i)
-        if (i * 32 + lane < nv) {
-          const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
-          q += (a * a + b * b) + (c * c + d * d);
-        }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-      const float rstd = rsqrtf(q / D + pd.eps);
+      for (int o = 16; o; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      float mean, rstd;
+      finish(s1, s2, mean, rstd);
 #pragma unroll
       for (int i = 0; i < MAXV4; ++i)
         if (i * 32 + lane < nv) emit(m, i * 32 + lane, v[i], mean, rstd);
     }
     return;
   }
-  // teams: row m = warp / ts (warps past M * ts only join the barriers); member j takes float4s
-  // j * 32 + lane + k * ts * 32
+  // teams: row m = warp / ts (warps past M * ts only join the barrier); member j takes float4s
+  // j * 32 + lane + k * ts * 32; the members' sums meet in shared memory (cx.red as 2 x NWARP doubles)
   const int mt = warp / ts, m = r0 + mt, j = warp % ts, step = ts * 32;
   const bool on = mt < Mc;
+  double* red = reinterpret_cast<double*>(cx.red);
   float4 v[MAXV4];
-  float s = 0.f;
   if (on) {
     const T* xr = x + (long long)(m0 + m) * D;
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
       if (j * 32 + lane + k * step < nv) v[k] = load4(xr, j * 32 + lane + k * step);
+    double s1 = 0.0, s2 = 0.0;
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
-      if (j * 32 + lane + k * step < nv) s += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+      if (j * 32 + lane + k * step < nv) moments(v[k], s1, s2);
     event(cx, 20);
 #pragma unroll
-    for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    if (lane == 0) cx.red[warp] = s;
+    for (int o = 16; o; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+      red[warp] = s1;
+      red[NWARP + warp] = s2;
+    }
   }
   csync();
   event(cx, 23);
-  float mean = 0.f, q = 0.f;
   if (on) {
-    float tot = 0.f;
-    for (int w = mt * ts; w < mt * ts + ts; ++w) tot += cx.red[w];
-    mean = tot / D;
-#pragma unroll
-    for (int k = 0; k < MAXV4; ++k)
-      if (j * 32 + lane + k * step < nv) {
-        const float a = v[k].x - mean, b = v[k].y - mean, c = v[k].z - mean, d = v[k].w - mean;
-        q += (a * a + b * b) + (c * c + d * d);
-      }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    if (lane == 0) cx.red[NWARP + warp] = q;
-  }
-  csync();
-  if (on) {
-    float tq = 0.f;
-    for (int w = mt * ts; w < mt * ts + ts; ++w) tq += cx.red[NWARP + w];
-    const float rstd = rsqrtf(tq / D + pd.eps);
+    double s1 = 0.0, s2 = 0.0;
+    for (int w = mt * ts; w < mt * ts + ts; ++w) {
+      s1 += red[w];
+      s2 += red[NWARP + w];
+    }
+    float mean, rstd;
+    finish(s1, s2, mean, rstd);
 #pragma unroll
     for (int k = 0; k < MAXV4; ++k)
       if (j * 32 + lane + k * step < nv) emit(m, j * 32 + lane + k * step, v[k], mean, rstd);

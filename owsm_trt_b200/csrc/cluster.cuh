@@ -604,14 +604,29 @@ __device__ void cl_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, in
 
 // This CTA's slice of the next residual buffer: + input residual + the stage's output bias; and its slice
 // of the free buffer zeroed (the stage after next adds into it).
+// Part c of n of the pass (the stage's idle CTAs share it when it has any, so the CTAs with work start their
+// LayerNorm at once; otherwise all P CTAs).
 __device__ void cl_residual(const PlanDev& pd, int gi, int l, const long long* xin, long long* xout, long long* xfree,
-                            int c) {
+                            int c, int n) {
   const long long total = (long long)pd.M * pd.D;
-  const long long lo = total * c / pd.P, hi = total * (c + 1) / pd.P;
+  const long long lo = total * c / n, hi = total * (c + 1) / n;
   const float* bias = pd.g[gi].b + (long long)l * pd.D;
-  for (long long i = lo + threadIdx.x; i < hi; i += NTHR) {
-    red_add_s64(xout + i, __ldcg(xin + i) + to_fix(__ldg(bias + i % pd.D)));
-    xfree[i] = 0;
+  // 4 elements per thread per round, loads first: one L2 round trip per round, not per element
+  for (long long i0 = lo + threadIdx.x; i0 < hi; i0 += 4 * NTHR) {
+    long long v[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const long long i = i0 + (long long)e * NTHR;
+      if (i < hi) v[e] = __ldcg(xin + i) + to_fix(__ldg(bias + i % pd.D));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const long long i = i0 + (long long)e * NTHR;
+      if (i < hi) {
+        red_add_s64(xout + i, v[e]);
+        xfree[i] = 0;
+      }
+    }
   }
 }
 
@@ -1130,9 +1145,15 @@ __global__ void __launch_bounds__(BLOCK, 1)
       const long long* xin = pd.xf[(g - 1) % 3];
       long long* xout = pd.xf[g % 3];
       long long* xfree = pd.xf[(g + 1) % 3];
-      cl_residual(pd, kind == 1 ? G_WO : (kind == 2 ? G_WCO : G_F2), l, xin, xout, xfree, c);
-      event(cx, 50);
       const Cl cl = cluster_view(pd);
+      const int busy = CS * (kind < 3 ? pd.H * pd.RG : pd.NCL3);  // CTAs 0 .. busy - 1 have stage work
+      const int gres = kind == 1 ? G_WO : (kind == 2 ? G_WCO : G_F2);
+      if (busy < pd.P) {
+        if (c >= busy) cl_residual(pd, gres, l, xin, xout, xfree, c - busy, pd.P - busy);
+      } else {
+        cl_residual(pd, gres, l, xin, xout, xfree, c, pd.P);
+      }
+      event(cx, 50);
       if (kind < 3) {
         if (cl.cid < pd.H * pd.RG && cl.Mg > 0)
           cl_attn_stage<NT, QM, WIDE>(pd, a, ring, cx, cl, pre, kind, l, work, xbar, ph, xin, xout);

@@ -486,10 +486,13 @@ __device__ __forceinline__ void warp_step32(WarpSoftmax<1>& st, const float* qp,
 // chunk; warp w takes the steps of 8 positions w, w + 7, ... of each chunk and keeps its own online-softmax
 // state, so no block barrier is needed per chunk), then with nnew > 0 the call's own keys/values (s.knew /
 // s.vnew [nnew][64], fp32; query q sees new key j <= q, Q = nnew) on the warp with the least chunk work.
-// The warps' states are merged once: s.out (unnormalised), s.mrun, s.lrun per query. Wide units (WIDE, one
+// The warps' states are merged once into the unit's partial state, handed to emit(q, c4, piece) as 17
+// 16-byte pieces per query (unnormalised output dims, then the max in natural-log units and the sum);
+// no barrier follows, so the caller passes one before it reads what emit stored. Wide units (WIDE, one
 // query) read the query from s.out in the permuted layout of qperm, which the caller writes beside s.q.
-template <int QM, bool WIDE>
-__device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew, const Ctx& cx) {
+template <int QM, bool WIDE, class Emit>
+__device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, int apos, int nnew, const Ctx& cx,
+                          Emit&& emit) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // long ranges of one query: steps of 32 positions (log2 domain); otherwise steps of 8 (the wide step's
   // registers would crowd the per-query state of several queries)
@@ -561,27 +564,31 @@ __device__ void attn_unit(const AttnSmem& s, Ring& ring, int Q, int p0, int p1, 
     *reinterpret_cast<float2*>(&s.scratch[(warp * Q + q) * DK + 2 * lane]) = make_float2(st.o0[q], st.o1[q]);
   }
   csync();
-  for (int idx = threadIdx.x; idx < Q * DK; idx += NTHR) {
-    const int q = idx / DK, d = idx % DK;
+  // per query 17 pieces of 4 floats: dims 4 c4 .. 4 c4 + 3 (c4 < 16), then (max in natural-log units, sum)
+  for (int idx = threadIdx.x; idx < Q * (XPS / 4); idx += NTHR) {
+    const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
     float mx = -INFINITY;
     for (int w = 0; w < NWARP; ++w) mx = fmaxf(mx, wm[w * QM + q]);
-    float o = 0.f, l = 0.f;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
     if (mx > -INFINITY)
       for (int w = 0; w < NWARP; ++w) {
         const float mw = wm[w * QM + q];
         if (mw > -INFINITY) {
           const float f = wide ? exp2f(mw - mx) : expf(mw - mx);
-          o += f * s.scratch[(w * Q + q) * DK + d];
-          l += f * wl[w * QM + q];
+          if (c4 < DK / 4) {
+            const float4 sv = lds128f(&s.scratch[(w * Q + q) * DK + c4 * 4]);
+            o.x += f * sv.x;
+            o.y += f * sv.y;
+            o.z += f * sv.z;
+            o.w += f * sv.w;
+          } else {
+            l += f * wl[w * QM + q];
+          }
         }
       }
-    s.out[idx] = o;
-    if (d == 0) {
-      s.mrun[q] = wide ? mx / kLog2e : mx;  // the partial's max in natural-log units
-      s.lrun[q] = l;
-    }
+    emit(q, c4, c4 < DK / 4 ? o : make_float4(wide ? mx / kLog2e : mx, l, 0.f, 0.f));
   }
-  csync();
 }
 
 // ------------------------------------------------------------------------------------------------ stages
@@ -760,12 +767,8 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         if (QM == 1 && WIDE) as.out[qperm(d)] = as.q[idx];
       }
     }
-    attn_unit<QM, WIDE>(as, ring, Qu, p0, p1, pd.apos, nnew, cx);
-    for (int idx = threadIdx.x; idx < Qu * (XPS / 4); idx += NTHR) {
-      const int q = idx / (XPS / 4), c4 = idx % (XPS / 4);
-      float4 v;
-      if (c4 < DK / 4) v = lds128f(&as.out[q * DK + c4 * 4]);
-      else v = make_float4(as.mrun[q], as.lrun[q], 0.f, 0.f);
+    // the unit's partial state -> this CTA's table and every other cluster CTA's
+    attn_unit<QM, WIDE>(as, ring, Qu, p0, p1, pd.apos, nnew, cx, [&](int q, int c4, const float4& v) {
       const int off = (k * Qu + q) * XPS + c4 * 4;
       sts128f(&sm.part[off], v);
       const uint4 w = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
@@ -774,10 +777,11 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
         const uint32_t dst = (uint32_t)((r + i) % CS);
         st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
       }
-    }
-    csync();
+    });
     event(cx, 54);
   }
+  csync();  // this CTA's own entries are in the table (the next unit's staging needed none: it touches no
+            // area the merge reads, and attn_unit starts with a barrier)
   if (!mbar_wait_cluster(&xbar[1], ph[1], pd.max_spin)) {
     ring.dead = true;
     atomicExch(pd.err, E_ERR_TIMEOUT);
@@ -785,10 +789,11 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
   ph[1] ^= 1u;
   event(cx, 55);
   // every token of the group: its units' parts combined in part order -> the out-projection's B operand
-  for (int idx = threadIdx.x; idx < NT * 8 * (DK / 2); idx += NTHR) {
+  // (padding tokens' columns are left as they are: the out-projection's epilogue drops them)
+  for (int idx = threadIdx.x; idx < Mg * (DK / 2); idx += NTHR) {
     const int m = idx / (DK / 2), dp = idx % (DK / 2);
     float n0 = 0.f, n1 = 0.f;
-    if (m < Mg) {
+    {
       const int item = m / Qu, q = m % Qu;
       const float* e0 = sm.part + ((size_t)(item * parts) * Qu + q) * XPS;
       const size_t step = (size_t)Qu * XPS;

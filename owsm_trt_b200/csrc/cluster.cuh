@@ -238,7 +238,8 @@ __device__ __forceinline__ void chunk_gemm(uint32_t abase, int nblk, uint32_t as
 // chain, not the data, sets its time, so a team finishes it in a fraction of one warp's time. The team's
 // other warps leave their partial sums in `red` and the first warp adds them up (in warp order) and runs epi.
 template <int NT, class Epi>
-__device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& epi, float* red = nullptr) {
+__device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& epi, float* red = nullptr,
+                             const Ctx* cx = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2;
   const int ns = ring.ns;
   if (red != nullptr && nch > 0 && 2 * nch <= NWARP && nch <= ns) {
@@ -247,8 +248,10 @@ __device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& e
       // whole groups of 4 k-blocks where nkb allows (block_mma's four-chain form), else pairs
       const int u = (nkb & 3) == 0 ? 4 : 2, units = nkb / u, k0 = u * (units * w / ts), k1 = u * (units * (w + 1) / ts);
       const uint8_t* slot = ring.wait_at(ring.i + j);
+      if (cx) event(*cx, 90);
       float acc[NT][4];
       block_mma<NT>(smem_u32(slot) + lane * 16 + (uint32_t)k0 * 512, k1 - k0, bsh + (uint32_t)k0 * NT * 256, acc);
+      if (cx) event(*cx, 91);
       float bia[2] = {0.f, 0.f};
       if (w == 0) {
         const float* tail = reinterpret_cast<const float*>(slot + (size_t)nkb * 512);
@@ -262,6 +265,7 @@ __device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& e
         for (int nt = 0; nt < NT; ++nt) sts128f(mine + nt * 4, make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]));
       }
       asm volatile("bar.sync %0, %1;" ::"r"(2 + j), "r"(ts * 32) : "memory");
+      if (cx) event(*cx, 92);
       if (w == 0) {
         for (int o = 1; o < ts; ++o)
 #pragma unroll
@@ -273,6 +277,7 @@ __device__ void block_chunks(Ring& ring, int nch, int nkb, uint32_t bsh, Epi&& e
             acc[nt][3] += p.w;
           }
         epi(j, acc, bia);
+        if (cx) event(*cx, 93);
       }
     }
     ring.i += nch;
@@ -682,6 +687,22 @@ __device__ void cl_ln_rows(const PlanDev& pd, const long long* x, int m0, int M,
   ph ^= 1u;
 }
 
+// Four consecutive fp16 values (exact: v holds fp16-rounded values) at p: one 8-byte store where p allows.
+__device__ __forceinline__ void store4h(__half* p, const float4& v) {
+  const __half2 lo = __floats2half2_rn(v.x, v.y), hi = __floats2half2_rn(v.z, v.w);
+  if ((reinterpret_cast<uintptr_t>(p) & 7) == 0) {
+    uint2 u;
+    u.x = *reinterpret_cast<const uint32_t*>(&lo);
+    u.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+    p[0] = __low2half(lo);
+    p[1] = __high2half(lo);
+    p[2] = __low2half(hi);
+    p[3] = __high2half(hi);
+  }
+}
+
 // S1 (kind 1, self-attention) or S2 (kind 2, cross-attention) of a cluster that owns (head h, row group).
 // QM: compile-time bound of the queries of an attention unit (1 for one-token calls without row sharing).
 template <int NT, int QM, bool WIDE>
@@ -715,24 +736,30 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
       for (int e = 0; e < 4; ++e) {
         const int row = my * r + j * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
         if (m >= Mg) continue;
-        const __half yh = __float2half_rn(acc[nt][e] + bia[e >> 1]);
-        const float y = __half2float(yh);  // fp16 like the projection output the reference attends with
-        const int idx = m * nq + row;
-        sm.xq[idx] = y;
-#pragma unroll
-        for (int i = 1; i < CS; ++i) {
-          const uint32_t dst = (uint32_t)((r + i) % CS);
-          st_async_b32(mapa_shared(xq_s + idx * 4, dst), __float_as_uint(y), mapa_shared(bar0_s, dst));
-        }
-        if (kind == 1 && row >= DK) {  // new key / value: the cache slot and new_kv
-          const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
-          const long long cslot = ((((long long)l * pd.Rs + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
-          (kv ? a.vc : a.kc)[cslot] = yh;
-          a.new_kv[((((long long)(l * 2 + kv) * pd.Rs + b) * H + h) * S + s) * DK + d] = yh;
-        }
+        // fp16 like the projection output the reference attends with
+        sm.xq[m * nq + row] = __half2float(__float2half_rn(acc[nt][e] + bia[e >> 1]));
       }
-  }, reinterpret_cast<float*>(sm.attn));
+  }, reinterpret_cast<float*>(sm.attn), &cx);
   csync();
+  // this CTA's rows of each token, 4 at a time: to the other cluster CTAs' exchange buffers and, for key and
+  // value rows (4 dims of one row: my and DK are multiples of 4), to the cache slot and new_kv
+  const int pieces = my / 4;
+  for (int i = threadIdx.x; i < Mg * pieces; i += NTHR) {
+    const int m = i / pieces, row = my * r + (i % pieces) * 4, idx = m * nq + row;
+    const float4 v = lds128f(&sm.xq[idx]);
+    const uint4 w = make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w));
+#pragma unroll
+    for (int q = 1; q < CS; ++q) {
+      const uint32_t dst = (uint32_t)((r + q) % CS);
+      st_async_v4(mapa_shared(xq_s + idx * 4, dst), w, mapa_shared(bar0_s, dst));
+    }
+    if (kind == 1 && row >= DK) {
+      const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
+      const long long cslot = ((((long long)l * pd.Rs + b) * H + h) * pd.C + cx.offs[b] + s) * DK + d;
+      store4h((kv ? a.vc : a.kc) + cslot, v);
+      store4h(a.new_kv + ((((long long)(l * 2 + kv) * pd.Rs + b) * H + h) * S + s) * DK + d, v);
+    }
+  }
   event(cx, 52);
   if (!mbar_wait_cluster(&xbar[0], ph[0], pd.max_spin)) {
     ring.dead = true;
@@ -858,7 +885,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
         const float y = m < M ? fmaxf(acc[nt][e] + bia[e >> 1], 0.f) : 0.f;
         hb[bfrag_idx(m, k, NT)] = __float2half_rn(y);
       }
-  }, reinterpret_cast<float*>(sm.attn));
+  }, reinterpret_cast<float*>(sm.attn), &cx);
   csync();
   event(cx, 61);
   const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;

@@ -123,7 +123,8 @@ def event_log(ts: torch.Tensor, c: int) -> list[list[float]]:
     events of the call: tags 21, 22, 20, 23 inside a LayerNorm (entry, padding zeroed, a row's loads done,
     a team's first barrier passed), 50-57 the steps of an attention stage, 60-63 of
     an FFN stage, 70-72 of the output stage, 80-82 inside an attention unit: queries ready, cached positions
-    done, new positions done)."""
+    done, new positions done, 90-93 inside a split projection chunk: data ready, partial product done, team
+    barrier passed, epilogue done)."""
     ev = ts.events[c]
     t0 = int(ts[0, :, 0].min())
     out = []

@@ -219,11 +219,13 @@ __device__ __forceinline__ void block_mma(uint32_t ash, int nkb, uint32_t bsh, f
 }
 
 // All consumer warps on one ring chunk of `nblk` blocks (block i at abase + i * astride): warp w takes
-// blocks w, w + 7, ...; epi(i, acc) per block.
+// the blocks i with (first + i) % 7 == w, so a stage whose blocks span several chunks (first = the chunk's
+// first block) spreads them evenly; epi(i, acc) per block.
 template <int NT, class Epi>
-__device__ __forceinline__ void chunk_gemm(uint32_t abase, int nblk, uint32_t astride, int nkb, uint32_t bsh, Epi&& epi) {
+__device__ __forceinline__ void chunk_gemm(uint32_t abase, int nblk, uint32_t astride, int nkb, uint32_t bsh, Epi&& epi,
+                                           int first = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = warp; i < nblk; i += NWARP) {
+  for (int i = (warp - first % NWARP + NWARP) % NWARP; i < nblk; i += NWARP) {
     float acc[NT][4];
     block_mma<NT>(abase + (uint32_t)i * astride + lane * 16, nkb, bsh, acc);
     epi(i, acc);
@@ -858,7 +860,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
           const int nn = rb * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
           if (m < Mg) red_add_s64(xout + (long long)(cl.m0 + m) * D + nn, to_fix(acc[nt][e]));
         }
-    });
+    }, bb);
     ring.release();
   }
 }
@@ -917,7 +919,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
           const int nn = rb * 16 + g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1);
           if (m < M) red_add_s64(xout + (long long)m * D + nn, to_fix(acc[nt][e]));
         }
-    });
+    }, bb);
     ring.release();
   }
 }

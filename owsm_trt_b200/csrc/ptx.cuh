@@ -234,7 +234,14 @@ __device__ __forceinline__ void cluster_sync_all() {
 __device__ __forceinline__ void red_add_s64(long long* p, long long v) {
   asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ long long to_fix(float v) { return __float2ll_rn(v * 4294967296.0f); }
+// (as the integer part plus the fraction scaled to 32 bits: two fast 32-bit conversions rather than one
+// 64-bit one; within 2^-24 of v rounded to the 2^-32 grid, and deterministic, which is what the exact
+// integer sums need; |v| < 2^31)
+__device__ __forceinline__ long long to_fix(float v) {
+  const float h = floorf(v);
+  const unsigned lo = __float2uint_rn((v - h) * 4294967296.0f);  // saturates at 2^32 - 1
+  return (long long)(int)h * 4294967296ll + (long long)lo;
+}
 // (high word as a 32-bit integer plus the low word scaled: two fast 32-bit conversions rather than one
 // 64-bit one, which is much slower; same value to within a rounding of the low word's contribution)
 __device__ __forceinline__ float from_fix(long long v) {

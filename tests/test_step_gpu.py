@@ -377,6 +377,29 @@ def test_medium_step_matches_reference_golden():
 
 
 @pytest.mark.slow
+def test_medium_batch16_matches_oracle():
+    """The benchmark's call shape on the 1B-shaped model (16 one-token rows, two token tiles, LayerNorm split
+    over each cluster, wide cross-attention steps for the units of 256 frames or more) against the oracle:
+    logits within the oracle tolerance, argmax bit-exact outside near-ties, new K/V and cache."""
+    from owsm_trt_b200.synthetic import MEDIUM_1B
+
+    d = MEDIUM_1B
+    sd, k = _medium()
+    R, C, T = 16, 64, 300
+    tokens, offset, kc, vc, ck, cv = cases.step_inputs(d, R, 1, C, T, 4242)
+    lens = [300, 256, 299, 255, 17, 280, 150, 300, 1, 270, 290, 120, 260, 300, 64, 257]
+    lo, kvo = ref.decoder_step(sd, d.H, tokens, offset, kc.float(), vc.float(), ck.float(), cv.float(),
+                               enc_len=torch.tensor(lens))  # fmt: skip
+    logits, new_kv, kc2, vc2, pred = _run_step(k, d, tokens, offset, kc.to(DEV), vc.to(DEV), ck, cv, enc_len=lens)
+    assert k.plan_kernel(k.step_fn(tokens.to(DEV), offset.to(DEV), kc2, vc2, ck.to(DEV), cv.to(DEV), logits,
+                                   new_kv)) == "cluster"  # fmt: skip
+    assert (logits.cpu() - lo).abs().max().item() < 0.02 * lo.abs().max().item()
+    torch.testing.assert_close(new_kv.float().cpu(), kvo, atol=0.05, rtol=0.02)
+    _check_cache(kc.to(DEV), vc.to(DEV), kc2, vc2, new_kv, offset)
+    _argmax_ok(lo, logits, pred)
+
+
+@pytest.mark.slow
 @pytest.mark.parametrize("R,S", [(16, 4), (64, 1), (1, 16), (15, 1), (1, 32)])
 def test_medium_row_counts_plan_and_run(R, S):
     """Every row count the benchmarks use on the 1B-shaped model (prefill of 16 x 4, 64 rows, 16- and

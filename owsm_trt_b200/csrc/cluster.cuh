@@ -1228,6 +1228,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
       atomicExch(&pd.ctr[0], 0u);
     }
   }
+  // no CTA leaves while another CTA of its cluster may still address its shared memory (an exchange store
+  // sent late after a timed-out wait); the producer warps, exited, do not count
+  cluster_sync_all();
 }
 
 }  // namespace owsm

@@ -141,6 +141,10 @@ int owsm_dec_set_path(OwsmDec* h, int path);
  * kernel (three per layer). */
 int owsm_dec_plan_kernel(const OwsmDecPlan* p);
 
+/* Kernel launches of one call of the plan: 1, or the number of row slices a call of more than 16 tokens is cut
+ * into (each slice one launch of the cluster kernel). No counterpart in owsm-trt (one launch per call). */
+int owsm_dec_plan_launches(const OwsmDecPlan* p);
+
 /* Testing hook: the in-kernel wait limit (polls) of later calls on this handle; 0 restores the default. */
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
 
@@ -152,6 +156,9 @@ int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls);
  * the bytes it needs. The scratch is one fixed array of the library per device: the first call for a
  * handle and shape on a device looks it up (cudaGetSymbolAddress, with the handle's device current),
  * zeroes it and uploads the block tables, synchronously -- make that first call before any stream capture.
+ * That set-up runs again, with a device-wide synchronisation, whenever the handle or any of R, S, C, T
+ * differs from the previous call on the device: keep the shape fixed between calls (pad rows of finished
+ * utterances instead of shrinking R) so that steady-state calls never block on the device.
  * Every call then zeroes the inter-CTA counters on `stream` and launches. Calls that overlap on one device
  * (other streams, other threads, other handles) share the array and race: run one at a time per device.
  * Arguments as owsm_dec_step, plus the call shape R, S, C (cache slots), T (encoder frames). */

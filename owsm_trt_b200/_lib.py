@@ -47,6 +47,7 @@ SIGNATURES = {
     "owsm_dec_set_max_spin": (i32, [vp, u32]),
     "owsm_dec_set_path": (i32, [vp, i32]),
     "owsm_dec_plan_kernel": (i32, [vp]),
+    "owsm_dec_plan_launches": (i32, [vp]),
     "owsm_dec_step_static": (i32, [vp, vp, i32, i32, i32, i32, vp, i64, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                    i32, i32]),  # fmt: skip
     "owsm_dec_last_error": (C.c_char_p, []),

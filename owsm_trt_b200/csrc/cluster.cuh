@@ -672,7 +672,8 @@ __device__ void cl_ln_rows(const PlanDev& pd, const long long* x, int m0, int M,
   // a token's fragments: per k-block 32 contiguous bytes, k-blocks NT * 256 bytes apart
   const uint32_t b_s = smem_u32(bbuf), xb_s = smem_u32(xb);
   const int per_row = D / 8;  // 16-byte pieces of a token
-  for (int i = threadIdx.x; i < (r1 - r0) * per_row; i += NTHR) {
+  // (a failed call sends nothing more: a peer that gave up waiting may be past the point of receiving)
+  for (int i = threadIdx.x; !ring.dead && i < (r1 - r0) * per_row; i += NTHR) {
     const int m = r0 + i / per_row, c = i % per_row;
     const uint32_t off = (uint32_t)((((c >> 1) * NT + (m >> 3)) * 32 + (m & 7) * 4) * 8 + (c & 1) * 16);
     const uint4 v = lds128_u32(b_s + off);
@@ -753,7 +754,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
 #pragma unroll
     for (int q = 1; q < CS; ++q) {
       const uint32_t dst = (uint32_t)((r + q) % CS);
-      st_async_v4(mapa_shared(xq_s + idx * 4, dst), w, mapa_shared(bar0_s, dst));
+      if (!ring.dead) st_async_v4(mapa_shared(xq_s + idx * 4, dst), w, mapa_shared(bar0_s, dst));
     }
     if (kind == 1 && row >= DK) {
       const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
@@ -804,7 +805,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
 #pragma unroll
       for (int i = 1; i < CS; ++i) {
         const uint32_t dst = (uint32_t)((r + i) % CS);
-        st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
+        if (!ring.dead) st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
       }
     });
     event(cx, 54);
@@ -892,7 +893,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
   event(cx, 61);
   const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;
   const uint32_t bar0 = smem_u32(&xbar[0]);
-  for (int i = threadIdx.x; i < (int)(my_bytes / 16); i += NTHR) {
+  for (int i = threadIdx.x; !ring.dead && i < (int)(my_bytes / 16); i += NTHR) {
     const uint4 v = lds128_u32(mine_s + i * 16);
 #pragma unroll
     for (int q = 1; q < CS; ++q) {
@@ -1215,7 +1216,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
     ring_i = ring.i;
     dead = ring.dead;
     if (ts && threadIdx.x == 0) ts[1] = globaltimer();
-    if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead);
+    if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead, reinterpret_cast<int*>(smem + pd.off_pre) + 1034);
     if (ts && threadIdx.x == 0) {
       ts[2] = globaltimer();
       ts[3] = ring.waited;

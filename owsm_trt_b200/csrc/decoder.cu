@@ -347,7 +347,9 @@ struct Ring {
 };
 
 // Grid barrier: all P CTAs arrive after their stage; bounded wait; the counter resets at kernel exit.
-__device__ void grid_sync(const PlanDev& pd, uint32_t target, bool& dead) {
+// sdead (shared memory, optional): thread 0 publishes there whether the call has failed (its own timed-out
+// wait or any CTA's error word), and every consumer thread takes it over as `dead`.
+__device__ void grid_sync(const PlanDev& pd, uint32_t target, bool& dead, int* sdead = nullptr) {
   csync();
   if (threadIdx.x == 0) {
     red_release_add(&pd.ctr[0], 1);
@@ -360,9 +362,13 @@ __device__ void grid_sync(const PlanDev& pd, uint32_t target, bool& dead) {
           break;
         }
       }
+    } else {
+      dead = true;
     }
+    if (sdead) *sdead = dead ? 1 : 0;
   }
   csync();
+  if (sdead) dead = *sdead != 0;
 }
 
 // ------------------------------------------------------------------------------------------------ GEMM
@@ -2293,6 +2299,9 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   int per_sm = 0;
   CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan_kernel(pd), BLOCK, p->smem));
   if (per_sm < 1) return bail(fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM"));
+  // the block-table uploads are pageable copies on the legacy stream, possibly still in flight; calls launch
+  // on the caller's stream (maybe a non-blocking one, unordered against the legacy stream): finish them now
+  CUDA_TRY(cudaDeviceSynchronize());
   *out = p;
   return OWSM_DEC_OK;
 }
@@ -2484,6 +2493,11 @@ int owsm_dec_plan_kernel(const OwsmDecPlan* p) {
   return p->pd.cl ? 2 : 1;
 }
 
+int owsm_dec_plan_launches(const OwsmDecPlan* p) {
+  if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
+  return p->subs.empty() ? 1 : (int)p->subs.size();
+}
+
 int owsm_dec_set_max_spin(OwsmDec* h, uint32_t polls) {
   if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
   h->max_spin = polls ? polls : DEFAULT_SPIN;
@@ -2642,6 +2656,10 @@ static int static_layout(OwsmDec* h, int R, int S, int C, int T, uint8_t* base, 
   int per_sm = 0;
   CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel_for(pd.NT), BLOCK, smem));
   if (per_sm < 1) return fail(OWSM_DEC_ERR_LIMIT, "the kernel does not fit an SM");
+  // The memset and the pageable uploads above run on the legacy stream and may still be in flight when they
+  // return; the call launches on the caller's stream, which need not be ordered after the legacy stream (a
+  // non-blocking stream is not): wait for them here, at set-up.
+  CUDA_TRY(cudaDeviceSynchronize());
   return OWSM_DEC_OK;
 }
 

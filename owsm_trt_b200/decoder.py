@@ -173,6 +173,10 @@ class B200Decoder:
         """"cluster" or "grid": the kernel behind a step_fn / beam_fn closure."""
         return "cluster" if _lib.lib().owsm_dec_plan_kernel(run.plan) == 2 else "grid"
 
+    def launches(self, run) -> int:
+        """Kernel launches of one call of a step_fn / beam_fn closure (1, or its row slices)."""
+        return int(_lib.lib().owsm_dec_plan_launches(run.plan))
+
     def set_max_spin(self, polls: int) -> None:
         """Testing hook: the in-kernel wait limit of later calls (0: the default)."""
         _lib.check(_lib.lib().owsm_dec_set_max_spin(self._h, polls), "owsm_dec_set_max_spin")

@@ -117,3 +117,28 @@ def cross_kv(sd: dict[str, torch.Tensor], dims: DecoderDims, enc: torch.Tensor) 
             kv.append(y.reshape(B, T, dims.H, dims.dk).transpose(1, 2))
         out.append(torch.stack(kv))
     return torch.stack(out)
+
+
+# The benchmark workload's fixed shapes: a 4-token prefix, 750 encoder frames, 256 cache slots.
+PREFIX, T_ENC, CACHE = 4, 750, 256
+
+
+def make_workload(d: DecoderDims, sd: dict[str, torch.Tensor], dev: torch.device, batch: int, seed: int,
+                  rows_per_utt: int = 1, enc_lo: int = 300):
+    """Inputs of one benchmark batch: cross K/V of ``batch / rows_per_utt`` utterances (encoder memory N(0,1)
+    [U, 750, D] through the decoder's K/V projections, :func:`cross_kv`), encoder lengths U[enc_lo, 750],
+    a 4-token prefix per row, and zeroed fp16 caches of 256 slots.
+    Returns (cross_k, cross_v, enc_len int32 (CPU), prefix int64 (CPU), self_k, self_v)."""
+    g = torch.Generator().manual_seed(seed)
+    U = batch // rows_per_utt
+    enc = torch.randn(U, T_ENC, d.D, generator=g).to(dev)
+    sd_dev = {k: v.to(dev) for k, v in sd.items() if ".src_attn.linear_k." in k or ".src_attn.linear_v." in k}
+    with torch.no_grad():
+        kv = cross_kv(sd_dev, d, enc).half()  # [L, 2, U, H, T, dk]
+    ck, cv = kv[:, 0].contiguous(), kv[:, 1].contiguous()
+    del kv, enc, sd_dev
+    enc_len = torch.randint(enc_lo, T_ENC + 1, (U,), generator=g).to(torch.int32)
+    prefix = torch.randint(0, d.V, (batch, PREFIX), generator=g)
+    kc = torch.zeros(d.L, batch, d.H, CACHE, d.dk, device=dev, dtype=torch.float16)
+    vc = torch.zeros_like(kc)
+    return ck, cv, enc_len, prefix, kc, vc

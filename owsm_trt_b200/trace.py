@@ -78,24 +78,20 @@ def main() -> None:
     1B-shaped decoder (seeded weights, the benchmark's synthetic encoder lengths, cache position 100)."""
     import argparse
     import json
-    import sys
-    from pathlib import Path
 
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", type=int, default=0, help="0: cluster kernel where it applies, 1: grid-stage kernel")
     ap.add_argument("--events", type=int, nargs="*", default=[], help="CTAs whose event log to print")
     args = ap.parse_args()
-    sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
-    import bench
     from .decoder import B200Decoder
-    from .synthetic import MEDIUM_1B, decoder_state_dict
+    from .synthetic import MEDIUM_1B, decoder_state_dict, make_workload
 
     d, dev, B = MEDIUM_1B, torch.device("cuda", 0), args.batch
     sd = decoder_state_dict(d, 0, False)
     k = B200Decoder.from_state_dict(sd, d.H, dev)
     k.set_path(args.path)
-    ck, cv, enc_len, prefix, kc, vc = bench.make_workload(d, sd, dev, B, 5)
+    ck, cv, enc_len, prefix, kc, vc = make_workload(d, sd, dev, B, 5)
     tok = prefix[:, -1:].to(dev).contiguous()
     off = torch.full((B,), 100, dtype=torch.long, device=dev)
     logits = torch.zeros(B, 1, d.V, device=dev)

@@ -43,13 +43,16 @@ def _outputs(R, S):
     return logits, new_kv, pred
 
 
-def _two_calls(kern, R, S, Cc, T, static: bool):
-    """Two calls in a row: the second feeds the first's argmax at the next offsets, on the updated cache."""
+def _two_calls(kern, R, S, Cc, T, static: bool, side_stream=None):
+    """Two calls in a row: the second feeds the first's argmax at the next offsets, on the updated cache.
+    side_stream: a torch.cuda.Stream (non-blocking against the legacy stream) to launch the calls on."""
     from owsm_trt_b200 import _lib
 
     lib = _lib.lib()
     tokens, offset, kc, vc, ck, cv = _inputs(R, S, Cc, T, 7)
-    stream = torch.cuda.current_stream(DEV).cuda_stream
+    if side_stream is not None:
+        side_stream.wait_stream(torch.cuda.current_stream(DEV))
+    stream = (side_stream or torch.cuda.current_stream(DEV)).cuda_stream
     plan = None if static else kern._plan(R, S, Cc, T, 1, 0)
     outs = []
     for _ in range(2):
@@ -70,17 +73,39 @@ def _two_calls(kern, R, S, Cc, T, static: bool):
     return outs, kc, vc
 
 
-@pytest.mark.parametrize("R,S", [(1, 1), (2, 3), (8, 1)])
-def test_static_scratch_call_equals_plan_call(kern, R, S):
-    Cc, T = 32, 96
-    ref, kc_ref, vc_ref = _two_calls(kern, R, S, Cc, T, static=False)
-    got, kc_got, vc_got = _two_calls(kern, R, S, Cc, T, static=True)
+def _same(ref, got):
+    (ref, kc_ref, vc_ref), (got, kc_got, vc_got) = ref, got
     for (l0, n0, p0), (l1, n1, p1) in zip(ref, got):
         assert bool(torch.isfinite(l1).all())
         assert torch.equal(l0, l1)
         assert torch.equal(n0, n1)
         assert torch.equal(p0, p1)
     assert torch.equal(kc_ref, kc_got) and torch.equal(vc_ref, vc_got)
+
+
+@pytest.mark.parametrize("R,S", [(1, 1), (2, 3), (8, 1)])
+def test_static_scratch_call_equals_plan_call(kern, R, S):
+    Cc, T = 32, 96
+    _same(_two_calls(kern, R, S, Cc, T, static=False), _two_calls(kern, R, S, Cc, T, static=True))
+
+
+def test_static_scratch_on_a_side_stream(kern):
+    """The first fixed-scratch call of a new shape (its set-up) followed at once by launches on a non-blocking
+    stream: the set-up's uploads must have landed before the kernel reads them."""
+    Cc, T = 40, 80
+    side = torch.cuda.Stream(DEV)
+    ref = _two_calls(kern, 3, 2, Cc, T, static=False)
+    got = _two_calls(kern, 3, 2, Cc, T, static=True, side_stream=side)
+    torch.cuda.synchronize()
+    _same(ref, got)
+
+
+def test_static_scratch_alternating_shapes(kern):
+    """One handle, shapes R = 2 then R = 1 then R = 2 again: each change re-lays the array out."""
+    Cc, T = 32, 96
+    ref = {R: _two_calls(kern, R, 1, Cc, T, static=False) for R in (2, 1)}
+    for R in (2, 1, 2):
+        _same(ref[R], _two_calls(kern, R, 1, Cc, T, static=True))
 
 
 def test_static_scratch_rejects_oversize_calls(kern):

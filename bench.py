@@ -208,11 +208,16 @@ class Greedy:
             enc_len = torch.full_like(enc_len, T_ENC)
         self.ck, self.cv, self.enc_len, self.prefix, self.kc, self.vc = ck, cv, enc_len, prefix, kc, vc
         self.enc_len_d = enc_len.to(dev)
-        lg_p = torch.zeros(B, PREFIX, d.V, device=dev)
-        kv_p = torch.zeros(d.L, 2, B, d.H, PREFIX, d.dk, device=dev, dtype=torch.float16)
-        pr_p = torch.zeros(B, PREFIX, dtype=torch.long, device=dev)
-        zero = torch.zeros(B, dtype=torch.long, device=dev)
-        kern.step_fn(prefix.to(dev), zero, kc, vc, ck, cv, lg_p, kv_p, pred=pr_p, enc_len=self.enc_len_d)()
+        # the prefix in one call, or one position per call where rows x 4 exceeds what a call takes
+        S = PREFIX if B * PREFIX <= kern.max_tokens else 1
+        lg_p = torch.zeros(B, S, d.V, device=dev)
+        kv_p = torch.zeros(d.L, 2, B, d.H, S, d.dk, device=dev, dtype=torch.float16)
+        pr_p = torch.zeros(B, S, dtype=torch.long, device=dev)
+        pre = prefix.to(dev)
+        for p0 in range(0, PREFIX, S):
+            off = torch.full((B,), p0, dtype=torch.long, device=dev)
+            kern.step_fn(pre[:, p0 : p0 + S].contiguous(), off, kc, vc, ck, cv, lg_p, kv_p, pred=pr_p,
+                         enc_len=self.enc_len_d)()  # fmt: skip
         self.tok = pr_p[:, -1:].clone()
         offs = (PREFIX + torch.arange(steps, device=dev))[:, None].expand(steps, B).contiguous()
         self.offs = offs

@@ -167,6 +167,25 @@ int owsm_dec_step_static(OwsmDec* h, void* stream, int R, int S, int C, int T, c
                          const void* cross_k, const void* cross_v, const int32_t* enc_len, float* logits,
                          void* new_kv, int64_t* pred, const uint8_t* notime, int first_time, int last_time);
 
+/* ---- cross-attention keys and values of the encoder output (once per utterance) ----------------------------
+ * Replaces Decoder.cross_kv (src/owsm_trt/modeling.py:490-499) as TorchBackend.encode calls it after the encoder
+ * (src/owsm_trt/runtime.py:63-74): for every layer, enc @ W_k^T + b_k and enc @ W_v^T + b_v, split into heads of
+ * 64, as one tcgen05 GEMM over all layers (fp16 in, fp32 accumulate, fp16 out). */
+typedef struct OwsmXkvLayer {
+  const void *wk, *wv;   /* src_attn.linear_k / linear_v weights [D, D] (weight_dtype) */
+  const float *bk, *bv;  /* their biases [D] (fp32) */
+} OwsmXkvLayer;
+typedef struct OwsmXkv OwsmXkv;
+
+/* Pack the L layers' K/V projections (fp16) on `device`; D = 64 H, L x 2 x D a multiple of 256. */
+int owsm_xkv_create(int L, int D, int H, int weight_dtype, const OwsmXkvLayer* layers, int device, OwsmXkv** out);
+/* enc fp16 [U, T, D] (contiguous) -> cross_k, cross_v fp16 [L, U, H, t_cap, 64] (frames T .. t_cap - 1 untouched);
+ * all three 128-byte aligned. Asynchronous on `stream`; no allocation, capturable in a CUDA graph. */
+int owsm_xkv_run(OwsmXkv* x, void* stream, const void* enc, int U, int T, int t_cap, void* cross_k, void* cross_v);
+/* Read and clear the error word of the handle's runs (synchronises): OWSM_DEC_OK or OWSM_DEC_ERR_TIMEOUT. */
+int owsm_xkv_get_error(OwsmXkv* x);
+void owsm_xkv_destroy(OwsmXkv* x);
+
 /* Last CUDA / argument error message of this thread ("" if none). */
 const char* owsm_dec_last_error(void);
 

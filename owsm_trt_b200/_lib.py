@@ -27,6 +27,10 @@ class Layer(C.Structure):
                                   "w1", "b1", "w2", "b2", "ln1_g", "ln1_b", "ln2_g", "ln2_b", "ln3_g", "ln3_b")]  # fmt: skip
 
 
+class XkvLayer(C.Structure):
+    _fields_ = [("wk", vp), ("wv", vp), ("bk", vp), ("bv", vp)]
+
+
 class Weights(C.Structure):
     _fields_ = [("weight_dtype", i32), ("emb", vp), ("pe", vp), ("layers", C.POINTER(Layer)), ("lnf_g", vp),
                 ("lnf_b", vp), ("wout", vp), ("bout", vp)]  # fmt: skip
@@ -51,6 +55,10 @@ SIGNATURES = {
     "owsm_dec_step_static": (i32, [vp, vp, i32, i32, i32, i32, vp, i64, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp,
                                    i32, i32]),  # fmt: skip
     "owsm_dec_last_error": (C.c_char_p, []),
+    "owsm_xkv_create": (i32, [i32, i32, i32, i32, C.POINTER(XkvLayer), i32, C.POINTER(vp)]),
+    "owsm_xkv_run": (i32, [vp, vp, vp, i32, i32, i32, vp, vp]),
+    "owsm_xkv_get_error": (i32, [vp]),
+    "owsm_xkv_destroy": (None, [vp]),
 }
 
 _lib = None

@@ -672,8 +672,7 @@ __device__ void cl_ln_rows(const PlanDev& pd, const long long* x, int m0, int M,
   // a token's fragments: per k-block 32 contiguous bytes, k-blocks NT * 256 bytes apart
   const uint32_t b_s = smem_u32(bbuf), xb_s = smem_u32(xb);
   const int per_row = D / 8;  // 16-byte pieces of a token
-  // (a failed call sends nothing more: a peer that gave up waiting may be past the point of receiving)
-  for (int i = threadIdx.x; !ring.dead && i < (r1 - r0) * per_row; i += NTHR) {
+  for (int i = threadIdx.x; i < (r1 - r0) * per_row; i += NTHR) {
     const int m = r0 + i / per_row, c = i % per_row;
     const uint32_t off = (uint32_t)((((c >> 1) * NT + (m >> 3)) * 32 + (m & 7) * 4) * 8 + (c & 1) * 16);
     const uint4 v = lds128_u32(b_s + off);
@@ -754,7 +753,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
 #pragma unroll
     for (int q = 1; q < CS; ++q) {
       const uint32_t dst = (uint32_t)((r + q) % CS);
-      if (!ring.dead) st_async_v4(mapa_shared(xq_s + idx * 4, dst), w, mapa_shared(bar0_s, dst));
+      st_async_v4(mapa_shared(xq_s + idx * 4, dst), w, mapa_shared(bar0_s, dst));
     }
     if (kind == 1 && row >= DK) {
       const int mg = cl.m0 + m, b = mg / S, s = mg % S, kv = (row - DK) / DK, d = (row - DK) % DK;
@@ -805,7 +804,7 @@ __device__ void cl_attn_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, 
 #pragma unroll
       for (int i = 1; i < CS; ++i) {
         const uint32_t dst = (uint32_t)((r + i) % CS);
-        if (!ring.dead) st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
+        st_async_v4(mapa_shared(part_s + off * 4, dst), w, mapa_shared(bar1_s, dst));
       }
     });
     event(cx, 54);
@@ -893,7 +892,7 @@ __device__ void cl_ffn_stage(const PlanDev& pd, Ring& ring, const Ctx& cx, const
   event(cx, 61);
   const uint32_t mine_s = smem_u32(hb) + (uint32_t)r * my_bytes;
   const uint32_t bar0 = smem_u32(&xbar[0]);
-  for (int i = threadIdx.x; !ring.dead && i < (int)(my_bytes / 16); i += NTHR) {
+  for (int i = threadIdx.x; i < (int)(my_bytes / 16); i += NTHR) {
     const uint4 v = lds128_u32(mine_s + i * 16);
 #pragma unroll
     for (int q = 1; q < CS; ++q) {
@@ -1173,7 +1172,11 @@ __global__ void __launch_bounds__(BLOCK, 1)
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, ring_i, pd.max_spin, pd.err, dead, 0ull, pd.ts != nullptr};
-    if (g == 0) {
+    // A failed call (this CTA's or another's timed-out wait, known to every thread of the CTA from the last grid
+    // barrier) runs no further stage: no exchange barrier is armed again while one of its phases may still be
+    // open, and no exchange is sent. Inside a live stage every sender sends, so each phase armed there completes.
+    if (dead) {
+    } else if (g == 0) {
       cl_embed(pd, a, cx, c);
     } else if (g < n_out) {
       const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;

@@ -362,9 +362,9 @@ __device__ void grid_sync(const PlanDev& pd, uint32_t target, bool& dead, int* s
           break;
         }
       }
-    } else {
-      dead = true;
     }
+    // any CTA's failure: its error word was set before its arrival, so after the acquiring poll it is visible
+    if (*(volatile int*)pd.err) dead = true;
     if (sdead) *sdead = dead ? 1 : 0;
   }
   csync();
@@ -1823,6 +1823,11 @@ struct DevBuf {
 };
 
 }  // namespace
+
+namespace owsm {
+// The library's last-error record for the other translation units (the K/V projection).
+int record_error(int code, const std::string& msg) { return fail(code, msg); }
+}  // namespace owsm
 
 static std::atomic<uint64_t> g_handle_serial{0};
 

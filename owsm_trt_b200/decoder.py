@@ -44,6 +44,7 @@ class B200Decoder:
 
     name = "b200-megakernel"
     argmax = True  # step_fn takes pred
+    max_tokens = 64  # rows x window of one call (MegaBackend's max_tokens for this kernel)
     solo_differs = False  # a single-row call is the same call with or without an encoder alongside
 
     @torch.no_grad()
@@ -116,6 +117,8 @@ class B200Decoder:
                        "owsm_dec_create")  # fmt: skip
         del keep
         self._h = h
+        self._xkv = None  # the K/V projection handle, made on first use (cross_kv_fn)
+        self._xkv_src = {k: v for k, v in sd.items() if ".src_attn.linear_k." in k or ".src_attn.linear_v." in k}
         self._plans: dict[tuple, C.c_void_p] = {}
         self.programs = self._plan_info(self._plan(1, 1, 16, 16, 1, 0))[0]
         self.max_pos = pe.shape[0]
@@ -137,6 +140,9 @@ class B200Decoder:
         return a.value, b.value, c.value
 
     def close(self) -> None:
+        if getattr(self, "_xkv", None):
+            _lib.lib().owsm_xkv_destroy(self._xkv)
+            self._xkv = None
         if getattr(self, "_h", None):
             lib = _lib.lib()
             for p in self._plans.values():
@@ -181,6 +187,64 @@ class B200Decoder:
         """Testing hook: the in-kernel wait limit of later calls (0: the default)."""
         _lib.check(_lib.lib().owsm_dec_set_max_spin(self._h, polls), "owsm_dec_set_max_spin")
 
+    # ------------------------------------------------------------------ cross K/V
+    def _xkv_handle(self):
+        if self._xkv is None:
+            keep = []
+
+            def dev(t, dt=torch.float32):
+                t = t.detach().to(device=self.device, dtype=dt).contiguous()
+                keep.append(t)
+                return t.data_ptr()
+
+            layers = (_lib.XkvLayer * self.L)()
+            for i in range(self.L):
+                p = f"decoders.{i}.src_attn."
+                ly = layers[i]
+                ly.wk, ly.wv = dev(self._xkv_src[p + "linear_k.weight"]), dev(self._xkv_src[p + "linear_v.weight"])
+                ly.bk, ly.bv = dev(self._xkv_src[p + "linear_k.bias"]), dev(self._xkv_src[p + "linear_v.bias"])
+            h = C.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.check(_lib.lib().owsm_xkv_create(self.L, self.D, self.H, _lib.F32, layers, self.device.index or 0,
+                                                      C.byref(h)), "owsm_xkv_create")  # fmt: skip
+            self._xkv = h
+        return self._xkv
+
+    def cross_kv_fn(self, enc: torch.Tensor, cross_k: torch.Tensor, cross_v: torch.Tensor):
+        """Every layer's cross-attention keys / values of encoder output ``enc`` [U, T, D] (fp16) into ``cross_k`` /
+        ``cross_v`` [L, U, H, T', 64] (fp16, T' >= T; frames T.. untouched): ``Decoder.cross_kv``
+        (src/owsm_trt/modeling.py:490-499) as one tcgen05 GEMM. Returns a graph-capturable ``run()``."""
+        U, T, D = enc.shape
+        if enc.dtype != torch.float16 or not enc.is_contiguous() or D != self.D:
+            raise TypeError(f"enc must be contiguous fp16 [U, T, {self.D}]")
+        for t in (cross_k, cross_v):
+            if t.dtype != torch.float16 or not t.is_contiguous() or t.shape[:3] != (self.L, U, self.H) or t.shape[4] != 64:
+                raise TypeError(f"cross_k / cross_v must be contiguous fp16 [{self.L}, {U}, {self.H}, T', 64]")
+        t_cap = cross_k.shape[3]
+        if t_cap < T or cross_v.shape != cross_k.shape:
+            raise ValueError("cross_k / cross_v need at least T frames")
+        h = self._xkv_handle()
+        fn, dev = _lib.lib().owsm_xkv_run, self.device
+
+        def run() -> None:
+            _lib.check(fn(h, torch.cuda.current_stream(dev).cuda_stream, enc.data_ptr(), U, T, t_cap,
+                          cross_k.data_ptr(), cross_v.data_ptr()), "owsm_xkv_run")  # fmt: skip
+
+        run.buffers = (enc, cross_k, cross_v)
+        return run
+
+    def cross_kv(self, enc: torch.Tensor) -> torch.Tensor:
+        """``Decoder.cross_kv`` with its return layout: [L, 2, U, H, T, 64] fp16 (allocates)."""
+        U, T, _ = enc.shape
+        kv = torch.empty(2, self.L, U, self.H, T, 64, device=self.device, dtype=torch.float16)
+        self.cross_kv_fn(enc.to(self.device, torch.float16).contiguous(), kv[0], kv[1])()
+        return kv.transpose(0, 1)
+
+    def check_cross_kv(self) -> None:
+        """Raise if a bounded wait of an earlier K/V projection gave up."""
+        if self._xkv is not None and _lib.lib().owsm_xkv_get_error(self._xkv) != _lib.OK:
+            raise RuntimeError("the K/V projection kernel timed out")
+
     # ------------------------------------------------------------------ calls
     def _validate(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G):
         R, S = tokens.shape
@@ -221,8 +285,13 @@ class B200Decoder:
         ntm, ft, lt = None, 0, -1
         if notime is not None and pred is not None:
             flags, ft, lt = notime
-            ntm = flags.to(torch.uint8) if flags.dtype != torch.uint8 else flags
-            ntm = ntm.contiguous()
+            # the kernel reads the caller's flags at every run (sessions set them in place after building their
+            # calls, runtime.py:579-584): one byte per row, bool or uint8, no copy
+            if flags.dtype not in (torch.bool, torch.uint8) or not flags.is_contiguous() or flags.shape != (R,):
+                raise TypeError("notime flags must be a contiguous bool or uint8 tensor [R]")
+            if flags.device != self.device:
+                raise ValueError(f"notime flags must be on {self.device}")
+            ntm = flags
         if enc_len is not None:
             if enc_len.dtype != torch.int32 or enc_len.numel() != R // G:
                 raise ValueError("enc_len must be int32 [R / rows_per_utt]")

@@ -11,7 +11,7 @@ ROOT = Path(__file__).resolve().parents[1]
 
 def declared() -> set[str]:
     text = (ROOT / "include" / "owsm_dec.h").read_text()
-    return set(re.findall(r"\b(owsm_dec_\w+)\s*\(", text))
+    return set(re.findall(r"\b(owsm_(?:dec|xkv)_\w+)\s*\(", text))
 
 
 @pytest.fixture(scope="module")
@@ -54,3 +54,17 @@ def test_error_codes_without_gpu(lib):
     assert lib.owsm_dec_create(C.byref(dims), C.byref(w), 0, 0, C.byref(out)) == _lib.ERR_LIMIT
     assert lib.owsm_dec_plan(None, 1, 1, 1, 1, 1, 0, C.byref(out)) == _lib.ERR_ARG
     assert lib.owsm_dec_get_error(None) == _lib.ERR_ARG
+
+
+def test_cross_kv_error_codes_without_gpu(lib):
+    """The K/V projection's argument checks run before any CUDA call."""
+    import ctypes as C
+
+    from owsm_trt_b200 import _lib
+
+    out = C.c_void_p()
+    assert lib.owsm_xkv_create(2, 256, 4, _lib.F32, None, 0, C.byref(out)) == _lib.ERR_ARG
+    layers = (_lib.XkvLayer * 2)()
+    assert lib.owsm_xkv_create(2, 100, 2, _lib.F32, layers, 0, C.byref(out)) == _lib.ERR_LIMIT  # heads of 50
+    assert lib.owsm_xkv_run(None, None, None, 1, 1, 1, None, None) == _lib.ERR_ARG
+    assert lib.owsm_xkv_get_error(None) == _lib.ERR_ARG

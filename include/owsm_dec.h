@@ -132,13 +132,15 @@ int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps);
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call);
 
 /* Which kernel later plans of this handle use (no counterpart in owsm-trt, which picks its kernel by GPU):
- * 0 (default) the cluster kernel where the call shape allows it (greedy, at most 16 tokens), else the
- * grid-stage kernel; 1 always the grid-stage kernel; 2 the cluster kernel, owsm_dec_plan failing with
- * OWSM_DEC_ERR_LIMIT where it does not apply. Existing plans keep their kernel. */
+ * 0 (default) the dense kernel (tcgen05 tensor-core GEMMs) for greedy calls of more than 32 tokens -- one launch
+ * up to 64 tokens, row slices of up to 64 tokens each beyond --, the cluster kernel where the call shape allows
+ * it (at most 16 tokens, or row slices of it up to 32), else the grid-stage kernel; 1 always the grid-stage
+ * kernel; 2 the cluster kernel; 3 the dense kernel; with 2 and 3 owsm_dec_plan fails with OWSM_DEC_ERR_LIMIT
+ * where the kernel does not apply. Existing plans keep their kernel. */
 int owsm_dec_set_path(OwsmDec* h, int path);
 
 /* The kernel a plan runs: 1 the grid-stage kernel (eight grid-wide stages per layer), 2 the cluster
- * kernel (three per layer). */
+ * kernel (three per layer), 3 the dense kernel (eight per layer, tcgen05 GEMMs). */
 int owsm_dec_plan_kernel(const OwsmDecPlan* p);
 
 /* Kernel launches of one call of the plan: 1, or the number of row slices a call of more than 16 tokens is cut

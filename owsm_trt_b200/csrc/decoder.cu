@@ -104,6 +104,15 @@ struct PlanDev {
   int Rs, Us;               // cluster kernel: rows / utterances of the caller's buffers (layer strides of the
                             // caches, new_kv and cross K/V), more than R / U when the call is a row slice
   long long* xf[3];         // cluster kernel: rotating fixed-point residual buffers [M][D]
+  // dense kernel (calls of 33 to 64 tokens; tcgen05 GEMMs)
+  int dense;
+  const __half* gt[NGEMM];  // weights in 128-row tiles [layer][tile][K / 64][128 x 64] (canonical K-major)
+  long long gtl[NGEMM];     // halves per layer
+  int nsplit[NGEMM];        // K ranges per tile
+  float* part;              // partial sums of split tiles [tile][range][64 tokens][128 rows]
+  uint32_t* tcnt;           // ranges arrived per tile (the last one resets it)
+  __half* obuf;             // attention output in the token-operand layout [D / 8][8][64] halves
+  __half* hbuf;             // FFN hidden in the token-operand layout [F / 8][8][64] halves
 };
 
 struct CallArgs {
@@ -1796,6 +1805,7 @@ __global__ void place_bias_kernel(const float* __restrict__ b, int N, uint4* __r
 }  // namespace owsm
 
 #include "cluster.cuh"
+#include "dense.cuh"
 
 // ================================================================================================ host / C ABI
 using namespace owsm;
@@ -1843,7 +1853,10 @@ struct OwsmDec {
   float* pe = nullptr;
   int* err = nullptr;  // device error word
   uint32_t max_spin = DEFAULT_SPIN;
-  int path = 0;  // 0: cluster kernel where it applies, 1: always the grid-stage kernel, 2: cluster kernel or fail
+  int path = 0;  // 0: cluster kernel where it applies, 1: always the grid-stage kernel, 2: cluster kernel or fail,
+                 // 3: dense kernel or fail
+  __half* gt[NGEMM] = {};  // weights in 128-row tiles for the dense kernel (made by its first plan)
+  long long gtl[NGEMM] = {};
   // Profiling aid: with OWSM_DEC_NO_COOP set when the handle is made, cluster-kernel calls are launched
   // without the cooperative attribute (the profiler rejects cooperative cluster launches). The grid-wide
   // barrier then relies on all CTAs being resident, which holds when the call runs alone (one CTA per SM,
@@ -1869,6 +1882,7 @@ struct OwsmDecPlan {
   // cluster-kernel launch each on the same stream (first row of each)
   std::vector<OwsmDecPlan*> subs;
   std::vector<int> sub_r0;
+  size_t tcnt_bytes = 0;  // dense kernel: the per-tile arrival counters (reset after a failed call)
   ~OwsmDecPlan() {
     for (OwsmDecPlan* q : subs) delete q;
     int cur = 0;
@@ -1984,7 +1998,12 @@ KernelFn cl_kernel_for(int NT, int Qmax, bool beam, bool wide) {
   return NT == 1 ? decoder_cl_kernel<1, CLQ, false, false> : decoder_cl_kernel<2, CLQ, false, false>;
 }
 
+KernelFn dense_kernel_for(int Qmax) {
+  return Qmax == 1 ? decoder_dense_kernel<1, true> : decoder_dense_kernel<CLQ, false>;
+}
+
 KernelFn plan_kernel(const PlanDev& pd) {
+  if (pd.dense) return dense_kernel_for(pd.Qmax);
   return pd.cl ? cl_kernel_for(pd.NT, pd.Qmax, pd.beam > 0, pd.wide != 0) : kernel_for(pd.NT);
 }
 
@@ -2311,11 +2330,186 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   return OWSM_DEC_OK;
 }
 
+// The handle's weights in 128-row tiles (from its fragment packing, on the device), once per handle.
+static int make_tiles(OwsmDec* h) {
+  if (h->gt[0]) return OWSM_DEC_OK;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const GemmW& gw = h->g[gi];
+    const int layers = gi == G_OUT ? 1 : h->dims.L;
+    const long long per = (long long)((gw.N + DN_TILE - 1) / DN_TILE) * DN_TILE * gw.K;
+    __half* t = nullptr;
+    int rc = dev_alloc(h->allocs, &t, (size_t)per * layers);
+    if (rc) return rc;
+    tile_pack_kernel<<<1024, 256>>>(gw.w, gw.N, gw.K, gw.bstride, gw.lstride, layers, t, per);
+    CUDA_TRY(cudaGetLastError());
+    h->gt[gi] = t;
+    h->gtl[gi] = per;
+  }
+  CUDA_TRY(cudaDeviceSynchronize());
+  return OWSM_DEC_OK;
+}
+
+// The plan of a greedy call of up to 64 tokens on the dense kernel.
+static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan** out) {
+  if (!h || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
+  *out = nullptr;
+  const OwsmDecDims& d = h->dims;
+  if (R < 1 || S < 1 || C < S || T < 1 || G < 1 || R % G) return fail(OWSM_DEC_ERR_ARG, "bad call shape");
+  const int M = R * S, U = R / G, Q = G * S;
+  if (M > DN_TOK) return fail(OWSM_DEC_ERR_LIMIT, "the dense kernel takes at most 64 tokens per launch");
+  if (Q > CLQ) return fail(OWSM_DEC_ERR_LIMIT, "the dense kernel takes at most 16 queries per utterance");
+  if (U > 1024) return fail(OWSM_DEC_ERR_LIMIT, "at most 1024 utterances");
+  DeviceGuard guard(h->device);
+  int rc = make_tiles(h);
+  if (rc) return rc;
+  OwsmDecPlan* p = new OwsmDecPlan();
+  p->h = h;
+  auto bail = [&](int code) {
+    delete p;
+    return code;
+  };
+  PlanDev& pd = p->pd;
+  pd.L = d.L; pd.D = d.D; pd.H = d.H; pd.F = d.F; pd.V = d.V; pd.max_pos = d.max_pos;
+  pd.eps = d.eps; pd.xscale = d.xscale;
+  pd.R = R; pd.S = S; pd.M = M; pd.NT = DN_MT; pd.C = C; pd.T = T; pd.G = G; pd.U = U; pd.beam = 0;
+  pd.Rs = R; pd.Us = U;
+  pd.P = h->programs;
+  pd.max_spin = h->max_spin;
+  pd.emb = h->emb;
+  pd.pe = h->pe;
+  pd.err = h->err;
+  pd.Qmax = std::max(S, Q);
+  pd.dense = 1;
+  const int P = pd.P;
+  int max_tiles_split = 0, max_tiles = 0;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    pd.g[gi] = h->g[gi];
+    pd.gt[gi] = h->gt[gi];
+    pd.gtl[gi] = h->gtl[gi];
+    pd.nsplit[gi] = dn_splits(h->g[gi].K);
+    const int nt = (h->g[gi].N + DN_TILE - 1) / DN_TILE;
+    max_tiles = std::max(max_tiles, nt);
+    if (pd.nsplit[gi] > 1) max_tiles_split = std::max(max_tiles_split, nt * pd.nsplit[gi]);
+  }
+  // work items (tile, K range): the six layer GEMMs on consecutive CTA ranges (a CTA's items of one layer are
+  // in different stages, so its ring streams them back to back), the output layer over all CTAs
+  std::vector<std::vector<int>> per[NGEMM];
+  for (int gi = 0; gi < NGEMM; ++gi) per[gi].assign(P, {});
+  int base = 0;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const int n = ((h->g[gi].N + DN_TILE - 1) / DN_TILE) * pd.nsplit[gi];
+    for (int j = 0; j < n; ++j) per[gi][(gi == G_OUT ? j : base + j) % P].push_back(j);
+    if (gi != G_OUT) base = (base + n) % P;
+  }
+  int64_t* tot = &p->scratch_bytes;
+  size_t max_items = 0;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    std::vector<int> off(P + 1, 0), blk;
+    for (int c = 0; c < P; ++c) {
+      off[c + 1] = off[c] + (int)per[gi][c].size();
+      blk.insert(blk.end(), per[gi][c].begin(), per[gi][c].end());
+    }
+    int *o, *b;
+    if ((rc = dev_alloc(p->allocs, &o, off.size(), tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &b, std::max<size_t>(blk.size(), 1), tot))) return bail(rc);
+    CUDA_TRY(cudaMemcpy(o, off.data(), off.size() * 4, cudaMemcpyHostToDevice));
+    if (!blk.empty()) CUDA_TRY(cudaMemcpy(b, blk.data(), blk.size() * 4, cudaMemcpyHostToDevice));
+    pd.goff[gi] = o;
+    pd.gblk[gi] = b;
+  }
+  for (int c = 0; c < P; ++c) {
+    size_t n = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) n += per[gi][c].size();
+    max_items = std::max(max_items, n);
+  }
+  const int D = d.D, F = d.F;
+  if ((rc = dev_alloc(p->allocs, &pd.x, (size_t)M * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.qkv, (size_t)M * 3 * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.obuf, (size_t)D * DN_TOK, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.hbuf, (size_t)F * DN_TOK, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.part, (size_t)std::max(max_tiles_split, 1) * DN_TOK * DN_TILE, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.tcnt, (size_t)max_tiles, tot))) return bail(rc);
+  p->tcnt_bytes = (size_t)max_tiles * sizeof(uint32_t);
+  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);
+  // shared memory: barriers | utterance prefix sums + flags | work items | row offsets | argmax state | ring | work
+  int maxkr = 0;
+  for (int gi = 0; gi < NGEMM; ++gi) maxkr = std::max(maxkr, h->g[gi].K / pd.nsplit[gi]);
+  const size_t off_pre = 256;
+  const size_t off_sched = (off_pre + 4 * 1072 + 127) & ~(size_t)127;
+  const size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_items) + 127) & ~(size_t)127;
+  const size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
+  const size_t off_ring = (off_out + out_smem(M, false) + 1023) & ~(size_t)1023;
+  size_t work = (size_t)DN_TOK * maxkr * 2;
+  work = std::max(work, ((attn_smem(pd.Qmax) + 15) & ~(size_t)15) + sizeof(float) * (size_t)pd.Qmax * XPS);
+  work = std::max(work, sizeof(float) * 2 * (size_t)P * M);  // the argmax partials of all CTAs
+  cudaDeviceProp prop;
+  CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
+  const size_t limit = prop.sharedMemPerBlockOptin;
+  if (off_ring + work + 2 * (SLOT + 128) > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small for the dense kernel"));
+  const int nslot = (int)std::min<size_t>((limit - off_ring - work) / (SLOT + 128), 6);
+  pd.nslot = nslot;
+  pd.slot = SLOT;
+  pd.apos = SLOT / (DK * 2);
+  pd.off_pre = (int)off_pre;
+  pd.off_sched = (int)off_sched;
+  pd.off_rows = (int)off_rows;
+  pd.inflight = nslot;  // every slot may be in flight: a work item streams 128 KB of weights
+  pd.off_out = (int)off_out;
+  pd.off_ring = (int)off_ring;
+  pd.sstride = SLOT + 128;
+  pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);
+  pd.work_bytes = (int)work;
+  p->smem = (size_t)pd.off_work + work;
+  CUDA_TRY(cudaFuncSetAttribute(plan_kernel(pd), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)limit));
+  int per_sm = 0;
+  CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, plan_kernel(pd), BLOCK, p->smem));
+  if (per_sm < 1) return bail(fail(OWSM_DEC_ERR_LIMIT, "the dense kernel does not fit an SM"));
+  CUDA_TRY(cudaDeviceSynchronize());  // the table uploads, before calls on any stream
+  *out = p;
+  return OWSM_DEC_OK;
+}
+
 extern "C" {
 
 int owsm_dec_plan(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, int beam, OwsmDecPlan** out) {
   if (!h || !out) return fail(OWSM_DEC_ERR_ARG, "null argument");
   const int G = rows_per_utt < 1 ? 1 : rows_per_utt;
+  // greedy calls of more than 32 tokens (or any, with path 3): the dense kernel (tcgen05 GEMMs), one launch for
+  // up to 64 tokens, consecutive row slices of whole utterances of up to 64 tokens each beyond
+  if (((h->path == 0 && R * S > 32) || h->path == 3) && !beam && R >= 1 && S >= 1 && R % G == 0 && G * S <= CLQ) {
+    int rc = OWSM_DEC_OK;
+    if (R * S <= DN_TOK) {
+      rc = plan_dense(h, R, S, C, T, G, out);
+    } else {
+      const int per = (DN_TOK / (S * G)) * G;  // rows per slice
+      OwsmDecPlan* p = new OwsmDecPlan();
+      p->h = h;
+      for (int r0 = 0; r0 < R && rc == OWSM_DEC_OK; r0 += per) {
+        OwsmDecPlan* q = nullptr;
+        rc = plan_dense(h, std::min(per, R - r0), S, C, T, G, &q);
+        if (rc == OWSM_DEC_OK) {
+          q->pd.Rs = R;
+          q->pd.Us = R / G;
+          p->subs.push_back(q);
+          p->sub_r0.push_back(r0);
+          p->scratch_bytes += q->scratch_bytes;
+        }
+      }
+      if (rc == OWSM_DEC_OK) {
+        p->pd = p->subs[0]->pd;
+        p->pd.R = R;
+        p->pd.M = R * S;
+        *out = p;
+      } else {
+        delete p;
+      }
+    }
+    if (rc == OWSM_DEC_OK || h->path == 3) return rc;
+  }
   // more than 16 tokens, greedy: row slices of whole utterances on the cluster kernel (each slice <= 16
   // tokens), launched one after another; the grid-stage kernel if that cannot be laid out
   if (h->path != 1 && !beam && R >= 1 && S >= 1 && R * S > 16 && R * S <= MAXNT * 8 && R % G == 0 && G * S <= 16) {
@@ -2462,6 +2656,7 @@ int owsm_dec_plan_reset(OwsmDecPlan* p) {
   CUDA_TRY(cudaDeviceSynchronize());
   CUDA_TRY(cudaMemset(p->pd.ctr, 0, 8 * sizeof(uint32_t)));
   CUDA_TRY(cudaMemset(p->pd.xcnt, 0, (size_t)p->pd.U * p->pd.H * sizeof(uint32_t)));
+  if (p->tcnt_bytes) CUDA_TRY(cudaMemset(p->pd.tcnt, 0, p->tcnt_bytes));
   return OWSM_DEC_OK;
 }
 
@@ -2488,14 +2683,14 @@ int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
 
 int owsm_dec_set_path(OwsmDec* h, int path) {
   if (!h) return fail(OWSM_DEC_ERR_ARG, "null handle");
-  if (path < 0 || path > 2) return fail(OWSM_DEC_ERR_ARG, "path must be 0, 1 or 2");
+  if (path < 0 || path > 3) return fail(OWSM_DEC_ERR_ARG, "path must be 0, 1, 2 or 3");
   h->path = path;
   return OWSM_DEC_OK;
 }
 
 int owsm_dec_plan_kernel(const OwsmDecPlan* p) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
-  return p->pd.cl ? 2 : 1;
+  return p->pd.dense ? 3 : (p->pd.cl ? 2 : 1);
 }
 
 int owsm_dec_plan_launches(const OwsmDecPlan* p) {

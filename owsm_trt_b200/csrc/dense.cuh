@@ -1,0 +1,631 @@
+// The dense kernel: decoder calls of 33 to 64 tokens (rows x window), where the layer GEMMs are dense enough for
+// the fifth-generation tensor cores. Included by decoder.cu after cluster.cuh (it uses the ring, the attention
+// units of the cluster kernel, the embedding and argmax stages of the grid-stage kernel).
+//
+// Stages (one grid barrier after each): embedding; per layer QKV (LN1 folded), self-attention, out-projection
+// + residual, cross-Q (LN2), cross-attention, cross-out + residual, FFN1 (LN3) + ReLU, FFN2 + residual; the
+// vocabulary projection (final LN) with the fused argmax.
+//
+// GEMMs y[token, n] = sum_k W[n, k] x[token, k] run swap-AB on tcgen05: the weights are the M = 128 operand
+// (a tile of 128 output rows), the call's tokens (padded to 64) the N = 64 operand, the fp32 accumulator
+// 128 TMEM lanes x 64 columns. A work item is (tile, K range): the weights of the range stream through the
+// ring as 16 KB chunks (128 rows x 64 k) prepacked in the canonical K-major layout (core matrices of 8 rows x 8
+// k, 128 contiguous bytes; k groups 2 KB apart, row groups 128 bytes apart), so a bulk copy lands them ready for
+// the MMA; the token operand (the range of the normalised residual rows, or of the attention / FFN output) sits
+// in shared memory in the same layout (k groups 8 x 128 bytes apart). One thread issues the MMAs; a finished
+// ring slot is handed back by tcgen05.commit; the item's accumulator is read by warps 0-3 (one TMEM lane
+// quarter each: a thread owns one output row and its 64 token columns).
+// A tile whose K is split writes each range's partial sums to global memory; the last range to arrive (counted
+// per tile) adds them up in range order -- the result does not depend on the arrival order -- and applies the
+// epilogue (bias, residual add, ReLU, fp16 stores, logits and argmax).
+// Attention: a unit is a (row, head) of self-attention or an (utterance, head) of cross-attention with all of its
+// positions, so no unit is split across CTAs; its warps step through the positions in parallel (attn_unit) and the
+// normalised output goes to the next GEMM's operand layout in global memory.
+
+#pragma once
+#include "tc.cuh"
+
+namespace owsm {
+
+constexpr int DN_MT = 8;                 // token groups of 8: up to 64 tokens
+constexpr int DN_TOK = DN_MT * 8;
+constexpr int DN_TILE = 128;             // weight rows per tile
+constexpr int DN_KR = 512;               // largest K range of a work item (B operand: 64 tokens x 512 fp16 = 64 KB)
+constexpr int DN_CHUNK = DN_TILE * 64 * 2;  // bytes of a 128 x 64 weight chunk
+constexpr int DN_BBYTES = DN_TOK * DN_KR * 2;
+
+// K splits of a GEMM: ranges of at most DN_KR features, each a multiple of 64.
+__host__ __device__ constexpr int dn_splits(int K) {
+  int n = (K + DN_KR - 1) / DN_KR;
+  while (K % n || (K / n) % 64) ++n;
+  return n;
+}
+
+// Index (halves) of element (token m, feature k) in the token-operand layout with DN_MT token groups: k groups of
+// DN_MT core matrices, a core matrix 8 tokens x 8 features, a token's 8 features contiguous.
+__device__ __forceinline__ int dn_bidx(int m, int k) {
+  return (((k >> 3) * DN_MT + (m >> 3)) << 6) + ((m & 7) << 3) + (k & 7);
+}
+
+// LayerNorm of the residual rows (fp32 [M][D]) into the token operand of features [k0, k0 + kr): the
+// statistics over the whole row (sum and sum of squares in fp64, one pass), padding tokens zero. A warp
+// normalises two rows at a time with all their loads issued together.
+__device__ __noinline__ void dn_ln(const PlanDev& pd, int k0, int kr, __half* bbuf) {
+  const int D = pd.D, M = pd.M, nv = D >> 7;  // float4 per lane per row (D <= 1024)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int m0 = warp * 2; m0 < DN_TOK; m0 += NWARP * 2) {
+    float4 v[2][MAXV4];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i < nv) v[r][i] = (m0 + r < M) ? __ldcg(reinterpret_cast<const float4*>(pd.x + (size_t)(m0 + r) * D) + lane + 32 * i)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int m = m0 + r;
+      double s1 = 0.0, s2 = 0.0;
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i)
+        if (i < nv) {
+          const float4 u = v[r][i];
+          s1 += ((double)u.x + (double)u.y) + ((double)u.z + (double)u.w);
+          s2 = fma((double)u.x, (double)u.x, s2);
+          s2 = fma((double)u.y, (double)u.y, s2);
+          s2 = fma((double)u.z, (double)u.z, s2);
+          s2 = fma((double)u.w, (double)u.w, s2);
+        }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      const double mean = s1 / D, var = fmax(s2 / D - mean * mean, 0.0);
+      const float fm = (float)mean, rs = (float)(1.0 / sqrt(var + (double)pd.eps));
+#pragma unroll
+      for (int i = 0; i < MAXV4; ++i) {
+        const int k = 4 * (lane + 32 * i);
+        if (i < nv && k >= k0 && k < k0 + kr) {
+          const float4 u = v[r][i];
+          uint2 h;
+          if (m < M) {
+            h.x = pack_half2((u.x - fm) * rs, (u.y - fm) * rs);
+            h.y = pack_half2((u.z - fm) * rs, (u.w - fm) * rs);
+          } else {
+            h.x = h.y = 0u;
+          }
+          *reinterpret_cast<uint2*>(bbuf + dn_bidx(m, k - k0)) = h;
+        }
+      }
+    }
+  }
+  fence_async_smem();  // the operand is read by the tensor cores (async proxy)
+}
+
+// The token operand of features [k0, k0 + kr) from a global buffer in the same layout (attention output, FFN
+// hidden): one bulk copy of the contiguous range, issued and awaited by thread 0 (the MMA issuer).
+__device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int kr, __half* bbuf, uint64_t* bar,
+                                              uint32_t& ph, uint32_t spin) {
+  // the source was written by other CTAs' ordinary stores before the grid barrier: order them before the
+  // bulk-copy engine's reads
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  const uint32_t bytes = (uint32_t)kr * DN_TOK * 2;
+  mbar_arrive_expect_tx(bar, bytes);
+  bulk_g2s_nohint(bbuf, src + (size_t)(k0 >> 3) * DN_MT * 64, bytes, bar);
+  const bool ok = mbar_wait(bar, ph, spin);
+  ph ^= 1u;
+  return ok;
+}
+
+// One GEMM stage of the dense kernel on this CTA: its work items (tile, K range) in schedule order.
+// stage(k0, kr) fills the token operand with features [k0, k0 + kr) (every consumer thread calls it; thread 0
+// only issues the MMAs, after it returns); epi(n, m0, v) finishes output row n of a tile for tokens m0 .. m0 + 31
+// from their complete sums v (warps 0-3, one row per thread, called by the CTA that completes the tile).
+template <class Stage, class Epi>
+__device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, uint64_t* accbar,
+                        uint32_t& accn, uint32_t& issued, __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
+  const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
+  if (nb0 == nb1) return;
+  const int K = pd.g[gi].K, ns = pd.nsplit[gi], kr = K / ns, nchunk = kr >> 6, nslot = (nchunk + 1) >> 1;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int staged = -1;
+  for (int i = nb0; i < nb1; ++i) {
+    const int item = cx.sb[i], tile = item / ns, split = item - tile * ns, k0 = split * kr;
+    if (k0 != staged) {  // (the previous item's MMAs, which read the operand, are complete: its accumulator was)
+      stage(k0, kr);
+      csync();
+      staged = k0;
+    }
+    // (a failed call issues nothing more, so at most the last commit is outstanding when the CTA leaves)
+    if (threadIdx.x == 0 && !ring.dead) {
+      constexpr uint32_t idesc = idesc_f16_f32(DN_TILE, DN_TOK);
+      const uint32_t bb = smem_u32(bbuf);
+      for (int j = 0; j < nslot; ++j) {
+        const uint32_t idx = ring.i + j;
+        const uint32_t sa = smem_u32(ring.wait_at(idx));
+        tc_fence_after();
+        const int nch = nchunk - 2 * j < 2 ? nchunk - 2 * j : 2;
+        for (int ch = 0; ch < nch; ++ch)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the range
+            tc_mma_f16(tmem, plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128),
+                       plain_desc(bb + (uint32_t)(kl >> 3) * DN_MT * 128, DN_MT * 128, 128), idesc,
+                       (j | ch | kk) != 0);
+          }
+        // the slot goes back to the producer when these MMAs have read it (one arrival), the other warps' share now
+        tc_commit(&ring.empty[idx % ring.ns]);
+        mbar_arrive_cnt(&ring.empty[idx % ring.ns], NWARP - 1);
+      }
+      tc_commit(accbar);
+      ++issued;
+    }
+    if (!ring.dead && !mbar_wait(accbar, accn & 1u, ring.spin)) {
+      ring.dead = true;
+      atomicExch(pd.err, E_ERR_TIMEOUT);
+    }
+    ++accn;  // accumulator phases so far (the parity of the next one)
+    tc_fence_after();
+    ring.i += nslot;
+    const int row = warp * 32 + lane, n = tile * DN_TILE + row;
+    // 32 token columns of this thread's accumulator row at a time (the accumulator stays in TMEM until the next
+    // item, so the last range of a split tile reads it again after the exchange)
+    auto columns = [&](int m0, float (&v)[32]) {
+      uint32_t r[32];
+      tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)m0, r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int m = 0; m < 32; ++m) v[m] = __uint_as_float(r[m]);
+    };
+    if (ns == 1) {
+      if (warp < 4)
+        for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
+          float v[32];
+          columns(m0, v);
+          epi(n, m0, v);
+        }
+    } else {
+      // this range's partial sums -> [tile][range][token][row]; the last range of the tile adds all of them in
+      // range order
+      float* pt = pd.part + (size_t)tile * ns * DN_TOK * DN_TILE;
+      if (warp < 4)
+        for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
+          float v[32];
+          columns(m0, v);
+#pragma unroll
+          for (int m = 0; m < 32; ++m) __stcg(pt + ((size_t)split * DN_TOK + m0 + m) * DN_TILE + row, v[m]);
+        }
+      __threadfence();
+      csync();
+      if (threadIdx.x == 0) *flag = (atomicAdd(&pd.tcnt[tile], 1u) == (uint32_t)(ns - 1));
+      csync();
+      if (*flag) {
+        __threadfence();
+        if (warp < 4)
+          for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
+            float v[32];
+            columns(m0, v);
+#pragma unroll 4
+            for (int m = 0; m < 32; ++m) {
+              float acc = 0.f;
+              for (int s2 = 0; s2 < ns; ++s2)
+                acc += (s2 == split) ? v[m] : __ldcg(pt + ((size_t)s2 * DN_TOK + m0 + m) * DN_TILE + row);
+              v[m] = acc;
+            }
+            epi(n, m0, v);
+          }
+        if (threadIdx.x == 0) atomicExch(&pd.tcnt[tile], 0u);
+      }
+    }
+    tc_fence_before();
+    csync();  // the next item's first MMA overwrites the accumulator
+  }
+}
+
+// Normalise a unit's partial states (tab [Q][XPS]: unnormalised output dims, max, sum) into the token operand
+// layout of the next GEMM: tok(q) = token of query q, k = h * 64 + dim.
+template <class Tok>
+__device__ __forceinline__ void dn_emit_unit(const float* tab, int Q, int h, __half* dst, Tok&& tok) {
+  for (int idx = threadIdx.x; idx < Q * (DK / 8); idx += NTHR) {
+    const int q = idx >> 3, d8 = idx & 7;
+    const float l = tab[q * XPS + DK + 1];
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float* o = tab + q * XPS + d8 * 8;
+    uint4 w;
+    w.x = pack_half2(o[0] * inv, o[1] * inv);
+    w.y = pack_half2(o[2] * inv, o[3] * inv);
+    w.z = pack_half2(o[4] * inv, o[5] * inv);
+    w.w = pack_half2(o[6] * inv, o[7] * inv);
+    *reinterpret_cast<uint4*>(dst + dn_bidx(tok(q), h * DK + d8 * 8)) = w;
+  }
+}
+
+// Self-attention: unit (row b, head h) for u = c, c + P, ...: the row's S queries over its cached positions
+// [0, offset) (ring chunks) and its S new keys / values (causal), which are also written to the cache at
+// offset .. offset + S - 1 and to new_kv.
+template <int QM, bool WIDE>
+__device__ __noinline__ void dn_satt(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, int layer, int c,
+                        uint8_t* work) {
+  const AttnSmem as = carve_attn(work, pd.Qmax);
+  float* tab = reinterpret_cast<float*>(work + ((attn_smem(pd.Qmax) + 15) & ~(size_t)15));
+  const int S = pd.S, D = pd.D, H = pd.H;
+  for (int u = c; u < pd.R * H; u += pd.P) {
+    const int b = u / H, h = u - b * H, off = cx.offs[b];
+    csync();  // the previous unit's readers of the staging area are done
+    for (int idx = threadIdx.x; idx < S * (DK / 8); idx += NTHR) {
+      const int q = idx >> 3, d0 = (idx & 7) * 8;
+      const __half* row = pd.qkv + (size_t)(b * S + q) * 3 * D + h * DK + d0;
+      const uint4 qv = __ldcg(reinterpret_cast<const uint4*>(row));
+      const uint4 kv = __ldcg(reinterpret_cast<const uint4*>(row + D));
+      const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(row + 2 * D));
+      const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
+      const __half2* k2 = reinterpret_cast<const __half2*>(&kv);
+      const __half2* v2 = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = __half22float2(q2[e]), fk = __half22float2(k2[e]), fv = __half22float2(v2[e]);
+        const int d = q * DK + d0 + 2 * e;
+        as.q[d] = fq.x * 0.125f;
+        as.q[d + 1] = fq.y * 0.125f;
+        if (QM == 1 && WIDE) {
+          as.out[qperm(d0 + 2 * e)] = fq.x * 0.125f;
+          as.out[qperm(d0 + 2 * e + 1)] = fq.y * 0.125f;
+        }
+        as.knew[d] = fk.x;
+        as.knew[d + 1] = fk.y;
+        as.vnew[d] = fv.x;
+        as.vnew[d + 1] = fv.y;
+      }
+      // (layer strides of the caller's buffers: Rs rows, more than R when the call is a row slice)
+      const size_t cs = ((((size_t)layer * pd.Rs + b) * H + h) * pd.C + off + q) * DK + d0;
+      *reinterpret_cast<uint4*>(a.kc + cs) = kv;
+      *reinterpret_cast<uint4*>(a.vc + cs) = vv;
+      *reinterpret_cast<uint4*>(a.new_kv + ((((size_t)(layer * 2) * pd.Rs + b) * H + h) * S + q) * DK + d0) = kv;
+      *reinterpret_cast<uint4*>(a.new_kv + ((((size_t)(layer * 2 + 1) * pd.Rs + b) * H + h) * S + q) * DK + d0) = vv;
+    }
+    attn_unit<QM, WIDE>(as, ring, S, 0, off, pd.apos, S, cx,
+                        [&](int q, int c4, const float4& v) { sts128f(&tab[q * XPS + c4 * 4], v); });
+    csync();
+    dn_emit_unit(tab, S, h, pd.obuf, [&](int q) { return b * S + q; });
+  }
+}
+
+// Cross-attention: unit (utterance uu, head h) for units c, c + P, ...: the utterance's G rows x S queries over
+// its first enc_len frames (ring chunks), one unit per CTA at a time (no unit is split).
+template <int QM, bool WIDE>
+__device__ __noinline__ void dn_xatt(const PlanDev& pd, Ring& ring, const Ctx& cx, const int* pre, int layer, int c,
+                        uint8_t* work) {
+  const AttnSmem as = carve_attn(work, pd.Qmax);
+  float* tab = reinterpret_cast<float*>(work + ((attn_smem(pd.Qmax) + 15) & ~(size_t)15));
+  const int S = pd.S, D = pd.D, H = pd.H, G = pd.G, Q = G * S;
+  for (int u = c; u < pd.U * H; u += pd.P) {
+    const int uu = u / H, h = u - uu * H, len = pre[uu + 1] - pre[uu];
+    csync();
+    for (int idx = threadIdx.x; idx < Q * (DK / 8); idx += NTHR) {
+      const int q = idx >> 3, d0 = (idx & 7) * 8;
+      const uint4 qv = __ldcg(reinterpret_cast<const uint4*>(pd.q2 + (size_t)(uu * Q + q) * D + h * DK + d0));
+      const __half2* q2 = reinterpret_cast<const __half2*>(&qv);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fq = __half22float2(q2[e]);
+        as.q[q * DK + d0 + 2 * e] = fq.x * 0.125f;
+        as.q[q * DK + d0 + 2 * e + 1] = fq.y * 0.125f;
+        if (QM == 1 && WIDE) {
+          as.out[qperm(d0 + 2 * e)] = fq.x * 0.125f;
+          as.out[qperm(d0 + 2 * e + 1)] = fq.y * 0.125f;
+        }
+      }
+    }
+    attn_unit<QM, WIDE>(as, ring, Q, 0, len, pd.apos, 0, cx,
+                        [&](int q, int c4, const float4& v) { sts128f(&tab[q * XPS + c4 * 4], v); });
+    csync();
+    dn_emit_unit(tab, Q, h, pd.obuf, [&](int q) { return uu * Q + q; });
+  }
+}
+
+// The producer's copies of stage g on CTA c, in consumption order: f(src, bytes) per ring slot.
+template <class Fn>
+__device__ void dn_chunks(const PlanDev& pd, const CallArgs& a, const Ctx& cx, const int* pre, int g, int c, Fn&& f) {
+  int layer;
+  const Kind k = stage_kind(pd, g, layer);
+  const int gi = gemm_of(k);
+  if (gi >= 0) {
+    const int K = pd.g[gi].K, ns = pd.nsplit[gi], nchunk = (K / ns) >> 6, cpt = K >> 6;
+    const __half* base = pd.gt[gi] + (k == K_OUT ? 0 : (long long)layer * pd.gtl[gi]);
+    for (int i = cx.so[gi]; i < cx.so[gi + 1]; ++i) {
+      const int item = cx.sb[i], tile = item / ns, split = item - tile * ns;
+      const __half* src = base + ((long long)tile * cpt + (long long)split * nchunk) * (DN_CHUNK / 2);
+      for (int j = 0; j < nchunk; j += 2)
+        f(src + (long long)j * (DN_CHUNK / 2), (uint32_t)((nchunk - j < 2 ? nchunk - j : 2) * DN_CHUNK));
+    }
+    return;
+  }
+  if (k == K_SATT) {
+    for (int u = c; u < pd.R * pd.H; u += pd.P) {
+      const int b = u / pd.H, h = u % pd.H, off = cx.offs[b];
+      const long long base = ((((long long)layer * pd.Rs + b) * pd.H + h) * pd.C) * DK;
+      for (int j0 = 0; j0 < off; j0 += pd.apos) {
+        const int n = off - j0 < pd.apos ? off - j0 : pd.apos;
+        f((const void*)(a.kc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+        f((const void*)(a.vc + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+      }
+    }
+    return;
+  }
+  if (k == K_XATT) {
+    for (int u = c; u < pd.U * pd.H; u += pd.P) {
+      const int uu = u / pd.H, h = u % pd.H, len = pre[uu + 1] - pre[uu];
+      const long long base = ((((long long)layer * pd.Us + uu) * pd.H + h) * pd.T) * DK;
+      for (int j0 = 0; j0 < len; j0 += pd.apos) {
+        const int n = len - j0 < pd.apos ? len - j0 : pd.apos;
+        f((const void*)(a.ck + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+        f((const void*)(a.cv + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
+      }
+    }
+  }
+}
+
+template <int QM, bool WIDE>
+__global__ void __launch_bounds__(BLOCK, 1)
+    decoder_dense_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+  uint64_t* empty = full + MAXSLOT;
+  uint64_t* accbar = empty + MAXSLOT;
+  uint64_t* bbar = accbar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bbar + 1);
+  int* pre = reinterpret_cast<int*>(smem + pd.off_pre);
+  uint8_t* ringdata = smem + pd.off_ring;
+  uint8_t* work = smem + pd.off_work;
+  __half* bbuf = reinterpret_cast<__half*>(work);
+  const int c = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_stages = 8 * pd.L + 2;
+  int* so = reinterpret_cast<int*>(smem + pd.off_sched);
+  int* sb = so + NGEMM + 1;
+  int* offs = reinterpret_cast<int*>(smem + pd.off_rows);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < pd.nslot; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NWARP);
+    }
+    mbar_init(accbar, 1);
+    mbar_init(bbar, 1);
+    fence_barrier_init();
+    pre[0] = 0;
+    for (int u = 0; u < pd.U; ++u) pre[u + 1] = pre[u] + utt_len(pd, a, u);
+    so[0] = 0;
+    for (int gi = 0; gi < NGEMM; ++gi) so[gi + 1] = so[gi] + (pd.goff[gi][c + 1] - pd.goff[gi][c]);
+  }
+  if (warp == 0) {  // the accumulator: 128 lanes x 64 columns of this SM's tensor memory
+    tmem_alloc(tmem_slot, DN_TOK);
+    tmem_relinquish();
+  }
+  for (int r = threadIdx.x; r < pd.R; r += BLOCK) offs[r] = row_off_global(pd, a, r);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const int base = pd.goff[gi][c];
+    for (int i = threadIdx.x; i < so[gi + 1] - so[gi]; i += BLOCK) sb[so[gi] + i] = pd.gblk[gi][base + i];
+  }
+  __syncthreads();
+  unsigned long long* evlog = pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
+  int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
+  if (threadIdx.x == 0) *nev = 0;
+  __syncthreads();
+  const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
+
+  if (warp == NWARP) {  // producer: the CTA's whole sequence of copies, as in the grid-stage kernel
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      uint32_t i = 0;
+      bool dead = false;
+      for (int g = 0; g < n_stages && !dead; ++g) {
+        dn_chunks(pd, a, cx, pre, g, c, [&](const void* src, uint32_t bytes) {
+          if (dead) return;
+          const int s = i % pd.nslot;
+          if (!mbar_wait(&empty[s], ((i / pd.nslot) & 1) ^ 1, pd.max_spin)) {
+            dead = true;
+            atomicExch(pd.err, E_ERR_TIMEOUT);
+            return;
+          }
+          if (i >= (uint32_t)pd.inflight) {
+            const uint32_t j = i - pd.inflight;
+            if (!mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, pd.max_spin)) {
+              dead = true;
+              atomicExch(pd.err, E_ERR_TIMEOUT);
+              return;
+            }
+          }
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(ringdata + (size_t)s * pd.sstride, src, bytes, &full[s], pol);
+          ++i;
+        });
+      }
+      const uint32_t first = i > (uint32_t)pd.nslot ? i - pd.nslot : 0;
+      for (uint32_t j = first; j < i; ++j) mbar_wait(&full[j % pd.nslot], (j / pd.nslot) & 1, DEFAULT_SPIN);
+    }
+    return;
+  }
+
+  Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
+  OutState os = carve_out(smem + pd.off_out, pd.M, false);
+  for (int m = threadIdx.x; m < pd.M; m += NTHR) {
+    os.amax[m] = -INFINITY;
+    os.aidx[m] = 0x7fffffff;
+  }
+  int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
+  int* tflag = reinterpret_cast<int*>(smem + pd.off_pre) + 1035;
+  uint32_t accn = 0, issued = 0, bph = 0;
+  bool copies = false;  // thread 0: an operand copy was issued (its completion is awaited before the CTA exits)
+  const int D = pd.D, M = pd.M, V = pd.V;
+  bool dead = false;
+  for (int g = 0; g < n_stages; ++g) {
+    int layer;
+    const Kind k = stage_kind(pd, g, layer);
+    unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (ts && threadIdx.x == 0) ts[0] = globaltimer();
+    ring.dead = dead;
+    const int gi = gemm_of(k);
+    const float* bias = gi >= 0 ? pd.g[gi].b + (k == K_OUT ? 0 : (long long)layer * pd.g[gi].N) : nullptr;
+    auto ln_stage = [&](int k0, int kr) { dn_ln(pd, k0, kr, bbuf); };
+    auto copy_stage = [&](const __half* src) {
+      return [&, src](int k0, int kr) {
+        if (threadIdx.x == 0 && !ring.dead) {
+          copies = true;
+          if (!dn_stage_copy(src, k0, kr, bbuf, bbar, bph, ring.spin)) {
+            ring.dead = true;
+            atomicExch(pd.err, E_ERR_TIMEOUT);
+          }
+        }
+      };
+    };
+    // residual epilogue: x[m][n] += y + b (this thread owns row n of every token)
+    auto res_epi = [&](int n, int m0, const float (&v)[32]) {
+      const float b = bias[n];
+#pragma unroll 8
+      for (int m = 0; m < 32; ++m)
+        if (m0 + m < M) pd.x[(size_t)(m0 + m) * D + n] += v[m] + b;
+    };
+    if (dead) {
+    } else if (k == K_EMBED) {
+      embed_stage(pd, a, cx, c);
+    } else if (k == K_QKV) {
+      dn_gemm(pd, ring, cx, G_QKV, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        const float b = bias[n];
+#pragma unroll 8
+        for (int m = 0; m < 32; ++m)
+          if (m0 + m < M) pd.qkv[(size_t)(m0 + m) * 3 * D + n] = __float2half_rn(v[m] + b);
+      });
+    } else if (k == K_SATT) {
+      dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
+    } else if (k == K_WO || k == K_WCO) {
+      dn_gemm(pd, ring, cx, gi, tmem, accbar, accn, issued, bbuf, tflag, copy_stage(pd.obuf), res_epi);
+    } else if (k == K_CQ) {
+      dn_gemm(pd, ring, cx, G_CQ, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        const float b = bias[n];
+#pragma unroll 8
+        for (int m = 0; m < 32; ++m)
+          if (m0 + m < M) pd.q2[(size_t)(m0 + m) * D + n] = __float2half_rn(v[m] + b);
+      });
+    } else if (k == K_XATT) {
+      dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
+    } else if (k == K_F1) {
+      dn_gemm(pd, ring, cx, G_F1, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        const float b = bias[n];
+#pragma unroll 8
+        for (int m = 0; m < 32; ++m) pd.hbuf[dn_bidx(m0 + m, n)] = __float2half_rn(m0 + m < M ? fmaxf(v[m] + b, 0.f) : 0.f);
+      });
+    } else if (k == K_F2) {
+      dn_gemm(pd, ring, cx, G_F2, tmem, accbar, accn, issued, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
+    } else if (k == K_OUT) {
+      for (int m = lane; m < M; m += 32) {  // this warp's running best per token
+        os.wamax[warp * M + m] = -INFINITY;
+        os.waidx[warp * M + m] = 0x7fffffff;
+      }
+      __syncwarp();
+      dn_gemm(pd, ring, cx, G_OUT, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        const bool in = n < V;
+        const float b = in ? bias[n] : 0.f;
+        const bool tmask = a.notime && n >= a.ft && n <= a.lt;
+#pragma unroll 1
+        for (int mm = 0; mm < 32 && m0 + mm < M; ++mm) {
+          const int m = m0 + mm;
+          const float y = v[mm] + b;
+          if (in) a.logits[(size_t)m * V + n] = y;
+          float bv = (in && !(tmask && a.notime[m / pd.S])) ? y : -INFINITY;
+          int bi = in ? n : 0x7fffffff;
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            merge_best(bv, bi, ov, oi);
+          }
+          if (lane == 0) merge_best(os.wamax[warp * M + m], os.waidx[warp * M + m], bv, bi);
+        }
+      });
+      csync();
+      for (int m = threadIdx.x; m < M; m += NTHR) {
+        float bv = os.amax[m];
+        int bi = os.aidx[m];
+        for (int w = 0; w < 4; ++w) merge_best(bv, bi, os.wamax[w * M + m], os.waidx[w * M + m]);
+        os.amax[m] = bv;
+        os.aidx[m] = bi;
+      }
+      csync();
+      if (a.pred) argmax_finish(pd, a, c, os, flag, work);
+    }
+    // the attention output / FFN hidden just written are read by the next stage's bulk copies (async proxy)
+    if (k == K_SATT || k == K_XATT || k == K_F1) asm volatile("fence.proxy.async.global;" ::: "memory");
+    dead = dead || ring.dead;
+    if (ts && threadIdx.x == 0) ts[1] = globaltimer();
+    if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead, reinterpret_cast<int*>(smem + pd.off_pre) + 1034);
+    if (ts && threadIdx.x == 0) {
+      ts[2] = globaltimer();
+      ts[3] = ring.waited;
+    }
+    ring.waited = 0;
+  }
+  csync();
+  if (threadIdx.x == 0) {
+    if (atom_acq_rel_add(&pd.ctr[1], 1) == (uint32_t)(pd.P - 1)) {
+      atomicExch(&pd.ctr[1], 0u);
+      atomicExch(&pd.ctr[0], 0u);
+    }
+  }
+  // before the CTA leaves: its last MMAs and operand copy (which a timed-out wait may have left running) are
+  // done -- both always finish, so the default limit -- then the accumulator columns are freed
+  if (threadIdx.x == 0) {
+    if (issued) mbar_wait(accbar, (issued - 1) & 1u, DEFAULT_SPIN);
+    if (copies) mbar_wait(bbar, bph ^ 1u, DEFAULT_SPIN);
+  }
+  tc_fence_before();
+  csync();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, DN_TOK);
+  }
+}
+
+// Fragment-ordered weights (the mma.sync packing of owsm_dec_create) -> 128-row tiles for the dense kernel:
+// out[layer][tile][K / 64][k group 8][row group 16][row 8][8 k] (halves; rows >= N zero). A thread writes one
+// 16-byte core-matrix row from four 32-bit fragment registers.
+__global__ void tile_pack_kernel(const uint4* __restrict__ frag, int N, int K, int bstride, long long lstride,
+                                 int layers, __half* __restrict__ out, long long out_lstride) {
+  const int ntile = (N + DN_TILE - 1) / DN_TILE, nchunk = K >> 6;
+  const long long per_layer = (long long)ntile * nchunk * 8 * 16 * 8;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < per_layer * layers;
+       i += (long long)gridDim.x * blockDim.x) {
+    const int layer = (int)(i / per_layer);
+    long long j = i - (long long)layer * per_layer;
+    const int r = (int)(j & 7);
+    j >>= 3;
+    const int rg = (int)(j & 15);
+    j >>= 4;
+    const int kg = (int)(j & 7);
+    j >>= 3;
+    const int chunk = (int)(j % nchunk), tile = (int)(j / nchunk);
+    const int row = tile * DN_TILE + rg * 8 + r, k0 = chunk * 64 + kg * 8;
+    uint4 o = make_uint4(0u, 0u, 0u, 0u);
+    if (row < N) {
+      // fragment order: block row >> 4, k block k0 >> 4; lane g * 4 + t holds rows g, g + 8 x k 2t, 2t + 1 (regs 0,
+      // 1) and k 2t + 8, 2t + 9 (regs 2, 3)
+      const int rb = row >> 4, rr = row & 15, g = rr & 7, hi = rr >> 3, kb = k0 >> 4, khi = (k0 & 15) >> 3;
+      const uint4* src = frag + (long long)layer * lstride + (long long)rb * bstride + kb * 32 + g * 4;
+      uint32_t w[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const uint4 f = src[t];
+        const uint32_t regs[4] = {f.x, f.y, f.z, f.w};
+        w[t] = regs[hi + 2 * khi];
+      }
+      o = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    const long long dst = (long long)layer * out_lstride + ((((long long)tile * nchunk + chunk) * 8 + kg) * 16 + rg) * 8 + r;
+    reinterpret_cast<uint4*>(out)[dst] = o;
+  }
+}
+
+}  // namespace owsm

@@ -103,6 +103,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* map, int x, i
       : "memory");
 }
 
+// Contiguous bytes global -> this CTA's shared memory by the bulk-copy engine, counted on bar (no cache hint).
+// dst, src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s_nohint(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // Make this thread's ordinary shared-memory writes visible to the async proxy (tensor-core operand reads).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 

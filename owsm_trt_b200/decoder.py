@@ -44,7 +44,7 @@ class B200Decoder:
 
     name = "b200-megakernel"
     argmax = True  # step_fn takes pred
-    max_tokens = 64  # rows x window of one call (MegaBackend's max_tokens for this kernel)
+    max_tokens = 4096  # rows x window of one call (larger greedy calls run as row slices of up to 64 tokens)
     solo_differs = False  # a single-row call is the same call with or without an encoder alongside
 
     @torch.no_grad()
@@ -168,16 +168,17 @@ class B200Decoder:
             raise RuntimeError("the decoder kernel timed out at a grid barrier (were all its CTAs resident?)")
 
     def set_path(self, path: int) -> None:
-        """Which kernel later calls use: 0 the cluster kernel where the call allows it (default), 1 the
-        grid-stage kernel, 2 the cluster kernel or an error. Drops the cached plans."""
+        """Which kernel later calls use: 0 the default (the dense tcgen05 kernel for greedy calls of more than 32
+        tokens, the cluster kernel for the others where it applies), 1 the grid-stage kernel, 2 the cluster kernel
+        or an error, 3 the dense kernel or an error. Drops the cached plans."""
         _lib.check(_lib.lib().owsm_dec_set_path(self._h, int(path)), "owsm_dec_set_path")
         for p in self._plans.values():
             _lib.lib().owsm_dec_plan_destroy(p)
         self._plans.clear()
 
     def plan_kernel(self, run) -> str:
-        """"cluster" or "grid": the kernel behind a step_fn / beam_fn closure."""
-        return "cluster" if _lib.lib().owsm_dec_plan_kernel(run.plan) == 2 else "grid"
+        """"cluster", "grid" or "dense": the kernel behind a step_fn / beam_fn closure."""
+        return {1: "grid", 2: "cluster", 3: "dense"}[_lib.lib().owsm_dec_plan_kernel(run.plan)]
 
     def launches(self, run) -> int:
         """Kernel launches of one call of a step_fn / beam_fn closure (1, or its row slices)."""

@@ -483,7 +483,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
       };
     };
     // residual epilogue: x[m][n] += y + b (this thread owns row n of every token)
+    const int N = gi >= 0 ? pd.g[gi].N : 0;
     auto res_epi = [&](int n, int m0, const float (&v)[32]) {
+      if (n >= N) return;
       const float b = bias[n];
 #pragma unroll 8
       for (int m = 0; m < 32; ++m)
@@ -494,6 +496,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       embed_stage(pd, a, cx, c);
     } else if (k == K_QKV) {
       dn_gemm(pd, ring, cx, G_QKV, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
         for (int m = 0; m < 32; ++m)
@@ -505,6 +508,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       dn_gemm(pd, ring, cx, gi, tmem, accbar, accn, issued, bbuf, tflag, copy_stage(pd.obuf), res_epi);
     } else if (k == K_CQ) {
       dn_gemm(pd, ring, cx, G_CQ, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
         for (int m = 0; m < 32; ++m)
@@ -514,6 +518,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
       dn_gemm(pd, ring, cx, G_F1, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+        if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
         for (int m = 0; m < 32; ++m) pd.hbuf[dn_bidx(m0 + m, n)] = __float2half_rn(m0 + m < M ? fmaxf(v[m] + b, 0.f) : 0.f);
@@ -590,8 +595,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
 }
 
 // Fragment-ordered weights (the mma.sync packing of owsm_dec_create) -> 128-row tiles for the dense kernel:
-// out[layer][tile][K / 64][k group 8][row group 16][row 8][8 k] (halves; rows >= N zero). A thread writes one
-// 16-byte core-matrix row from four 32-bit fragment registers.
+// out[layer][tile][K / 64][k group 8][row group 16][row 8][8 k] (halves; rows >= N zero; out_lstride halves per
+// layer). A thread writes one 16-byte core-matrix row from four 32-bit fragment registers.
 __global__ void tile_pack_kernel(const uint4* __restrict__ frag, int N, int K, int bstride, long long lstride,
                                  int layers, __half* __restrict__ out, long long out_lstride) {
   const int ntile = (N + DN_TILE - 1) / DN_TILE, nchunk = K >> 6;
@@ -623,7 +628,8 @@ __global__ void tile_pack_kernel(const uint4* __restrict__ frag, int N, int K, i
       }
       o = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    const long long dst = (long long)layer * out_lstride + ((((long long)tile * nchunk + chunk) * 8 + kg) * 16 + rg) * 8 + r;
+    // (16-byte units: out_lstride counts halves)
+    const long long dst = (long long)layer * (out_lstride >> 3) + ((((long long)tile * nchunk + chunk) * 8 + kg) * 16 + rg) * 8 + r;
     reinterpret_cast<uint4*>(out)[dst] = o;
   }
 }

@@ -16,7 +16,7 @@ ROOT = PKG.parent
 LIB = PKG / "libowsmdec.so"
 OBJ = PKG / "_build"
 SOURCES = [PKG / "csrc" / "decoder.cu", PKG / "csrc" / "xkv.cu"]
-HEADERS = [PKG / "csrc" / "ptx.cuh", PKG / "csrc" / "cluster.cuh", PKG / "csrc" / "tc.cuh", ROOT / "include" / "owsm_dec.h"]
+HEADERS = sorted((PKG / "csrc").glob("*.cuh")) + [ROOT / "include" / "owsm_dec.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -209,7 +209,7 @@ class Greedy:
         self.ck, self.cv, self.enc_len, self.prefix, self.kc, self.vc = ck, cv, enc_len, prefix, kc, vc
         self.enc_len_d = enc_len.to(dev)
         # the prefix in one call, or one position per call where rows x 4 exceeds what a call takes
-        S = PREFIX if B * PREFIX <= kern.max_tokens else 1
+        S = PREFIX if B * PREFIX <= 64 else 1
         lg_p = torch.zeros(B, S, d.V, device=dev)
         kv_p = torch.zeros(d.L, 2, B, d.H, S, d.dk, device=dev, dtype=torch.float16)
         pr_p = torch.zeros(B, S, dtype=torch.long, device=dev)

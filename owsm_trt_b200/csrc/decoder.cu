@@ -113,6 +113,8 @@ struct PlanDev {
   uint32_t* tcnt;           // ranges arrived per tile (the last one resets it)
   __half* obuf;             // attention output in the token-operand layout [D / 8][8][64] halves
   __half* hbuf;             // FFN hidden in the token-operand layout [F / 8][8][64] halves
+  float* xstat;             // LayerNorm partial sums of the residual rows [D / 32][64 tokens][sum, sum of squares]
+  int off_stat;             // shared memory: the stage's LayerNorm mean and 1 / std per token [64][2]
 };
 
 struct CallArgs {
@@ -2428,6 +2430,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.obuf, (size_t)D * DN_TOK, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.hbuf, (size_t)F * DN_TOK, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xstat, (size_t)(D / 32) * DN_TOK * 2, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.part, (size_t)std::max(max_tiles_split, 1) * DN_TOK * DN_TILE, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.tcnt, (size_t)max_tiles, tot))) return bail(rc);
   p->tcnt_bytes = (size_t)max_tiles * sizeof(uint32_t);
@@ -2436,13 +2439,17 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);
   // shared memory: barriers | utterance prefix sums + flags | work items | row offsets | argmax state | ring | work
-  int maxkr = 0;
-  for (int gi = 0; gi < NGEMM; ++gi) maxkr = std::max(maxkr, h->g[gi].K / pd.nsplit[gi]);
+  int maxkr = 0;  // the largest operand half
+  for (int gi = 0; gi < NGEMM; ++gi) {
+    const int kr = h->g[gi].K / pd.nsplit[gi];
+    maxkr = std::max(maxkr, kr / dn_halves(kr));
+  }
   const size_t off_pre = 256;
   const size_t off_sched = (off_pre + 4 * 1072 + 127) & ~(size_t)127;
   const size_t off_rows = (off_sched + 4 * (NGEMM + 1 + max_items) + 127) & ~(size_t)127;
   const size_t off_out = (off_rows + 4 * (size_t)R + 127) & ~(size_t)127;
-  const size_t off_ring = (off_out + out_smem(M, false) + 1023) & ~(size_t)1023;
+  const size_t off_stat = (off_out + out_smem(M, false) + 127) & ~(size_t)127;
+  const size_t off_ring = (off_stat + DN_TOK * 2 * sizeof(float) + 1023) & ~(size_t)1023;
   size_t work = (size_t)DN_TOK * maxkr * 2;
   work = std::max(work, ((attn_smem(pd.Qmax) + 15) & ~(size_t)15) + sizeof(float) * (size_t)pd.Qmax * XPS);
   work = std::max(work, sizeof(float) * 2 * (size_t)P * M);  // the argmax partials of all CTAs
@@ -2459,6 +2466,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   pd.off_rows = (int)off_rows;
   pd.inflight = nslot;  // every slot may be in flight: a work item streams 128 KB of weights
   pd.off_out = (int)off_out;
+  pd.off_stat = (int)off_stat;
   pd.off_ring = (int)off_ring;
   pd.sstride = SLOT + 128;
   pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);

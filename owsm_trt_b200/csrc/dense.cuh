@@ -30,14 +30,21 @@ namespace owsm {
 constexpr int DN_MT = 8;                 // token groups of 8: up to 64 tokens
 constexpr int DN_TOK = DN_MT * 8;
 constexpr int DN_TILE = 128;             // weight rows per tile
-constexpr int DN_KR = 512;               // largest K range of a work item (B operand: 64 tokens x 512 fp16 = 64 KB)
+constexpr int DN_KR = 512;               // largest operand half (64 tokens x 512 fp16 = 64 KB of shared memory)
+constexpr int DN_KI = 1024;              // largest K range of a work item (FFN2 splits its K in ranges of this size)
 constexpr int DN_CHUNK = DN_TILE * 64 * 2;  // bytes of a 128 x 64 weight chunk
 constexpr int DN_BBYTES = DN_TOK * DN_KR * 2;
 
-// K splits of a GEMM: ranges of at most DN_KR features, each a multiple of 64.
+// K ranges of a GEMM's work items (at most DN_KI features, a multiple of 128), and the halves an item streams its
+// token operand in (at most DN_KR features, a multiple of 128: a half is a whole number of two-chunk ring slots).
 __host__ __device__ constexpr int dn_splits(int K) {
-  int n = (K + DN_KR - 1) / DN_KR;
-  while (K % n || (K / n) % 64) ++n;
+  int n = (K + DN_KI - 1) / DN_KI;
+  while (K % n || (K / n) % 128) ++n;
+  return n;
+}
+__host__ __device__ constexpr int dn_halves(int kr) {
+  int n = (kr + DN_KR - 1) / DN_KR;
+  while (kr % n || (kr / n) % 128) ++n;
   return n;
 }
 
@@ -47,69 +54,58 @@ __device__ __forceinline__ int dn_bidx(int m, int k) {
   return (((k >> 3) * DN_MT + (m >> 3)) << 6) + ((m & 7) << 3) + (k & 7);
 }
 
-// LayerNorm of the residual rows (fp32 [M][D]) into the token operand of features [k0, k0 + kr): the
-// statistics over the whole row (sum and sum of squares in fp64, one pass), padding tokens zero. A warp
-// normalises two rows at a time with all their loads issued together.
-__device__ __noinline__ void dn_ln(const PlanDev& pd, int k0, int kr, __half* bbuf) {
-  const int D = pd.D, M = pd.M, nv = D >> 7;  // float4 per lane per row (D <= 1024)
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int m0 = warp * 2; m0 < DN_TOK; m0 += NWARP * 2) {
-    float4 v[2][MAXV4];
-#pragma unroll
-    for (int r = 0; r < 2; ++r)
-#pragma unroll
-      for (int i = 0; i < MAXV4; ++i)
-        if (i < nv) v[r][i] = (m0 + r < M) ? __ldcg(reinterpret_cast<const float4*>(pd.x + (size_t)(m0 + r) * D) + lane + 32 * i)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      const int m = m0 + r;
+// LayerNorm statistics of the residual rows from the partial sums the residual's producers left (xstat
+// [D / 32][64 tokens][sum, sum of squares]: one slot per 32 features): mean and 1 / sqrt(var + eps) per token
+// into st[64][2] (shared memory), fp64 over the slots; padding tokens 0.
+__device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
+  const int m = threadIdx.x;
+  if (m < DN_TOK) {
+    float mean = 0.f, rs = 0.f;
+    if (m < pd.M) {
       double s1 = 0.0, s2 = 0.0;
-#pragma unroll
-      for (int i = 0; i < MAXV4; ++i)
-        if (i < nv) {
-          const float4 u = v[r][i];
-          s1 += ((double)u.x + (double)u.y) + ((double)u.z + (double)u.w);
-          s2 = fma((double)u.x, (double)u.x, s2);
-          s2 = fma((double)u.y, (double)u.y, s2);
-          s2 = fma((double)u.z, (double)u.z, s2);
-          s2 = fma((double)u.w, (double)u.w, s2);
-        }
-#pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      for (int sl = 0; sl < (pd.D >> 5); ++sl) {
+        const float2 p = __ldcg(reinterpret_cast<const float2*>(pd.xstat) + (size_t)sl * DN_TOK + m);
+        s1 += p.x;
+        s2 += p.y;
       }
-      const double mean = s1 / D, var = fmax(s2 / D - mean * mean, 0.0);
-      const float fm = (float)mean, rs = (float)(1.0 / sqrt(var + (double)pd.eps));
-#pragma unroll
-      for (int i = 0; i < MAXV4; ++i) {
-        const int k = 4 * (lane + 32 * i);
-        if (i < nv && k >= k0 && k < k0 + kr) {
-          const float4 u = v[r][i];
-          uint2 h;
-          if (m < M) {
-            h.x = pack_half2((u.x - fm) * rs, (u.y - fm) * rs);
-            h.y = pack_half2((u.z - fm) * rs, (u.w - fm) * rs);
-          } else {
-            h.x = h.y = 0u;
-          }
-          *reinterpret_cast<uint2*>(bbuf + dn_bidx(m, k - k0)) = h;
-        }
-      }
+      const double mu = s1 / pd.D, var = fmax(s2 / pd.D - mu * mu, 0.0);
+      mean = (float)mu;
+      rs = (float)(1.0 / sqrt(var + (double)pd.eps));
     }
+    st[2 * m] = mean;
+    st[2 * m + 1] = rs;
+  }
+}
+
+// The normalised residual, features [k0, k0 + hs), into the token operand: a thread per (token, 8 features),
+// consecutive threads consecutive tokens (16-byte stores into one core matrix after another), padding zero.
+__device__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, __half* bbuf) {
+  const int D = pd.D, M = pd.M;
+  for (int idx = threadIdx.x; idx < DN_TOK * (hs >> 3); idx += NTHR) {
+    const int m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
+    uint4 w = make_uint4(0u, 0u, 0u, 0u);
+    if (m < M) {
+      const float4* xr = reinterpret_cast<const float4*>(pd.x + (size_t)m * D + k0 + f);
+      const float4 u0 = __ldcg(xr), u1 = __ldcg(xr + 1);
+      const float mu = st[2 * m], rs = st[2 * m + 1];
+      w.x = pack_half2((u0.x - mu) * rs, (u0.y - mu) * rs);
+      w.y = pack_half2((u0.z - mu) * rs, (u0.w - mu) * rs);
+      w.z = pack_half2((u1.x - mu) * rs, (u1.y - mu) * rs);
+      w.w = pack_half2((u1.z - mu) * rs, (u1.w - mu) * rs);
+    }
+    *reinterpret_cast<uint4*>(bbuf + dn_bidx(m, f)) = w;
   }
   fence_async_smem();  // the operand is read by the tensor cores (async proxy)
 }
 
-// The token operand of features [k0, k0 + kr) from a global buffer in the same layout (attention output, FFN
+// The token operand of features [k0, k0 + hs) from a global buffer in the same layout (attention output, FFN
 // hidden): one bulk copy of the contiguous range, issued and awaited by thread 0 (the MMA issuer).
-__device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int kr, __half* bbuf, uint64_t* bar,
+__device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int hs, __half* bbuf, uint64_t* bar,
                                               uint32_t& ph, uint32_t spin) {
   // the source was written by other CTAs' ordinary stores before the grid barrier: order them before the
   // bulk-copy engine's reads
   asm volatile("fence.proxy.async.global;" ::: "memory");
-  const uint32_t bytes = (uint32_t)kr * DN_TOK * 2;
+  const uint32_t bytes = (uint32_t)hs * DN_TOK * 2;
   mbar_arrive_expect_tx(bar, bytes);
   bulk_g2s_nohint(bbuf, src + (size_t)(k0 >> 3) * DN_MT * 64, bytes, bar);
   const bool ok = mbar_wait(bar, ph, spin);
@@ -117,59 +113,76 @@ __device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int kr,
   return ok;
 }
 
-// One GEMM stage of the dense kernel on this CTA: its work items (tile, K range) in schedule order.
-// stage(k0, kr) fills the token operand with features [k0, k0 + kr) (every consumer thread calls it; thread 0
-// only issues the MMAs, after it returns); epi(n, m0, v) finishes output row n of a tile for tokens m0 .. m0 + 31
-// from their complete sums v (warps 0-3, one row per thread, called by the CTA that completes the tile).
+// Completion of this thread's tcgen05 work, counted on an mbarrier: `issued` commits made (thread 0), `seen`
+// phases awaited (every consumer thread).
+struct TcBar {
+  uint64_t* bar;
+  uint32_t issued, seen;
+};
+
+__device__ __forceinline__ void tc_wait(const PlanDev& pd, Ring& ring, TcBar& b) {
+  if (!ring.dead && !mbar_wait(b.bar, b.seen & 1u, ring.spin)) {
+    ring.dead = true;
+    atomicExch(pd.err, E_ERR_TIMEOUT);
+  }
+  ++b.seen;
+  tc_fence_after();
+}
+
+// One GEMM stage of the dense kernel on this CTA: its work items (tile, K range) in schedule order. An item
+// streams its token operand in halves: stage(k, hs) fills the operand with features [k, k + hs) (every consumer
+// thread calls it; thread 0 issues the half's MMAs after it), the accumulator collects all halves in TMEM.
+// epi(n, m0, v) finishes output row n of the tile for tokens m0 .. m0 + 31 from their complete sums v (warps 0-3,
+// one row per thread). A tile whose K is split (FFN2) writes each range's partial sums to global memory; the last
+// range to arrive adds all of them in range order (every thread a share, into shared memory) and finishes the tile.
 template <class Stage, class Epi>
-__device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, uint64_t* accbar,
-                        uint32_t& accn, uint32_t& issued, __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
+__device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, TcBar& acc, TcBar& opb,
+                        __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
-  const int K = pd.g[gi].K, ns = pd.nsplit[gi], kr = K / ns, nchunk = kr >> 6, nslot = (nchunk + 1) >> 1;
+  const int K = pd.g[gi].K, ns = pd.nsplit[gi], kr = K / ns, nh = dn_halves(kr), hs = kr / nh;
+  const int hslots = hs >> 7;  // ring slots (two 64-wide chunks each) per half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int staged = -1;
   for (int i = nb0; i < nb1; ++i) {
     const int item = cx.sb[i], tile = item / ns, split = item - tile * ns, k0 = split * kr;
-    if (k0 != staged) {  // (the previous item's MMAs, which read the operand, are complete: its accumulator was)
-      stage(k0, kr);
+    for (int h = 0; h < nh; ++h) {
+      if (h > 0) tc_wait(pd, ring, opb);  // the previous half's MMAs have read the operand
+      stage(k0 + h * hs, hs);
       csync();
-      staged = k0;
-    }
-    // (a failed call issues nothing more, so at most the last commit is outstanding when the CTA leaves)
-    if (threadIdx.x == 0 && !ring.dead) {
-      constexpr uint32_t idesc = idesc_f16_f32(DN_TILE, DN_TOK);
-      const uint32_t bb = smem_u32(bbuf);
-      for (int j = 0; j < nslot; ++j) {
-        const uint32_t idx = ring.i + j;
-        const uint32_t sa = smem_u32(ring.wait_at(idx));
-        tc_fence_after();
-        const int nch = nchunk - 2 * j < 2 ? nchunk - 2 * j : 2;
-        for (int ch = 0; ch < nch; ++ch)
+      // (a failed call issues nothing more, so at most the last commit is outstanding when the CTA leaves)
+      if (threadIdx.x == 0 && !ring.dead) {
+        constexpr uint32_t idesc = idesc_f16_f32(DN_TILE, DN_TOK);
+        const uint32_t bb = smem_u32(bbuf);
+        for (int j = 0; j < hslots; ++j) {
+          const uint32_t idx = ring.i + h * hslots + j;
+          const uint32_t sa = smem_u32(ring.wait_at(idx));
+          tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the range
-            tc_mma_f16(tmem, plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128),
-                       plain_desc(bb + (uint32_t)(kl >> 3) * DN_MT * 128, DN_MT * 128, 128), idesc,
-                       (j | ch | kk) != 0);
-          }
-        // the slot goes back to the producer when these MMAs have read it (one arrival), the other warps' share now
-        tc_commit(&ring.empty[idx % ring.ns]);
-        mbar_arrive_cnt(&ring.empty[idx % ring.ns], NWARP - 1);
+          for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the half
+              tc_mma_f16(tmem, plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128),
+                         plain_desc(bb + (uint32_t)(kl >> 3) * DN_MT * 128, DN_MT * 128, 128), idesc,
+                         (h | j | ch | kk) != 0);
+            }
+          // the slot goes back to the producer when these MMAs have read it (one arrival), the other warps'
+          // share now
+          tc_commit(&ring.empty[idx % ring.ns]);
+          mbar_arrive_cnt(&ring.empty[idx % ring.ns], NWARP - 1);
+        }
+        if (h < nh - 1) {
+          tc_commit(opb.bar);
+          ++opb.issued;
+        } else {
+          tc_commit(acc.bar);
+          ++acc.issued;
+        }
       }
-      tc_commit(accbar);
-      ++issued;
     }
-    if (!ring.dead && !mbar_wait(accbar, accn & 1u, ring.spin)) {
-      ring.dead = true;
-      atomicExch(pd.err, E_ERR_TIMEOUT);
-    }
-    ++accn;  // accumulator phases so far (the parity of the next one)
-    tc_fence_after();
-    ring.i += nslot;
+    tc_wait(pd, ring, acc);
+    ring.i += nh * hslots;
     const int row = warp * 32 + lane, n = tile * DN_TILE + row;
-    // 32 token columns of this thread's accumulator row at a time (the accumulator stays in TMEM until the next
-    // item, so the last range of a split tile reads it again after the exchange)
     auto columns = [&](int m0, float (&v)[32]) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)m0, r);
@@ -185,9 +198,7 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
           epi(n, m0, v);
         }
     } else {
-      // this range's partial sums -> [tile][range][token][row]; the last range of the tile adds all of them in
-      // range order
-      float* pt = pd.part + (size_t)tile * ns * DN_TOK * DN_TILE;
+      float* pt = pd.part + (size_t)tile * ns * DN_TOK * DN_TILE;  // [range][token][row]
       if (warp < 4)
         for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
           float v[32];
@@ -201,24 +212,73 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
       csync();
       if (*flag) {
         __threadfence();
-        if (warp < 4)
+        // the ranges' sums in range order into shared memory (the operand area: this CTA's MMAs are done)
+        float4* sum = reinterpret_cast<float4*>(bbuf);
+        const float4* p4 = reinterpret_cast<const float4*>(pt);
+        for (int q = threadIdx.x; q < DN_TOK * DN_TILE / 4; q += NTHR) {
+          float4 t = __ldcg(p4 + q);
+          for (int s2 = 1; s2 < ns; ++s2) {
+            const float4 u = __ldcg(p4 + (size_t)s2 * (DN_TOK * DN_TILE / 4) + q);
+            t.x += u.x;
+            t.y += u.y;
+            t.z += u.z;
+            t.w += u.w;
+          }
+          sum[q] = t;
+        }
+        csync();
+        if (warp < 4) {
+          const float* sf = reinterpret_cast<const float*>(bbuf);
           for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
             float v[32];
-            columns(m0, v);
-#pragma unroll 4
-            for (int m = 0; m < 32; ++m) {
-              float acc = 0.f;
-              for (int s2 = 0; s2 < ns; ++s2)
-                acc += (s2 == split) ? v[m] : __ldcg(pt + ((size_t)s2 * DN_TOK + m0 + m) * DN_TILE + row);
-              v[m] = acc;
-            }
+#pragma unroll
+            for (int m = 0; m < 32; ++m) v[m] = sf[(m0 + m) * DN_TILE + row];
             epi(n, m0, v);
           }
+        }
         if (threadIdx.x == 0) atomicExch(&pd.tcnt[tile], 0u);
       }
     }
     tc_fence_before();
-    csync();  // the next item's first MMA overwrites the accumulator
+    csync();  // the next item's first MMA overwrites the accumulator (and its staging the operand)
+  }
+}
+
+// Embedding into the residual rows (a CTA per token) and their LayerNorm partial sums (slot 0 holds the row's
+// sums, the other slots zero).
+__device__ void dn_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
+  const int D = pd.D, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* red = cx.red;  // [2 * NWARP]
+  for (int m = c; m < pd.M; m += pd.P) {
+    const int r = m / pd.S, s = m % pd.S;
+    long long t = a.tok[(long long)r * a.tok_stride + s];
+    t = t < 0 ? 0 : (t >= pd.V ? pd.V - 1 : t);
+    long long pos = (long long)cx.offs[r] + s;
+    pos = pos >= pd.max_pos ? pd.max_pos - 1 : pos;
+    float s1 = 0.f, s2 = 0.f;
+    for (int n = threadIdx.x; n < D; n += NTHR) {
+      const float v = __half2float(pd.emb[t * D + n]) * pd.xscale + pd.pe[pos * D + n];
+      pd.x[(size_t)m * D + n] = v;
+      s1 += v;
+      s2 = fmaf(v, v, s2);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+      s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    }
+    if (lane == 0) {
+      red[2 * warp] = s1;
+      red[2 * warp + 1] = s2;
+    }
+    csync();
+    for (int sl = threadIdx.x; sl < (D >> 5); sl += NTHR) {
+      float2 v = make_float2(0.f, 0.f);
+      if (sl == 0)
+        for (int w = 0; w < NWARP; ++w) v.x += red[2 * w], v.y += red[2 * w + 1];
+      reinterpret_cast<float2*>(pd.xstat)[(size_t)sl * DN_TOK + m] = v;
+    }
+    csync();
   }
 }
 
@@ -371,8 +431,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
   extern __shared__ __align__(1024) uint8_t smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + MAXSLOT;
-  uint64_t* accbar = empty + MAXSLOT;
-  uint64_t* bbar = accbar + 1;
+  uint64_t* accbar = empty + MAXSLOT;  // the accumulator of an item is complete
+  uint64_t* opbar = accbar + 1;        // an operand half has been read by its MMAs
+  uint64_t* bbar = opbar + 1;          // an operand copy has landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bbar + 1);
   int* pre = reinterpret_cast<int*>(smem + pd.off_pre);
   uint8_t* ringdata = smem + pd.off_ring;
@@ -390,6 +451,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       mbar_init(&empty[s], NWARP);
     }
     mbar_init(accbar, 1);
+    mbar_init(opbar, 1);
     mbar_init(bbar, 1);
     fence_barrier_init();
     pre[0] = 0;
@@ -458,7 +520,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
   }
   int* flag = reinterpret_cast<int*>(smem + pd.off_pre) + 1032;
   int* tflag = reinterpret_cast<int*>(smem + pd.off_pre) + 1035;
-  uint32_t accn = 0, issued = 0, bph = 0;
+  float* st = reinterpret_cast<float*>(smem + pd.off_stat);  // [64][mean, rstd] of the stage's LayerNorm
+  TcBar acc{accbar, 0, 0}, opb{opbar, 0, 0};
+  uint32_t bph = 0;
   bool copies = false;  // thread 0: an operand copy was issued (its completion is awaited before the CTA exits)
   const int D = pd.D, M = pd.M, V = pd.V;
   bool dead = false;
@@ -469,33 +533,52 @@ __global__ void __launch_bounds__(BLOCK, 1)
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     ring.dead = dead;
     const int gi = gemm_of(k);
-    const float* bias = gi >= 0 ? pd.g[gi].b + (k == K_OUT ? 0 : (long long)layer * pd.g[gi].N) : nullptr;
-    auto ln_stage = [&](int k0, int kr) { dn_ln(pd, k0, kr, bbuf); };
+    const int N = gi >= 0 ? pd.g[gi].N : 0;
+    const float* bias = gi >= 0 ? pd.g[gi].b + (k == K_OUT ? 0 : (long long)layer * N) : nullptr;
+    auto ln_stage = [&](int k0, int hs) { dn_ln_half(pd, st, k0, hs, bbuf); };
     auto copy_stage = [&](const __half* src) {
-      return [&, src](int k0, int kr) {
+      return [&, src](int k0, int hs) {
         if (threadIdx.x == 0 && !ring.dead) {
           copies = true;
-          if (!dn_stage_copy(src, k0, kr, bbuf, bbar, bph, ring.spin)) {
+          if (!dn_stage_copy(src, k0, hs, bbuf, bbar, bph, ring.spin)) {
             ring.dead = true;
             atomicExch(pd.err, E_ERR_TIMEOUT);
           }
         }
       };
     };
-    // residual epilogue: x[m][n] += y + b (this thread owns row n of every token)
-    const int N = gi >= 0 ? pd.g[gi].N : 0;
+    // residual epilogue: x[m][n] += y + b (this thread owns row n of every token), and the LayerNorm partial sums
+    // of the warp's 32 features per token for the next LayerNorm
     auto res_epi = [&](int n, int m0, const float (&v)[32]) {
-      if (n >= N) return;
-      const float b = bias[n];
-#pragma unroll 8
-      for (int m = 0; m < 32; ++m)
-        if (m0 + m < M) pd.x[(size_t)(m0 + m) * D + n] += v[m] + b;
+      const int lane_ = threadIdx.x & 31, slot = n >> 5;
+      const float b = n < N ? bias[n] : 0.f;
+      float xo[32];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) xo[m] = (m0 + m < M && n < N) ? __ldcg(pd.x + (size_t)(m0 + m) * D + n) : 0.f;
+#pragma unroll 4
+      for (int m = 0; m < 32; ++m) {
+        const float y = xo[m] + v[m] + b;
+        if (m0 + m < M && n < N) pd.x[(size_t)(m0 + m) * D + n] = y;
+        float s1 = (m0 + m < M && n < N) ? y : 0.f, s2 = s1 * s1;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+          s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (lane_ == 0 && m0 + m < M) reinterpret_cast<float2*>(pd.xstat)[(size_t)slot * DN_TOK + m0 + m] = make_float2(s1, s2);
+      }
     };
+    if (k == K_QKV || k == K_CQ || k == K_F1 || k == K_OUT) {
+      if (!dead && cx.so[gi] < cx.so[gi + 1]) {
+        dn_stats(pd, st);
+        csync();
+      }
+    }
     if (dead) {
     } else if (k == K_EMBED) {
-      embed_stage(pd, a, cx, c);
+      dn_embed(pd, a, cx, c);
     } else if (k == K_QKV) {
-      dn_gemm(pd, ring, cx, G_QKV, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+      dn_gemm(pd, ring, cx, G_QKV, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
         if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
@@ -505,9 +588,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_SATT) {
       dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
     } else if (k == K_WO || k == K_WCO) {
-      dn_gemm(pd, ring, cx, gi, tmem, accbar, accn, issued, bbuf, tflag, copy_stage(pd.obuf), res_epi);
+      dn_gemm(pd, ring, cx, gi, tmem, acc, opb, bbuf, tflag, copy_stage(pd.obuf), res_epi);
     } else if (k == K_CQ) {
-      dn_gemm(pd, ring, cx, G_CQ, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+      dn_gemm(pd, ring, cx, G_CQ, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
         if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
@@ -517,21 +600,21 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_XATT) {
       dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
-      dn_gemm(pd, ring, cx, G_F1, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+      dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
         if (n >= N) return;
         const float b = bias[n];
 #pragma unroll 8
         for (int m = 0; m < 32; ++m) pd.hbuf[dn_bidx(m0 + m, n)] = __float2half_rn(m0 + m < M ? fmaxf(v[m] + b, 0.f) : 0.f);
       });
     } else if (k == K_F2) {
-      dn_gemm(pd, ring, cx, G_F2, tmem, accbar, accn, issued, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
+      dn_gemm(pd, ring, cx, G_F2, tmem, acc, opb, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
     } else if (k == K_OUT) {
       for (int m = lane; m < M; m += 32) {  // this warp's running best per token
         os.wamax[warp * M + m] = -INFINITY;
         os.waidx[warp * M + m] = 0x7fffffff;
       }
       __syncwarp();
-      dn_gemm(pd, ring, cx, G_OUT, tmem, accbar, accn, issued, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
+      dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
         const bool in = n < V;
         const float b = in ? bias[n] : 0.f;
         const bool tmask = a.notime && n >= a.ft && n <= a.lt;
@@ -583,7 +666,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
   // before the CTA leaves: its last MMAs and operand copy (which a timed-out wait may have left running) are
   // done -- both always finish, so the default limit -- then the accumulator columns are freed
   if (threadIdx.x == 0) {
-    if (issued) mbar_wait(accbar, (issued - 1) & 1u, DEFAULT_SPIN);
+    if (acc.issued) mbar_wait(accbar, (acc.issued - 1) & 1u, DEFAULT_SPIN);
+    if (opb.issued) mbar_wait(opbar, (opb.issued - 1) & 1u, DEFAULT_SPIN);
     if (copies) mbar_wait(bbar, bph ^ 1u, DEFAULT_SPIN);
   }
   tc_fence_before();

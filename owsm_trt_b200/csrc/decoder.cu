@@ -113,7 +113,7 @@ struct PlanDev {
   uint32_t* tcnt;           // ranges arrived per tile (the last one resets it)
   __half* obuf;             // attention output in the token-operand layout [D / 8][8][64] halves
   __half* hbuf;             // FFN hidden in the token-operand layout [F / 8][8][64] halves
-  float* xstat;             // LayerNorm partial sums of the residual rows [D / 32][64 tokens][sum, sum of squares]
+  float* xstat;             // LayerNorm partial sums of the residual rows [D / 128][64 tokens][sum, sum of squares]
   int off_stat;             // shared memory: the stage's LayerNorm mean and 1 / std per token [64][2]
 };
 
@@ -2430,7 +2430,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.q2, (size_t)M * D, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.obuf, (size_t)D * DN_TOK, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.hbuf, (size_t)F * DN_TOK, tot))) return bail(rc);
-  if ((rc = dev_alloc(p->allocs, &pd.xstat, (size_t)(D / 32) * DN_TOK * 2, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xstat, (size_t)(D / DN_TILE) * DN_TOK * 2, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.part, (size_t)std::max(max_tiles_split, 1) * DN_TOK * DN_TILE, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.tcnt, (size_t)max_tiles, tot))) return bail(rc);
   p->tcnt_bytes = (size_t)max_tiles * sizeof(uint32_t);

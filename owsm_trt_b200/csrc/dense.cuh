@@ -55,7 +55,7 @@ __device__ __forceinline__ int dn_bidx(int m, int k) {
 }
 
 // LayerNorm statistics of the residual rows from the partial sums the residual's producers left (xstat
-// [D / 32][64 tokens][sum, sum of squares]: one slot per 32 features): mean and 1 / sqrt(var + eps) per token
+// [D / 128][64 tokens][sum, sum of squares]: one slot per 128-feature tile): mean and 1 / sqrt(var + eps) per token
 // into st[64][2] (shared memory), fp64 over the slots; padding tokens 0.
 __device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
   const int m = threadIdx.x;
@@ -63,7 +63,7 @@ __device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
     float mean = 0.f, rs = 0.f;
     if (m < pd.M) {
       double s1 = 0.0, s2 = 0.0;
-      for (int sl = 0; sl < (pd.D >> 5); ++sl) {
+      for (int sl = 0; sl < (pd.D >> 7); ++sl) {
         const float2 p = __ldcg(reinterpret_cast<const float2*>(pd.xstat) + (size_t)sl * DN_TOK + m);
         s1 += p.x;
         s2 += p.y;
@@ -78,22 +78,36 @@ __device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
 }
 
 // The normalised residual, features [k0, k0 + hs), into the token operand: a thread per (token, 8 features),
-// consecutive threads consecutive tokens (16-byte stores into one core matrix after another), padding zero.
+// consecutive threads consecutive tokens (16-byte stores into one core matrix after another), padding zero. Loads
+// for eight items per thread are in flight together (one L2 round trip per eight, not per item).
 __device__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, __half* bbuf) {
-  const int D = pd.D, M = pd.M;
-  for (int idx = threadIdx.x; idx < DN_TOK * (hs >> 3); idx += NTHR) {
-    const int m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
-    uint4 w = make_uint4(0u, 0u, 0u, 0u);
-    if (m < M) {
-      const float4* xr = reinterpret_cast<const float4*>(pd.x + (size_t)m * D + k0 + f);
-      const float4 u0 = __ldcg(xr), u1 = __ldcg(xr + 1);
-      const float mu = st[2 * m], rs = st[2 * m + 1];
-      w.x = pack_half2((u0.x - mu) * rs, (u0.y - mu) * rs);
-      w.y = pack_half2((u0.z - mu) * rs, (u0.w - mu) * rs);
-      w.z = pack_half2((u1.x - mu) * rs, (u1.y - mu) * rs);
-      w.w = pack_half2((u1.z - mu) * rs, (u1.w - mu) * rs);
+  const int D = pd.D, M = pd.M, n = DN_TOK * (hs >> 3);
+  constexpr int B = 8;
+  for (int base = threadIdx.x; base < n; base += B * NTHR) {
+    float4 u[B][2];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int idx = base + j * NTHR, m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
+      if (idx < n && m < M) {
+        const float4* xr = reinterpret_cast<const float4*>(pd.x + (size_t)m * D + k0 + f);
+        u[j][0] = __ldcg(xr);
+        u[j][1] = __ldcg(xr + 1);
+      }
     }
-    *reinterpret_cast<uint4*>(bbuf + dn_bidx(m, f)) = w;
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int idx = base + j * NTHR, m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
+      if (idx >= n) break;
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (m < M) {
+        const float mu = st[2 * m], rs = st[2 * m + 1];
+        w.x = pack_half2((u[j][0].x - mu) * rs, (u[j][0].y - mu) * rs);
+        w.y = pack_half2((u[j][0].z - mu) * rs, (u[j][0].w - mu) * rs);
+        w.z = pack_half2((u[j][1].x - mu) * rs, (u[j][1].y - mu) * rs);
+        w.w = pack_half2((u[j][1].z - mu) * rs, (u[j][1].w - mu) * rs);
+      }
+      *reinterpret_cast<uint4*>(bbuf + dn_bidx(m, f)) = w;
+    }
   }
   fence_async_smem();  // the operand is read by the tensor cores (async proxy)
 }
@@ -132,11 +146,11 @@ __device__ __forceinline__ void tc_wait(const PlanDev& pd, Ring& ring, TcBar& b)
 // One GEMM stage of the dense kernel on this CTA: its work items (tile, K range) in schedule order. An item
 // streams its token operand in halves: stage(k, hs) fills the operand with features [k, k + hs) (every consumer
 // thread calls it; thread 0 issues the half's MMAs after it), the accumulator collects all halves in TMEM.
-// epi(n, m0, v) finishes output row n of the tile for tokens m0 .. m0 + 31 from their complete sums v (warps 0-3,
-// one row per thread). A tile whose K is split (FFN2) writes each range's partial sums to global memory; the last
-// range to arrive adds all of them in range order (every thread a share, into shared memory) and finishes the tile.
+// epi(tile, y) finishes a tile from its complete sums y [64 tokens][128 rows] (shared memory; every consumer thread
+// calls it). A tile whose K is split (FFN2) writes each range's partial sums to global memory; the last range to
+// arrive adds all of them in range order (every thread a share) and finishes the tile.
 template <class Stage, class Epi>
-__device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, TcBar& acc, TcBar& opb,
+__device__ __noinline__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, TcBar& acc, TcBar& opb,
                         __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
@@ -145,10 +159,12 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = nb0; i < nb1; ++i) {
     const int item = cx.sb[i], tile = item / ns, split = item - tile * ns, k0 = split * kr;
+    event(cx, 100);
     for (int h = 0; h < nh; ++h) {
       if (h > 0) tc_wait(pd, ring, opb);  // the previous half's MMAs have read the operand
       stage(k0 + h * hs, hs);
       csync();
+      event(cx, 101);
       // (a failed call issues nothing more, so at most the last commit is outstanding when the CTA leaves)
       if (threadIdx.x == 0 && !ring.dead) {
         constexpr uint32_t idesc = idesc_f16_f32(DN_TILE, DN_TOK);
@@ -178,11 +194,14 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
           tc_commit(acc.bar);
           ++acc.issued;
         }
+        event(cx, 102);
       }
     }
     tc_wait(pd, ring, acc);
+    event(cx, 103);
     ring.i += nh * hslots;
-    const int row = warp * 32 + lane, n = tile * DN_TILE + row;
+    const int row = warp * 32 + lane;
+    float* ysm = reinterpret_cast<float*>(bbuf);  // the tile's sums [token][row] (the operand's MMAs are done)
     auto columns = [&](int m0, float (&v)[32]) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)m0, r);
@@ -190,12 +209,14 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
 #pragma unroll
       for (int m = 0; m < 32; ++m) v[m] = __uint_as_float(r[m]);
     };
+    bool finish = true;
     if (ns == 1) {
       if (warp < 4)
         for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
           float v[32];
           columns(m0, v);
-          epi(n, m0, v);
+#pragma unroll
+          for (int m = 0; m < 32; ++m) ysm[(m0 + m) * DN_TILE + row] = v[m];
         }
     } else {
       float* pt = pd.part + (size_t)tile * ns * DN_TOK * DN_TILE;  // [range][token][row]
@@ -210,10 +231,11 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
       csync();
       if (threadIdx.x == 0) *flag = (atomicAdd(&pd.tcnt[tile], 1u) == (uint32_t)(ns - 1));
       csync();
-      if (*flag) {
+      finish = *flag != 0;
+      if (finish) {
         __threadfence();
-        // the ranges' sums in range order into shared memory (the operand area: this CTA's MMAs are done)
-        float4* sum = reinterpret_cast<float4*>(bbuf);
+        // the ranges' sums in range order (every thread a share)
+        float4* sum = reinterpret_cast<float4*>(ysm);
         const float4* p4 = reinterpret_cast<const float4*>(pt);
         for (int q = threadIdx.x; q < DN_TOK * DN_TILE / 4; q += NTHR) {
           float4 t = __ldcg(p4 + q);
@@ -226,21 +248,14 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
           }
           sum[q] = t;
         }
-        csync();
-        if (warp < 4) {
-          const float* sf = reinterpret_cast<const float*>(bbuf);
-          for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
-            float v[32];
-#pragma unroll
-            for (int m = 0; m < 32; ++m) v[m] = sf[(m0 + m) * DN_TILE + row];
-            epi(n, m0, v);
-          }
-        }
         if (threadIdx.x == 0) atomicExch(&pd.tcnt[tile], 0u);
       }
     }
+    csync();
+    if (finish) epi(tile, ysm);
     tc_fence_before();
     csync();  // the next item's first MMA overwrites the accumulator (and its staging the operand)
+    event(cx, 104);
   }
 }
 
@@ -272,7 +287,7 @@ __device__ void dn_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, in
       red[2 * warp + 1] = s2;
     }
     csync();
-    for (int sl = threadIdx.x; sl < (D >> 5); sl += NTHR) {
+    for (int sl = threadIdx.x; sl < (D >> 7); sl += NTHR) {
       float2 v = make_float2(0.f, 0.f);
       if (sl == 0)
         for (int w = 0; w < NWARP; ++w) v.x += red[2 * w], v.y += red[2 * w + 1];
@@ -547,26 +562,74 @@ __global__ void __launch_bounds__(BLOCK, 1)
         }
       };
     };
-    // residual epilogue: x[m][n] += y + b (this thread owns row n of every token), and the LayerNorm partial sums
-    // of the warp's 32 features per token for the next LayerNorm
-    auto res_epi = [&](int n, int m0, const float (&v)[32]) {
-      const int lane_ = threadIdx.x & 31, slot = n >> 5;
-      const float b = n < N ? bias[n] : 0.f;
-      float xo[32];
+    // Tile epilogues on all consumer warps: item idx = (token m, rows 4 g .. 4 g + 3), a warp per token (its 32
+    // lanes cover the tile's 128 rows), loads of several items in flight per thread.
+    auto tile_loop = [&](int tokens, auto&& body) {
+      constexpr int B = 4;
+      const int n_items = tokens * 32;
+      for (int base = threadIdx.x; base < n_items; base += B * NTHR) {
+        float4 pre4[B];
 #pragma unroll
-      for (int m = 0; m < 32; ++m) xo[m] = (m0 + m < M && n < N) ? __ldcg(pd.x + (size_t)(m0 + m) * D + n) : 0.f;
-#pragma unroll 4
-      for (int m = 0; m < 32; ++m) {
-        const float y = xo[m] + v[m] + b;
-        if (m0 + m < M && n < N) pd.x[(size_t)(m0 + m) * D + n] = y;
-        float s1 = (m0 + m < M && n < N) ? y : 0.f, s2 = s1 * s1;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-          s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        for (int j = 0; j < B; ++j) {
+          const int idx = base + j * NTHR;
+          if (idx < n_items) pre4[j] = body.load(idx >> 5, idx & 31);
         }
-        if (lane_ == 0 && m0 + m < M) reinterpret_cast<float2*>(pd.xstat)[(size_t)slot * DN_TOK + m0 + m] = make_float2(s1, s2);
+#pragma unroll
+        for (int j = 0; j < B; ++j) {
+          const int idx = base + j * NTHR;
+          if (idx < n_items) body.apply(idx >> 5, idx & 31, pre4[j]);  // (warp-uniform: n_items % 32 == 0)
+        }
       }
+    };
+    struct NoLoad {
+      __device__ float4 load(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
+    };
+    // residual: x[m][n] += y + b, and the LayerNorm partial sums of the tile's 128 features per token
+    auto res_epi = [&](int tile, const float* y) {
+      struct Body {
+        const PlanDev& pd;
+        const float* y;
+        const float* bias;
+        int tile, D;
+        __device__ float4 load(int m, int g) const {
+          return __ldcg(reinterpret_cast<const float4*>(pd.x + (size_t)m * D + tile * DN_TILE) + g);
+        }
+        __device__ void apply(int m, int g, const float4& xo) const {
+          const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+          const float4 r = make_float4(xo.x + v.x + b.x, xo.y + v.y + b.y, xo.z + v.z + b.z, xo.w + v.w + b.w);
+          reinterpret_cast<float4*>(pd.x + (size_t)m * D + tile * DN_TILE)[g] = r;
+          float s1 = (r.x + r.y) + (r.z + r.w);
+          float s2 = fmaf(r.x, r.x, fmaf(r.y, r.y, fmaf(r.z, r.z, r.w * r.w)));
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+          }
+          if ((threadIdx.x & 31) == 0) reinterpret_cast<float2*>(pd.xstat)[(size_t)tile * DN_TOK + m] = make_float2(s1, s2);
+        }
+      } body{pd, y, bias, tile, D};
+      tile_loop(M, body);
+    };
+    // fp16 outputs [M][ld] (q / k / v, cross queries): y + b
+    auto half_epi = [&](__half* out, int ld) {
+      return [&, out, ld](int tile, const float* y) {
+        struct Body : NoLoad {
+          const float* y;
+          const float* bias;
+          __half* out;
+          int tile, ld;
+          __device__ void apply(int m, int g, const float4&) const {
+            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+            const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+            uint2 h;
+            h.x = pack_half2(v.x + b.x, v.y + b.y);
+            h.y = pack_half2(v.z + b.z, v.w + b.w);
+            *reinterpret_cast<uint2*>(out + (size_t)m * ld + tile * DN_TILE + 4 * g) = h;
+          }
+        } body{{}, y, bias, out, tile, ld};
+        tile_loop(M, body);
+      };
     };
     if (k == K_QKV || k == K_CQ || k == K_F1 || k == K_OUT) {
       if (!dead && cx.so[gi] < cx.so[gi + 1]) {
@@ -578,33 +641,34 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_EMBED) {
       dn_embed(pd, a, cx, c);
     } else if (k == K_QKV) {
-      dn_gemm(pd, ring, cx, G_QKV, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
-        if (n >= N) return;
-        const float b = bias[n];
-#pragma unroll 8
-        for (int m = 0; m < 32; ++m)
-          if (m0 + m < M) pd.qkv[(size_t)(m0 + m) * 3 * D + n] = __float2half_rn(v[m] + b);
-      });
+      dn_gemm(pd, ring, cx, G_QKV, tmem, acc, opb, bbuf, tflag, ln_stage, half_epi(pd.qkv, 3 * D));
     } else if (k == K_SATT) {
       dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
     } else if (k == K_WO || k == K_WCO) {
       dn_gemm(pd, ring, cx, gi, tmem, acc, opb, bbuf, tflag, copy_stage(pd.obuf), res_epi);
     } else if (k == K_CQ) {
-      dn_gemm(pd, ring, cx, G_CQ, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
-        if (n >= N) return;
-        const float b = bias[n];
-#pragma unroll 8
-        for (int m = 0; m < 32; ++m)
-          if (m0 + m < M) pd.q2[(size_t)(m0 + m) * D + n] = __float2half_rn(v[m] + b);
-      });
+      dn_gemm(pd, ring, cx, G_CQ, tmem, acc, opb, bbuf, tflag, ln_stage, half_epi(pd.q2, D));
     } else if (k == K_XATT) {
       dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
-      dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
-        if (n >= N) return;
-        const float b = bias[n];
-#pragma unroll 8
-        for (int m = 0; m < 32; ++m) pd.hbuf[dn_bidx(m0 + m, n)] = __float2half_rn(m0 + m < M ? fmaxf(v[m] + b, 0.f) : 0.f);
+      dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int tile, const float* y) {
+        struct Body : NoLoad {  // ReLU(y + b) into the FFN2 operand layout; padding tokens zero
+          const float* y;
+          const float* bias;
+          __half* out;
+          int tile, M;
+          __device__ void apply(int m, int g, const float4&) const {
+            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+            const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+            uint2 h = make_uint2(0u, 0u);
+            if (m < M) {
+              h.x = pack_half2(fmaxf(v.x + b.x, 0.f), fmaxf(v.y + b.y, 0.f));
+              h.y = pack_half2(fmaxf(v.z + b.z, 0.f), fmaxf(v.w + b.w, 0.f));
+            }
+            *reinterpret_cast<uint2*>(out + dn_bidx(m, tile * DN_TILE + 4 * g)) = h;
+          }
+        } body{{}, y, bias, pd.hbuf, tile, M};
+        tile_loop(DN_TOK, body);
       });
     } else if (k == K_F2) {
       dn_gemm(pd, ring, cx, G_F2, tmem, acc, opb, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
@@ -614,31 +678,46 @@ __global__ void __launch_bounds__(BLOCK, 1)
         os.waidx[warp * M + m] = 0x7fffffff;
       }
       __syncwarp();
-      dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int n, int m0, const float (&v)[32]) {
-        const bool in = n < V;
-        const float b = in ? bias[n] : 0.f;
-        const bool tmask = a.notime && n >= a.ft && n <= a.lt;
-#pragma unroll 1
-        for (int mm = 0; mm < 32 && m0 + mm < M; ++mm) {
-          const int m = m0 + mm;
-          const float y = v[mm] + b;
-          if (in) a.logits[(size_t)m * V + n] = y;
-          float bv = (in && !(tmask && a.notime[m / pd.S])) ? y : -INFINITY;
-          int bi = in ? n : 0x7fffffff;
+      dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int tile, const float* y) {
+        struct Body : NoLoad {  // logits, and each warp's running best per token (first index on ties)
+          const CallArgs& a;
+          const float* y;
+          const float* bias;
+          OutState& os;
+          int tile, M, V, S;
+          __device__ void apply(int m, int g, const float4&) const {
+            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+            const int n0 = tile * DN_TILE + 4 * g;
+            const bool masked = a.notime && a.notime[m / S];
+            float bv = -INFINITY;
+            int bi = 0x7fffffff;
 #pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            merge_best(bv, bi, ov, oi);
+            for (int e = 0; e < 4; ++e) {
+              const int n = n0 + e;
+              if (n < V) {
+                const float yv = vv[e] + bias[n];
+                a.logits[(size_t)m * V + n] = yv;
+                if (!(masked && n >= a.ft && n <= a.lt)) merge_best(bv, bi, yv, n);
+              }
+            }
+#pragma unroll
+            for (int o = 16; o; o >>= 1) {
+              const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+              const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+              merge_best(bv, bi, ov, oi);
+            }
+            const int w = threadIdx.x >> 5;
+            if ((threadIdx.x & 31) == 0) merge_best(os.wamax[w * M + m], os.waidx[w * M + m], bv, bi);
           }
-          if (lane == 0) merge_best(os.wamax[warp * M + m], os.waidx[warp * M + m], bv, bi);
-        }
+        } body{{}, a, y, bias, os, tile, M, V, pd.S};
+        tile_loop(M, body);
       });
       csync();
       for (int m = threadIdx.x; m < M; m += NTHR) {
         float bv = os.amax[m];
         int bi = os.aidx[m];
-        for (int w = 0; w < 4; ++w) merge_best(bv, bi, os.wamax[w * M + m], os.waidx[w * M + m]);
+        for (int w = 0; w < NWARP; ++w) merge_best(bv, bi, os.wamax[w * M + m], os.waidx[w * M + m]);
         os.amax[m] = bv;
         os.aidx[m] = bi;
       }

@@ -2456,8 +2456,10 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   cudaDeviceProp prop;
   CUDA_TRY(cudaGetDeviceProperties(&prop, h->device));
   const size_t limit = prop.sharedMemPerBlockOptin;
-  if (off_ring + work + 2 * (SLOT + 128) > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small for the dense kernel"));
-  const int nslot = (int)std::min<size_t>((limit - off_ring - work) / (SLOT + 128), 6);
+  // ring slots of exactly 32 KB (no bias tails here), so the work area -- the token operand, swizzled in 1024-byte
+  // groups -- starts 1024-byte aligned
+  if (off_ring + work + 2 * SLOT > limit) return bail(fail(OWSM_DEC_ERR_LIMIT, "shared memory too small for the dense kernel"));
+  const int nslot = (int)std::min<size_t>((limit - off_ring - work) / SLOT, 6);
   pd.nslot = nslot;
   pd.slot = SLOT;
   pd.apos = SLOT / (DK * 2);
@@ -2468,7 +2470,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   pd.off_out = (int)off_out;
   pd.off_stat = (int)off_stat;
   pd.off_ring = (int)off_ring;
-  pd.sstride = SLOT + 128;
+  pd.sstride = SLOT;
   pd.off_work = (int)(off_ring + (size_t)nslot * pd.sstride);
   pd.work_bytes = (int)work;
   p->smem = (size_t)pd.off_work + work;

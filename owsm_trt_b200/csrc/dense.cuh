@@ -48,10 +48,12 @@ __host__ __device__ constexpr int dn_halves(int kr) {
   return n;
 }
 
-// Index (halves) of element (token m, feature k) in the token-operand layout with DN_MT token groups: k groups of
-// DN_MT core matrices, a core matrix 8 tokens x 8 features, a token's 8 features contiguous.
+// Index (halves) of element (token m, feature k) in the token-operand layout: blocks of 64 features (8 KB: 64
+// token rows of 128 bytes), a row's 16-byte chunks XOR-swizzled by the token's row within its group of 8 -- the
+// K-major 128-byte-swizzle layout of the tensor cores (8-row groups 1024 bytes apart), so a warp writing one
+// token's consecutive 8-feature chunks touches every bank once. Blocks must start 1024-byte aligned.
 __device__ __forceinline__ int dn_bidx(int m, int k) {
-  return (((k >> 3) * DN_MT + (m >> 3)) << 6) + ((m & 7) << 3) + (k & 7);
+  return ((k >> 6) << 12) + (m << 6) + ((((k >> 3) & 7) ^ (m & 7)) << 3) + (k & 7);
 }
 
 // LayerNorm statistics of the residual rows from the partial sums the residual's producers left (xstat
@@ -78,16 +80,16 @@ __device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
 }
 
 // The normalised residual, features [k0, k0 + hs), into the token operand: a thread per (token, 8 features),
-// consecutive threads consecutive tokens (16-byte stores into one core matrix after another), padding zero. Loads
-// for eight items per thread are in flight together (one L2 round trip per eight, not per item).
-__device__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, __half* bbuf) {
+// consecutive threads consecutive chunks of a token (coalesced loads, swizzled conflict-free 16-byte stores),
+// padding zero. Loads for eight items per thread are in flight together.
+__device__ __noinline__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, __half* bbuf) {
   const int D = pd.D, M = pd.M, n = DN_TOK * (hs >> 3);
   constexpr int B = 8;
   for (int base = threadIdx.x; base < n; base += B * NTHR) {
     float4 u[B][2];
 #pragma unroll
     for (int j = 0; j < B; ++j) {
-      const int idx = base + j * NTHR, m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
+      const int idx = base + j * NTHR, m = idx / (hs >> 3), f = (idx % (hs >> 3)) << 3;
       if (idx < n && m < M) {
         const float4* xr = reinterpret_cast<const float4*>(pd.x + (size_t)m * D + k0 + f);
         u[j][0] = __ldcg(xr);
@@ -96,7 +98,7 @@ __device__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, _
     }
 #pragma unroll
     for (int j = 0; j < B; ++j) {
-      const int idx = base + j * NTHR, m = idx & (DN_TOK - 1), f = (idx >> 6) << 3;
+      const int idx = base + j * NTHR, m = idx / (hs >> 3), f = (idx % (hs >> 3)) << 3;
       if (idx >= n) break;
       uint4 w = make_uint4(0u, 0u, 0u, 0u);
       if (m < M) {
@@ -121,7 +123,7 @@ __device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int hs,
   asm volatile("fence.proxy.async.global;" ::: "memory");
   const uint32_t bytes = (uint32_t)hs * DN_TOK * 2;
   mbar_arrive_expect_tx(bar, bytes);
-  bulk_g2s_nohint(bbuf, src + (size_t)(k0 >> 3) * DN_MT * 64, bytes, bar);
+  bulk_g2s_nohint(bbuf, src + (size_t)(k0 >> 6) * (DN_TOK * 64), bytes, bar);
   const bool ok = mbar_wait(bar, ph, spin);
   ph ^= 1u;
   return ok;
@@ -150,7 +152,7 @@ __device__ __forceinline__ void tc_wait(const PlanDev& pd, Ring& ring, TcBar& b)
 // calls it). A tile whose K is split (FFN2) writes each range's partial sums to global memory; the last range to
 // arrive adds all of them in range order (every thread a share) and finishes the tile.
 template <class Stage, class Epi>
-__device__ __noinline__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, TcBar& acc, TcBar& opb,
+__device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, uint32_t tmem, TcBar& acc, TcBar& opb,
                         __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
@@ -179,7 +181,7 @@ __device__ __noinline__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& c
             for (int kk = 0; kk < 4; ++kk) {
               const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the half
               tc_mma_f16(tmem, plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128),
-                         plain_desc(bb + (uint32_t)(kl >> 3) * DN_MT * 128, DN_MT * 128, 128), idesc,
+                         sw128_desc(bb + (uint32_t)(kl >> 6) * (DN_TOK * 128) + (uint32_t)(kl & 63) * 2), idesc,
                          (h | j | ch | kk) != 0);
             }
           // the slot goes back to the producer when these MMAs have read it (one arrival), the other warps'
@@ -202,31 +204,22 @@ __device__ __noinline__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& c
     ring.i += nh * hslots;
     const int row = warp * 32 + lane;
     float* ysm = reinterpret_cast<float*>(bbuf);  // the tile's sums [token][row] (the operand's MMAs are done)
-    auto columns = [&](int m0, float (&v)[32]) {
+    // 32 token columns of this thread's accumulator row at a time, straight from the TMEM load's registers
+    auto columns_to = [&](int m0, float* dst, int stride) {
       uint32_t r[32];
       tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)m0, r);
       tmem_ld_wait();
 #pragma unroll
-      for (int m = 0; m < 32; ++m) v[m] = __uint_as_float(r[m]);
+      for (int m = 0; m < 32; ++m) dst[(size_t)m * stride] = __uint_as_float(r[m]);
     };
     bool finish = true;
     if (ns == 1) {
       if (warp < 4)
-        for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
-          float v[32];
-          columns(m0, v);
-#pragma unroll
-          for (int m = 0; m < 32; ++m) ysm[(m0 + m) * DN_TILE + row] = v[m];
-        }
+        for (int m0 = 0; m0 < DN_TOK; m0 += 32) columns_to(m0, ysm + m0 * DN_TILE + row, DN_TILE);
     } else {
       float* pt = pd.part + (size_t)tile * ns * DN_TOK * DN_TILE;  // [range][token][row]
       if (warp < 4)
-        for (int m0 = 0; m0 < DN_TOK; m0 += 32) {
-          float v[32];
-          columns(m0, v);
-#pragma unroll
-          for (int m = 0; m < 32; ++m) __stcg(pt + ((size_t)split * DN_TOK + m0 + m) * DN_TILE + row, v[m]);
-        }
+        for (int m0 = 0; m0 < DN_TOK; m0 += 32) columns_to(m0, pt + ((size_t)split * DN_TOK + m0) * DN_TILE + row, DN_TILE);
       __threadfence();
       csync();
       if (threadIdx.x == 0) *flag = (atomicAdd(&pd.tcnt[tile], 1u) == (uint32_t)(ns - 1));
@@ -261,7 +254,7 @@ __device__ __noinline__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& c
 
 // Embedding into the residual rows (a CTA per token) and their LayerNorm partial sums (slot 0 holds the row's
 // sums, the other slots zero).
-__device__ void dn_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
+__device__ __noinline__ void dn_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
   const int D = pd.D, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* red = cx.red;  // [2 * NWARP]
   for (int m = c; m < pd.M; m += pd.P) {
@@ -440,6 +433,102 @@ __device__ void dn_chunks(const PlanDev& pd, const CallArgs& a, const Ctx& cx, c
   }
 }
 
+// ---- tile epilogues: every consumer thread, item idx = (token m, rows 4 g .. 4 g + 3) of a tile's sums
+// y [64 tokens][128 rows] (shared memory), a warp per token (its 32 lanes cover the 128 rows); out of line (once
+// per tile), so the stage loops keep their registers.
+
+// residual: x[m][n] += y + b, and the LayerNorm partial sums of the tile's 128 features per token
+__device__ __noinline__ void dn_epi_res(const PlanDev& pd, const float* y, const float* bias, int tile) {
+  constexpr int B = 4;
+  const int D = pd.D, n_items = pd.M * 32;
+  for (int base = threadIdx.x; base < n_items; base += B * NTHR) {
+    float4 xo[B];
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int idx = base + j * NTHR;
+      if (idx < n_items) xo[j] = __ldcg(reinterpret_cast<const float4*>(pd.x + (size_t)(idx >> 5) * D + tile * DN_TILE) + (idx & 31));
+    }
+#pragma unroll
+    for (int j = 0; j < B; ++j) {
+      const int idx = base + j * NTHR, m = idx >> 5, g = idx & 31;
+      if (idx >= n_items) break;  // (warp-uniform: n_items is a multiple of 32)
+      const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+      const float4 r = make_float4(xo[j].x + v.x + b.x, xo[j].y + v.y + b.y, xo[j].z + v.z + b.z, xo[j].w + v.w + b.w);
+      reinterpret_cast<float4*>(pd.x + (size_t)m * D + tile * DN_TILE)[g] = r;
+      float s1 = (r.x + r.y) + (r.z + r.w);
+      float s2 = fmaf(r.x, r.x, fmaf(r.y, r.y, fmaf(r.z, r.z, r.w * r.w)));
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      }
+      if ((threadIdx.x & 31) == 0) reinterpret_cast<float2*>(pd.xstat)[(size_t)tile * DN_TOK + m] = make_float2(s1, s2);
+    }
+  }
+}
+
+// fp16 outputs out[m][ld] (q / k / v, cross queries): y + b
+__device__ __noinline__ void dn_epi_half(const PlanDev& pd, const float* y, const float* bias, int tile, __half* out,
+                                         int ld) {
+  for (int idx = threadIdx.x; idx < pd.M * 32; idx += NTHR) {
+    const int m = idx >> 5, g = idx & 31;
+    const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+    const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+    uint2 h;
+    h.x = pack_half2(v.x + b.x, v.y + b.y);
+    h.y = pack_half2(v.z + b.z, v.w + b.w);
+    *reinterpret_cast<uint2*>(out + (size_t)m * ld + tile * DN_TILE + 4 * g) = h;
+  }
+}
+
+// ReLU(y + b) into the FFN2 operand layout; padding tokens zero
+__device__ __noinline__ void dn_epi_relu(const PlanDev& pd, const float* y, const float* bias, int tile) {
+  for (int idx = threadIdx.x; idx < DN_TOK * 32; idx += NTHR) {
+    const int m = idx >> 5, g = idx & 31;
+    uint2 h = make_uint2(0u, 0u);
+    if (m < pd.M) {
+      const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+      const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
+      h.x = pack_half2(fmaxf(v.x + b.x, 0.f), fmaxf(v.y + b.y, 0.f));
+      h.y = pack_half2(fmaxf(v.z + b.z, 0.f), fmaxf(v.w + b.w, 0.f));
+    }
+    *reinterpret_cast<uint2*>(pd.hbuf + dn_bidx(m, tile * DN_TILE + 4 * g)) = h;
+  }
+}
+
+// logits = y + b, and each warp's running best per token (first index on ties; ids first_time .. last_time left
+// out for the rows flagged <notimestamps>)
+__device__ __noinline__ void dn_epi_out(const PlanDev& pd, const CallArgs& a, const float* y, const float* bias, int tile,
+                                        OutState& os) {
+  const int M = pd.M, V = pd.V, w = threadIdx.x >> 5;
+  for (int idx = threadIdx.x; idx < M * 32; idx += NTHR) {
+    const int m = idx >> 5, g = idx & 31;
+    const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    const int n0 = tile * DN_TILE + 4 * g;
+    const bool masked = a.notime && a.notime[m / pd.S];
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int n = n0 + e;
+      if (n < V) {
+        const float yv = vv[e] + bias[n];
+        a.logits[(size_t)m * V + n] = yv;
+        if (!(masked && n >= a.ft && n <= a.lt)) merge_best(bv, bi, yv, n);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      merge_best(bv, bi, ov, oi);
+    }
+    if ((threadIdx.x & 31) == 0) merge_best(os.wamax[w * M + m], os.waidx[w * M + m], bv, bi);
+  }
+}
+
 template <int QM, bool WIDE>
 __global__ void __launch_bounds__(BLOCK, 1)
     decoder_dense_kernel(const __grid_constant__ PlanDev pd, const __grid_constant__ CallArgs a) {
@@ -528,6 +617,11 @@ __global__ void __launch_bounds__(BLOCK, 1)
   }
 
   Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, 0, pd.max_spin, pd.err, false, 0ull, pd.ts != nullptr};
+  bool dead = false;
+  if ((smem_u32(bbuf) & 1023u) != 0) {  // the swizzled operand needs 1024-byte alignment: refuse rather than misread
+    if (threadIdx.x == 0) atomicExch(pd.err, E_ERR_TIMEOUT);
+    dead = true;
+  }
   OutState os = carve_out(smem + pd.off_out, pd.M, false);
   for (int m = threadIdx.x; m < pd.M; m += NTHR) {
     os.amax[m] = -INFINITY;
@@ -540,7 +634,6 @@ __global__ void __launch_bounds__(BLOCK, 1)
   uint32_t bph = 0;
   bool copies = false;  // thread 0: an operand copy was issued (its completion is awaited before the CTA exits)
   const int D = pd.D, M = pd.M, V = pd.V;
-  bool dead = false;
   for (int g = 0; g < n_stages; ++g) {
     int layer;
     const Kind k = stage_kind(pd, g, layer);
@@ -562,74 +655,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
         }
       };
     };
-    // Tile epilogues on all consumer warps: item idx = (token m, rows 4 g .. 4 g + 3), a warp per token (its 32
-    // lanes cover the tile's 128 rows), loads of several items in flight per thread.
-    auto tile_loop = [&](int tokens, auto&& body) {
-      constexpr int B = 4;
-      const int n_items = tokens * 32;
-      for (int base = threadIdx.x; base < n_items; base += B * NTHR) {
-        float4 pre4[B];
-#pragma unroll
-        for (int j = 0; j < B; ++j) {
-          const int idx = base + j * NTHR;
-          if (idx < n_items) pre4[j] = body.load(idx >> 5, idx & 31);
-        }
-#pragma unroll
-        for (int j = 0; j < B; ++j) {
-          const int idx = base + j * NTHR;
-          if (idx < n_items) body.apply(idx >> 5, idx & 31, pre4[j]);  // (warp-uniform: n_items % 32 == 0)
-        }
-      }
-    };
-    struct NoLoad {
-      __device__ float4 load(int, int) const { return make_float4(0.f, 0.f, 0.f, 0.f); }
-    };
-    // residual: x[m][n] += y + b, and the LayerNorm partial sums of the tile's 128 features per token
-    auto res_epi = [&](int tile, const float* y) {
-      struct Body {
-        const PlanDev& pd;
-        const float* y;
-        const float* bias;
-        int tile, D;
-        __device__ float4 load(int m, int g) const {
-          return __ldcg(reinterpret_cast<const float4*>(pd.x + (size_t)m * D + tile * DN_TILE) + g);
-        }
-        __device__ void apply(int m, int g, const float4& xo) const {
-          const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
-          const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
-          const float4 r = make_float4(xo.x + v.x + b.x, xo.y + v.y + b.y, xo.z + v.z + b.z, xo.w + v.w + b.w);
-          reinterpret_cast<float4*>(pd.x + (size_t)m * D + tile * DN_TILE)[g] = r;
-          float s1 = (r.x + r.y) + (r.z + r.w);
-          float s2 = fmaf(r.x, r.x, fmaf(r.y, r.y, fmaf(r.z, r.z, r.w * r.w)));
-#pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
-            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-          }
-          if ((threadIdx.x & 31) == 0) reinterpret_cast<float2*>(pd.xstat)[(size_t)tile * DN_TOK + m] = make_float2(s1, s2);
-        }
-      } body{pd, y, bias, tile, D};
-      tile_loop(M, body);
-    };
-    // fp16 outputs [M][ld] (q / k / v, cross queries): y + b
+    auto res_epi = [&](int tile, const float* y) { dn_epi_res(pd, y, bias, tile); };
     auto half_epi = [&](__half* out, int ld) {
-      return [&, out, ld](int tile, const float* y) {
-        struct Body : NoLoad {
-          const float* y;
-          const float* bias;
-          __half* out;
-          int tile, ld;
-          __device__ void apply(int m, int g, const float4&) const {
-            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
-            const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
-            uint2 h;
-            h.x = pack_half2(v.x + b.x, v.y + b.y);
-            h.y = pack_half2(v.z + b.z, v.w + b.w);
-            *reinterpret_cast<uint2*>(out + (size_t)m * ld + tile * DN_TILE + 4 * g) = h;
-          }
-        } body{{}, y, bias, out, tile, ld};
-        tile_loop(M, body);
-      };
+      return [&, out, ld](int tile, const float* y) { dn_epi_half(pd, y, bias, tile, out, ld); };
     };
     if (k == K_QKV || k == K_CQ || k == K_F1 || k == K_OUT) {
       if (!dead && cx.so[gi] < cx.so[gi + 1]) {
@@ -651,25 +679,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_XATT) {
       dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
-      dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int tile, const float* y) {
-        struct Body : NoLoad {  // ReLU(y + b) into the FFN2 operand layout; padding tokens zero
-          const float* y;
-          const float* bias;
-          __half* out;
-          int tile, M;
-          __device__ void apply(int m, int g, const float4&) const {
-            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
-            const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
-            uint2 h = make_uint2(0u, 0u);
-            if (m < M) {
-              h.x = pack_half2(fmaxf(v.x + b.x, 0.f), fmaxf(v.y + b.y, 0.f));
-              h.y = pack_half2(fmaxf(v.z + b.z, 0.f), fmaxf(v.w + b.w, 0.f));
-            }
-            *reinterpret_cast<uint2*>(out + dn_bidx(m, tile * DN_TILE + 4 * g)) = h;
-          }
-        } body{{}, y, bias, pd.hbuf, tile, M};
-        tile_loop(DN_TOK, body);
-      });
+      dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage,
+              [&](int tile, const float* y) { dn_epi_relu(pd, y, bias, tile); });
     } else if (k == K_F2) {
       dn_gemm(pd, ring, cx, G_F2, tmem, acc, opb, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
     } else if (k == K_OUT) {
@@ -678,41 +689,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
         os.waidx[warp * M + m] = 0x7fffffff;
       }
       __syncwarp();
-      dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage, [&](int tile, const float* y) {
-        struct Body : NoLoad {  // logits, and each warp's running best per token (first index on ties)
-          const CallArgs& a;
-          const float* y;
-          const float* bias;
-          OutState& os;
-          int tile, M, V, S;
-          __device__ void apply(int m, int g, const float4&) const {
-            const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
-            const float vv[4] = {v.x, v.y, v.z, v.w};
-            const int n0 = tile * DN_TILE + 4 * g;
-            const bool masked = a.notime && a.notime[m / S];
-            float bv = -INFINITY;
-            int bi = 0x7fffffff;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int n = n0 + e;
-              if (n < V) {
-                const float yv = vv[e] + bias[n];
-                a.logits[(size_t)m * V + n] = yv;
-                if (!(masked && n >= a.ft && n <= a.lt)) merge_best(bv, bi, yv, n);
-              }
-            }
-#pragma unroll
-            for (int o = 16; o; o >>= 1) {
-              const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-              const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-              merge_best(bv, bi, ov, oi);
-            }
-            const int w = threadIdx.x >> 5;
-            if ((threadIdx.x & 31) == 0) merge_best(os.wamax[w * M + m], os.waidx[w * M + m], bv, bi);
-          }
-        } body{{}, a, y, bias, os, tile, M, V, pd.S};
-        tile_loop(M, body);
-      });
+      dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage,
+              [&](int tile, const float* y) { dn_epi_out(pd, a, y, bias, tile, os); });
       csync();
       for (int m = threadIdx.x; m < M; m += NTHR) {
         float bv = os.amax[m];

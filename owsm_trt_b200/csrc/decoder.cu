@@ -114,6 +114,9 @@ struct PlanDev {
   __half* obuf;             // attention output in the token-operand layout [D / 8][8][64] halves
   __half* hbuf;             // FFN hidden in the token-operand layout [F / 8][8][64] halves
   float* xstat;             // LayerNorm partial sums of the residual rows [D / 128][64 tokens][sum, sum of squares]
+  const float* gcs[NGEMM];  // row sums of the LayerNorm-folded fp16 weights [layer][N] (the GEMMs after a LayerNorm)
+  __half* xop;              // the residual rows as the token operand: fp16 high parts [D / 64 blocks][64][64], then
+                            // the low parts (x - high) in the same layout
   int off_stat;             // shared memory: the stage's LayerNorm mean and 1 / std per token [64][2]
 };
 
@@ -1859,6 +1862,7 @@ struct OwsmDec {
                  // 3: dense kernel or fail
   __half* gt[NGEMM] = {};  // weights in 128-row tiles for the dense kernel (made by its first plan)
   long long gtl[NGEMM] = {};
+  float* gcs[NGEMM] = {};  // their row sums, for the GEMMs after a LayerNorm
   // Profiling aid: with OWSM_DEC_NO_COOP set when the handle is made, cluster-kernel calls are launched
   // without the cooperative attribute (the profiler rejects cooperative cluster launches). The grid-wide
   // barrier then relies on all CTAs being resident, which holds when the call runs alone (one CTA per SM,
@@ -2346,6 +2350,13 @@ static int make_tiles(OwsmDec* h) {
     CUDA_TRY(cudaGetLastError());
     h->gt[gi] = t;
     h->gtl[gi] = per;
+    if (gi == G_QKV || gi == G_CQ || gi == G_F1 || gi == G_OUT) {
+      float* cs = nullptr;
+      if ((rc = dev_alloc(h->allocs, &cs, (size_t)gw.N * layers))) return rc;
+      tile_rowsum_kernel<<<(gw.N * layers + 255) / 256, 256>>>(t, gw.N, gw.K, layers, per, cs);
+      CUDA_TRY(cudaGetLastError());
+      h->gcs[gi] = cs;
+    }
   }
   CUDA_TRY(cudaDeviceSynchronize());
   return OWSM_DEC_OK;
@@ -2388,6 +2399,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
     pd.g[gi] = h->g[gi];
     pd.gt[gi] = h->gt[gi];
     pd.gtl[gi] = h->gtl[gi];
+    pd.gcs[gi] = h->gcs[gi];
     pd.nsplit[gi] = dn_splits(h->g[gi].K);
     const int nt = (h->g[gi].N + DN_TILE - 1) / DN_TILE;
     max_tiles = std::max(max_tiles, nt);
@@ -2431,6 +2443,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.obuf, (size_t)D * DN_TOK, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.hbuf, (size_t)F * DN_TOK, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.xstat, (size_t)(D / DN_TILE) * DN_TOK * 2, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xop, (size_t)2 * D * DN_TOK, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.part, (size_t)std::max(max_tiles_split, 1) * DN_TOK * DN_TILE, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.tcnt, (size_t)max_tiles, tot))) return bail(rc);
   p->tcnt_bytes = (size_t)max_tiles * sizeof(uint32_t);
@@ -2439,10 +2452,10 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);
   // shared memory: barriers | utterance prefix sums + flags | work items | row offsets | argmax state | ring | work
-  int maxkr = 0;  // the largest operand half
+  int maxkr = 0;  // the largest operand part (features x 2 for the high / low residual parts)
   for (int gi = 0; gi < NGEMM; ++gi) {
-    const int kr = h->g[gi].K / pd.nsplit[gi];
-    maxkr = std::max(maxkr, kr / dn_halves(kr));
+    const int kr = h->g[gi].K / pd.nsplit[gi], hilo = dn_hilo(gi);
+    maxkr = std::max(maxkr, (kr / dn_parts(kr, hilo)) * (hilo ? 2 : 1));
   }
   const size_t off_pre = 256;
   const size_t off_sched = (off_pre + 4 * 1072 + 127) & ~(size_t)127;

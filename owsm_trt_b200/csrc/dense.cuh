@@ -42,8 +42,15 @@ __host__ __device__ constexpr int dn_splits(int K) {
   while (K % n || (K / n) % 128) ++n;
   return n;
 }
-__host__ __device__ constexpr int dn_halves(int kr) {
-  int n = (kr + DN_KR - 1) / DN_KR;
+// The GEMMs after a LayerNorm read the residual itself, as fp16 high and low parts (two MMAs per K slice), and
+// apply the normalisation in the epilogue: y = rstd (W' x - mean c) + b', c = W' 1 (the reference megakernel's
+// algebra, src/owsm_trt/megakernel.py:82-117, :150-250). Their operand parts carry both halves of a K range.
+__host__ __device__ constexpr bool dn_hilo(int gi) { return gi == 0 /*QKV*/ || gi == 2 /*CQ*/ || gi == 4 /*F1*/ || gi == 6 /*OUT*/; }
+// The parts an item streams its token operand in: at most DN_KR / 2 features with high and low parts (64 KB), at
+// most DN_KR otherwise, a multiple of 128 (a whole number of two-chunk ring slots).
+__host__ __device__ constexpr int dn_parts(int kr, bool hilo) {
+  const int mx = hilo ? DN_KR / 2 : DN_KR;
+  int n = (kr + mx - 1) / mx;
   while (kr % n || (kr / n) % 128) ++n;
   return n;
 }
@@ -79,51 +86,18 @@ __device__ __forceinline__ void dn_stats(const PlanDev& pd, float* st) {
   }
 }
 
-// The normalised residual, features [k0, k0 + hs), into the token operand: a thread per (token, 8 features),
-// consecutive threads consecutive chunks of a token (coalesced loads, swizzled conflict-free 16-byte stores),
-// padding zero. Loads for eight items per thread are in flight together.
-__device__ __noinline__ void dn_ln_half(const PlanDev& pd, const float* st, int k0, int hs, __half* bbuf) {
-  const int D = pd.D, M = pd.M, n = DN_TOK * (hs >> 3);
-  constexpr int B = 8;
-  for (int base = threadIdx.x; base < n; base += B * NTHR) {
-    float4 u[B][2];
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      const int idx = base + j * NTHR, m = idx / (hs >> 3), f = (idx % (hs >> 3)) << 3;
-      if (idx < n && m < M) {
-        const float4* xr = reinterpret_cast<const float4*>(pd.x + (size_t)m * D + k0 + f);
-        u[j][0] = __ldcg(xr);
-        u[j][1] = __ldcg(xr + 1);
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < B; ++j) {
-      const int idx = base + j * NTHR, m = idx / (hs >> 3), f = (idx % (hs >> 3)) << 3;
-      if (idx >= n) break;
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (m < M) {
-        const float mu = st[2 * m], rs = st[2 * m + 1];
-        w.x = pack_half2((u[j][0].x - mu) * rs, (u[j][0].y - mu) * rs);
-        w.y = pack_half2((u[j][0].z - mu) * rs, (u[j][0].w - mu) * rs);
-        w.z = pack_half2((u[j][1].x - mu) * rs, (u[j][1].y - mu) * rs);
-        w.w = pack_half2((u[j][1].z - mu) * rs, (u[j][1].w - mu) * rs);
-      }
-      *reinterpret_cast<uint4*>(bbuf + dn_bidx(m, f)) = w;
-    }
-  }
-  fence_async_smem();  // the operand is read by the tensor cores (async proxy)
-}
-
 // The token operand of features [k0, k0 + hs) from a global buffer in the same layout (attention output, FFN
 // hidden): one bulk copy of the contiguous range, issued and awaited by thread 0 (the MMA issuer).
-__device__ __forceinline__ bool dn_stage_copy(const __half* src, int k0, int hs, __half* bbuf, uint64_t* bar,
-                                              uint32_t& ph, uint32_t spin) {
+// With lo (the low parts of the residual operand), a second range of the same features follows in the operand.
+__device__ __forceinline__ bool dn_stage_copy(const __half* src, const __half* lo, int k0, int hs, __half* bbuf,
+                                              uint64_t* bar, uint32_t& ph, uint32_t spin) {
   // the source was written by other CTAs' ordinary stores before the grid barrier: order them before the
   // bulk-copy engine's reads
   asm volatile("fence.proxy.async.global;" ::: "memory");
   const uint32_t bytes = (uint32_t)hs * DN_TOK * 2;
-  mbar_arrive_expect_tx(bar, bytes);
+  mbar_arrive_expect_tx(bar, lo ? 2 * bytes : bytes);
   bulk_g2s_nohint(bbuf, src + (size_t)(k0 >> 6) * (DN_TOK * 64), bytes, bar);
+  if (lo) bulk_g2s_nohint(bbuf + (size_t)hs * DN_TOK, lo + (size_t)(k0 >> 6) * (DN_TOK * 64), bytes, bar);
   const bool ok = mbar_wait(bar, ph, spin);
   ph ^= 1u;
   return ok;
@@ -156,7 +130,8 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
                         __half* bbuf, int* flag, Stage&& stage, Epi&& epi) {
   const int nb0 = cx.so[gi], nb1 = cx.so[gi + 1];
   if (nb0 == nb1) return;
-  const int K = pd.g[gi].K, ns = pd.nsplit[gi], kr = K / ns, nh = dn_halves(kr), hs = kr / nh;
+  const bool hilo = dn_hilo(gi);
+  const int K = pd.g[gi].K, ns = pd.nsplit[gi], kr = K / ns, nh = dn_parts(kr, hilo), hs = kr / nh;
   const int hslots = hs >> 7;  // ring slots (two 64-wide chunks each) per half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int i = nb0; i < nb1; ++i) {
@@ -179,10 +154,11 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
           for (int ch = 0; ch < 2; ++ch)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
-              const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the half
-              tc_mma_f16(tmem, plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128),
-                         sw128_desc(bb + (uint32_t)(kl >> 6) * (DN_TOK * 128) + (uint32_t)(kl & 63) * 2), idesc,
-                         (h | j | ch | kk) != 0);
+              const int kl = (2 * j + ch) * 64 + kk * 16;  // feature offset in the part
+              const uint64_t ad = plain_desc(sa + ch * DN_CHUNK + kk * 4096, 2048, 128);
+              const uint32_t bo = bb + (uint32_t)(kl >> 6) * (DN_TOK * 128) + (uint32_t)(kl & 63) * 2;
+              tc_mma_f16(tmem, ad, sw128_desc(bo), idesc, (h | j | ch | kk) != 0);
+              if (hilo) tc_mma_f16(tmem, ad, sw128_desc(bo + (uint32_t)hs * DN_TOK * 2), idesc, 1u);
             }
           // the slot goes back to the producer when these MMAs have read it (one arrival), the other warps'
           // share now
@@ -252,6 +228,8 @@ __device__ void dn_gemm(const PlanDev& pd, Ring& ring, const Ctx& cx, int gi, ui
   }
 }
 
+__device__ __forceinline__ void dn_store_hilo(const PlanDev& pd, int m, int n, const float4& r);
+
 // Embedding into the residual rows (a CTA per token) and their LayerNorm partial sums (slot 0 holds the row's
 // sums, the other slots zero).
 __device__ __noinline__ void dn_embed(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
@@ -264,11 +242,16 @@ __device__ __noinline__ void dn_embed(const PlanDev& pd, const CallArgs& a, cons
     long long pos = (long long)cx.offs[r] + s;
     pos = pos >= pd.max_pos ? pd.max_pos - 1 : pos;
     float s1 = 0.f, s2 = 0.f;
-    for (int n = threadIdx.x; n < D; n += NTHR) {
-      const float v = __half2float(pd.emb[t * D + n]) * pd.xscale + pd.pe[pos * D + n];
-      pd.x[(size_t)m * D + n] = v;
-      s1 += v;
-      s2 = fmaf(v, v, s2);
+    for (int n = 4 * threadIdx.x; n < D; n += 4 * NTHR) {
+      float4 v;
+      v.x = __half2float(pd.emb[t * D + n]) * pd.xscale + pd.pe[pos * D + n];
+      v.y = __half2float(pd.emb[t * D + n + 1]) * pd.xscale + pd.pe[pos * D + n + 1];
+      v.z = __half2float(pd.emb[t * D + n + 2]) * pd.xscale + pd.pe[pos * D + n + 2];
+      v.w = __half2float(pd.emb[t * D + n + 3]) * pd.xscale + pd.pe[pos * D + n + 3];
+      *reinterpret_cast<float4*>(pd.x + (size_t)m * D + n) = v;
+      dn_store_hilo(pd, m, n, v);
+      s1 += (v.x + v.y) + (v.z + v.w);
+      s2 = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, s2))));
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) {
@@ -437,7 +420,22 @@ __device__ void dn_chunks(const PlanDev& pd, const CallArgs& a, const Ctx& cx, c
 // y [64 tokens][128 rows] (shared memory), a warp per token (its 32 lanes cover the 128 rows); out of line (once
 // per tile), so the stage loops keep their registers.
 
-// residual: x[m][n] += y + b, and the LayerNorm partial sums of the tile's 128 features per token
+// Four residual values of token m (features n .. n + 3) into the GEMM operand as fp16 high and low parts.
+__device__ __forceinline__ void dn_store_hilo(const PlanDev& pd, int m, int n, const float4& r) {
+  const __half2 h0 = __floats2half2_rn(r.x, r.y), h1 = __floats2half2_rn(r.z, r.w);
+  const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+  uint2 hi, lo;
+  hi.x = *reinterpret_cast<const uint32_t*>(&h0);
+  hi.y = *reinterpret_cast<const uint32_t*>(&h1);
+  lo.x = pack_half2(r.x - f0.x, r.y - f0.y);
+  lo.y = pack_half2(r.z - f1.x, r.w - f1.y);
+  const int i = dn_bidx(m, n);
+  *reinterpret_cast<uint2*>(pd.xop + i) = hi;
+  *reinterpret_cast<uint2*>(pd.xop + (size_t)pd.D * DN_TOK + i) = lo;
+}
+
+// residual: x[m][n] += y + b, its fp16 high / low operand parts, and the LayerNorm partial sums of the tile's 128
+// features per token
 __device__ __noinline__ void dn_epi_res(const PlanDev& pd, const float* y, const float* bias, int tile) {
   constexpr int B = 4;
   const int D = pd.D, n_items = pd.M * 32;
@@ -456,6 +454,7 @@ __device__ __noinline__ void dn_epi_res(const PlanDev& pd, const float* y, const
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
       const float4 r = make_float4(xo[j].x + v.x + b.x, xo[j].y + v.y + b.y, xo[j].z + v.z + b.z, xo[j].w + v.w + b.w);
       reinterpret_cast<float4*>(pd.x + (size_t)m * D + tile * DN_TILE)[g] = r;
+      dn_store_hilo(pd, m, tile * DN_TILE + 4 * g, r);
       float s1 = (r.x + r.y) + (r.z + r.w);
       float s2 = fmaf(r.x, r.x, fmaf(r.y, r.y, fmaf(r.z, r.z, r.w * r.w)));
 #pragma unroll
@@ -468,12 +467,20 @@ __device__ __noinline__ void dn_epi_res(const PlanDev& pd, const float* y, const
   }
 }
 
-// fp16 outputs out[m][ld] (q / k / v, cross queries): y + b
-__device__ __noinline__ void dn_epi_half(const PlanDev& pd, const float* y, const float* bias, int tile, __half* out,
-                                         int ld) {
+// The LayerNorm applied to a GEMM of the raw residual: rstd (acc - mean c) for 4 rows of token m (st [64][mean,
+// rstd] in shared memory, c the weights' row sums).
+__device__ __forceinline__ float4 dn_norm(const float4& acc, const float* st, const float* cs, int m, int n) {
+  const float mu = st[2 * m], rs = st[2 * m + 1];
+  const float4 c = __ldg(reinterpret_cast<const float4*>(cs + n));
+  return make_float4(rs * (acc.x - mu * c.x), rs * (acc.y - mu * c.y), rs * (acc.z - mu * c.z), rs * (acc.w - mu * c.w));
+}
+
+// fp16 outputs out[m][ld] (q / k / v, cross queries): LN-corrected y + b
+__device__ __noinline__ void dn_epi_half(const PlanDev& pd, const float* y, const float* bias, const float* st,
+                                         const float* cs, int tile, __half* out, int ld) {
   for (int idx = threadIdx.x; idx < pd.M * 32; idx += NTHR) {
     const int m = idx >> 5, g = idx & 31;
-    const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+    const float4 v = dn_norm(reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g], st, cs, m, tile * DN_TILE + 4 * g);
     const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
     uint2 h;
     h.x = pack_half2(v.x + b.x, v.y + b.y);
@@ -482,13 +489,14 @@ __device__ __noinline__ void dn_epi_half(const PlanDev& pd, const float* y, cons
   }
 }
 
-// ReLU(y + b) into the FFN2 operand layout; padding tokens zero
-__device__ __noinline__ void dn_epi_relu(const PlanDev& pd, const float* y, const float* bias, int tile) {
+// ReLU(LN-corrected y + b) into the FFN2 operand layout; padding tokens zero
+__device__ __noinline__ void dn_epi_relu(const PlanDev& pd, const float* y, const float* bias, const float* st,
+                                         const float* cs, int tile) {
   for (int idx = threadIdx.x; idx < DN_TOK * 32; idx += NTHR) {
     const int m = idx >> 5, g = idx & 31;
     uint2 h = make_uint2(0u, 0u);
     if (m < pd.M) {
-      const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+      const float4 v = dn_norm(reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g], st, cs, m, tile * DN_TILE + 4 * g);
       const float4 b = __ldg(reinterpret_cast<const float4*>(bias + tile * DN_TILE) + g);
       h.x = pack_half2(fmaxf(v.x + b.x, 0.f), fmaxf(v.y + b.y, 0.f));
       h.y = pack_half2(fmaxf(v.z + b.z, 0.f), fmaxf(v.w + b.w, 0.f));
@@ -499,12 +507,12 @@ __device__ __noinline__ void dn_epi_relu(const PlanDev& pd, const float* y, cons
 
 // logits = y + b, and each warp's running best per token (first index on ties; ids first_time .. last_time left
 // out for the rows flagged <notimestamps>)
-__device__ __noinline__ void dn_epi_out(const PlanDev& pd, const CallArgs& a, const float* y, const float* bias, int tile,
-                                        OutState& os) {
+__device__ __noinline__ void dn_epi_out(const PlanDev& pd, const CallArgs& a, const float* y, const float* bias,
+                                        const float* st, const float* cs, int tile, OutState& os) {
   const int M = pd.M, V = pd.V, w = threadIdx.x >> 5;
   for (int idx = threadIdx.x; idx < M * 32; idx += NTHR) {
     const int m = idx >> 5, g = idx & 31;
-    const float4 v = reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g];
+    const float4 v = dn_norm(reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g], st, cs, m, tile * DN_TILE + 4 * g);
     const float vv[4] = {v.x, v.y, v.z, v.w};
     const int n0 = tile * DN_TILE + 4 * g;
     const bool masked = a.notime && a.notime[m / pd.S];
@@ -643,12 +651,11 @@ __global__ void __launch_bounds__(BLOCK, 1)
     const int gi = gemm_of(k);
     const int N = gi >= 0 ? pd.g[gi].N : 0;
     const float* bias = gi >= 0 ? pd.g[gi].b + (k == K_OUT ? 0 : (long long)layer * N) : nullptr;
-    auto ln_stage = [&](int k0, int hs) { dn_ln_half(pd, st, k0, hs, bbuf); };
-    auto copy_stage = [&](const __half* src) {
-      return [&, src](int k0, int hs) {
+    auto copy_stage = [&](const __half* src, const __half* lo) {
+      return [&, src, lo](int k0, int hs) {
         if (threadIdx.x == 0 && !ring.dead) {
           copies = true;
-          if (!dn_stage_copy(src, k0, hs, bbuf, bbar, bph, ring.spin)) {
+          if (!dn_stage_copy(src, lo, k0, hs, bbuf, bbar, bph, ring.spin)) {
             ring.dead = true;
             atomicExch(pd.err, E_ERR_TIMEOUT);
           }
@@ -656,9 +663,11 @@ __global__ void __launch_bounds__(BLOCK, 1)
       };
     };
     auto res_epi = [&](int tile, const float* y) { dn_epi_res(pd, y, bias, tile); };
+    const float* cs = gi >= 0 && pd.gcs[gi] ? pd.gcs[gi] + (k == K_OUT ? 0 : (long long)layer * N) : nullptr;
     auto half_epi = [&](__half* out, int ld) {
-      return [&, out, ld](int tile, const float* y) { dn_epi_half(pd, y, bias, tile, out, ld); };
+      return [&, out, ld](int tile, const float* y) { dn_epi_half(pd, y, bias, st, cs, tile, out, ld); };
     };
+    const auto ln_stage = copy_stage(pd.xop, pd.xop + (size_t)D * DN_TOK);
     if (k == K_QKV || k == K_CQ || k == K_F1 || k == K_OUT) {
       if (!dead && cx.so[gi] < cx.so[gi + 1]) {
         dn_stats(pd, st);
@@ -673,16 +682,16 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_SATT) {
       dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
     } else if (k == K_WO || k == K_WCO) {
-      dn_gemm(pd, ring, cx, gi, tmem, acc, opb, bbuf, tflag, copy_stage(pd.obuf), res_epi);
+      dn_gemm(pd, ring, cx, gi, tmem, acc, opb, bbuf, tflag, copy_stage(pd.obuf, nullptr), res_epi);
     } else if (k == K_CQ) {
       dn_gemm(pd, ring, cx, G_CQ, tmem, acc, opb, bbuf, tflag, ln_stage, half_epi(pd.q2, D));
     } else if (k == K_XATT) {
       dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
       dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage,
-              [&](int tile, const float* y) { dn_epi_relu(pd, y, bias, tile); });
+              [&](int tile, const float* y) { dn_epi_relu(pd, y, bias, st, cs, tile); });
     } else if (k == K_F2) {
-      dn_gemm(pd, ring, cx, G_F2, tmem, acc, opb, bbuf, tflag, copy_stage(pd.hbuf), res_epi);
+      dn_gemm(pd, ring, cx, G_F2, tmem, acc, opb, bbuf, tflag, copy_stage(pd.hbuf, nullptr), res_epi);
     } else if (k == K_OUT) {
       for (int m = lane; m < M; m += 32) {  // this warp's running best per token
         os.wamax[warp * M + m] = -INFINITY;
@@ -690,7 +699,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       }
       __syncwarp();
       dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage,
-              [&](int tile, const float* y) { dn_epi_out(pd, a, y, bias, tile, os); });
+              [&](int tile, const float* y) { dn_epi_out(pd, a, y, bias, st, cs, tile, os); });
       csync();
       for (int m = threadIdx.x; m < M; m += NTHR) {
         float bv = os.amax[m];
@@ -702,8 +711,9 @@ __global__ void __launch_bounds__(BLOCK, 1)
       csync();
       if (a.pred) argmax_finish(pd, a, c, os, flag, work);
     }
-    // the attention output / FFN hidden just written are read by the next stage's bulk copies (async proxy)
-    if (k == K_SATT || k == K_XATT || k == K_F1) asm volatile("fence.proxy.async.global;" ::: "memory");
+    // the operands just written (residual parts, attention output, FFN hidden) are read by a later stage's bulk
+    // copies (async proxy)
+    if (k != K_QKV && k != K_CQ && k != K_OUT) asm volatile("fence.proxy.async.global;" ::: "memory");
     dead = dead || ring.dead;
     if (ts && threadIdx.x == 0) ts[1] = globaltimer();
     if (g < n_stages - 1) grid_sync(pd, (uint32_t)(g + 1) * pd.P, dead, reinterpret_cast<int*>(smem + pd.off_pre) + 1034);
@@ -773,6 +783,23 @@ __global__ void tile_pack_kernel(const uint4* __restrict__ frag, int N, int K, i
     const long long dst = (long long)layer * (out_lstride >> 3) + ((((long long)tile * nchunk + chunk) * 8 + kg) * 16 + rg) * 8 + r;
     reinterpret_cast<uint4*>(out)[dst] = o;
   }
+}
+
+// Row sums of the tile-packed fp16 weights (fp32 sums of the fp16 values): cs[layer][n], n < N.
+__global__ void tile_rowsum_kernel(const __half* __restrict__ t, int N, int K, int layers, long long lstride,
+                                   float* __restrict__ cs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= N * layers) return;
+  const int layer = i / N, row = i - layer * N, tile = row / DN_TILE, rg = (row % DN_TILE) >> 3, r = row & 7;
+  const int nchunk = K >> 6;
+  float s = 0.f;
+  for (int ch = 0; ch < nchunk; ++ch)
+    for (int kg = 0; kg < 8; ++kg) {
+      const __half* p = t + (long long)layer * lstride + ((((long long)tile * nchunk + ch) * 8 + kg) * 16 + rg) * 64 + r * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) s += __half2float(p[e]);
+    }
+  cs[i] = s;
 }
 
 }  // namespace owsm

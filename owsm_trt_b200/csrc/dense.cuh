@@ -391,6 +391,7 @@ __device__ void dn_chunks(const PlanDev& pd, const CallArgs& a, const Ctx& cx, c
     }
     return;
   }
+  if ((k == K_SATT || k == K_XATT) && pd.Qmax == 1) return;  // one-query units read their positions directly
   if (k == K_SATT) {
     for (int u = c; u < pd.R * pd.H; u += pd.P) {
       const int b = u / pd.H, h = u % pd.H, off = cx.offs[b];
@@ -413,6 +414,128 @@ __device__ void dn_chunks(const PlanDev& pd, const CallArgs& a, const Ctx& cx, c
         f((const void*)(a.cv + base + (long long)j0 * DK), (uint32_t)n * DK * 2);
       }
     }
+  }
+}
+
+// One-query attention units (greedy calls: a row's single token, an utterance's single row), a warp per unit with
+// no CTA barrier: the warp walks the unit's positions 32 at a time straight from global memory (lane j scores
+// position p0 + j against the query held in every lane, in the log2 domain; the warp max and the lanes' running
+// sums give the online softmax; the value rows are accumulated two dims per lane, each position's probability
+// broadcast from its lane). Self-attention adds the row's new key / value (also written to the cache slot at the
+// row's offset and to new_kv). Units are spread over all warps of the grid: unit u on warp u mod (P x 7).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __noinline__ void dn_attn_q1(const PlanDev& pd, const CallArgs& a, const Ctx& cx, const int* pre, int layer,
+                                        int c, bool self) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = pd.H, D = pd.D;
+  const int nunits = (self ? pd.R : pd.U) * H;
+  const float qs = 0.125f * kLog2e;  // 1 / sqrt(64), scores in the log2 domain
+  for (int u = c * NWARP + warp; u < nunits; u += pd.P * NWARP) {
+    const int r = u / H, h = u - r * H;
+    int n;
+    const __half *K, *V, *qrow;
+    if (self) {
+      n = cx.offs[r];
+      qrow = pd.qkv + (size_t)r * 3 * D + h * DK;
+      const size_t base = (((size_t)layer * pd.Rs + r) * H + h) * pd.C * DK;
+      K = a.kc + base;
+      V = a.vc + base;
+    } else {
+      n = pre[r + 1] - pre[r];
+      qrow = pd.q2 + (size_t)r * D + h * DK;
+      const size_t base = (((size_t)layer * pd.Us + r) * H + h) * pd.T * DK;
+      K = a.ck + base;
+      V = a.cv + base;
+    }
+    float q[DK];
+#pragma unroll
+    for (int i = 0; i < DK / 8; ++i) {
+      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(qrow) + i);
+      const __half2* h2 = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h2[e]);
+        q[i * 8 + 2 * e] = f.x * qs;
+        q[i * 8 + 2 * e + 1] = f.y * qs;
+      }
+    }
+    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int p0 = 0; p0 < n; p0 += 32) {
+      const int j = p0 + lane, cnt = n - p0 < 32 ? n - p0 : 32;
+      float sc = -INFINITY;
+      if (j < n) {
+        const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * DK);
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < DK / 8; ++i) {
+          const uint4 w = __ldg(kr + i);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h2[e]);
+            acc = fmaf(f.x, q[i * 8 + 2 * e], fmaf(f.y, q[i * 8 + 2 * e + 1], acc));
+          }
+        }
+        sc = acc;
+      }
+      const float mn = fmaxf(m, warp_max(sc));
+      const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
+      const float p = j < n ? exp2f(sc - mn) : 0.f;
+      l = l * alpha + p;
+      o0 *= alpha;
+      o1 *= alpha;
+      m = mn;
+      const uint32_t* vr = reinterpret_cast<const uint32_t*>(V + (size_t)p0 * DK) + lane;
+      uint32_t vv[32];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < cnt ? __ldg(vr + jj * (DK / 2)) : 0u;
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const float pj = __shfl_sync(0xffffffffu, p, jj);
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj]));
+        o0 = fmaf(pj, f.x, o0);
+        o1 = fmaf(pj, f.y, o1);
+      }
+    }
+    if (self) {  // the new key / value: the query sees it (causal: its own position); lane 0 scores it
+      const __half* kn = qrow + D;
+      const __half* vn = qrow + 2 * D;
+      float sc = -INFINITY;
+      if (lane == 0) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < DK / 8; ++i) {
+          const uint4 w = __ldcg(reinterpret_cast<const uint4*>(kn) + i);
+          const __half2* h2 = reinterpret_cast<const __half2*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(h2[e]);
+            acc = fmaf(f.x, q[i * 8 + 2 * e], fmaf(f.y, q[i * 8 + 2 * e + 1], acc));
+          }
+        }
+        sc = acc;
+      }
+      const float mn = fmaxf(m, warp_max(sc));
+      const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
+      const float p = __shfl_sync(0xffffffffu, lane == 0 ? exp2f(sc - mn) : 0.f, 0);
+      const float2 vf = __half22float2(reinterpret_cast<const __half2*>(vn)[lane]);
+      l = l * alpha + (lane == 0 ? p : 0.f);
+      o0 = o0 * alpha + p * vf.x;
+      o1 = o1 * alpha + p * vf.y;
+      const uint32_t kw = reinterpret_cast<const uint32_t*>(kn)[lane], vw = reinterpret_cast<const uint32_t*>(vn)[lane];
+      const size_t cs = ((((size_t)layer * pd.Rs + r) * H + h) * pd.C + n) * DK;
+      reinterpret_cast<uint32_t*>(a.kc + cs)[lane] = kw;
+      reinterpret_cast<uint32_t*>(a.vc + cs)[lane] = vw;
+      reinterpret_cast<uint32_t*>(a.new_kv + ((((size_t)(layer * 2) * pd.Rs + r) * H + h)) * DK)[lane] = kw;
+      reinterpret_cast<uint32_t*>(a.new_kv + ((((size_t)(layer * 2 + 1) * pd.Rs + r) * H + h)) * DK)[lane] = vw;
+    }
+    const float lt = warp_sum(l);
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    *reinterpret_cast<uint32_t*>(pd.obuf + dn_bidx(r, h * DK + 2 * lane)) = pack_half2(o0 * inv, o1 * inv);
   }
 }
 
@@ -680,13 +803,15 @@ __global__ void __launch_bounds__(BLOCK, 1)
     } else if (k == K_QKV) {
       dn_gemm(pd, ring, cx, G_QKV, tmem, acc, opb, bbuf, tflag, ln_stage, half_epi(pd.qkv, 3 * D));
     } else if (k == K_SATT) {
-      dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
+      if (QM == 1) dn_attn_q1(pd, a, cx, pre, layer, c, true);
+      else dn_satt<QM, WIDE>(pd, a, ring, cx, layer, c, work);
     } else if (k == K_WO || k == K_WCO) {
       dn_gemm(pd, ring, cx, gi, tmem, acc, opb, bbuf, tflag, copy_stage(pd.obuf, nullptr), res_epi);
     } else if (k == K_CQ) {
       dn_gemm(pd, ring, cx, G_CQ, tmem, acc, opb, bbuf, tflag, ln_stage, half_epi(pd.q2, D));
     } else if (k == K_XATT) {
-      dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
+      if (QM == 1) dn_attn_q1(pd, a, cx, pre, layer, c, false);
+      else dn_xatt<QM, WIDE>(pd, ring, cx, pre, layer, c, work);
     } else if (k == K_F1) {
       dn_gemm(pd, ring, cx, G_F1, tmem, acc, opb, bbuf, tflag, ln_stage,
               [&](int tile, const float* y) { dn_epi_relu(pd, y, bias, st, cs, tile); });

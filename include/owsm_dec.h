@@ -13,6 +13,7 @@
  *                           RingDecoder.step_fn         src/owsm_trt/megakernel_ring.py:794-830
  *   owsm_dec_step        <- the returned run()          src/owsm_trt/megakernel.py:667-672,
  *                           megakernel_ring.py:852-853 (pred / notime: :794-799)
+ *   owsm_dec_step_verify <- run() + kernels.choose + kernels.accept  src/owsm_trt/runtime.py:1292-1316
  *   owsm_dec_beam_step   <- run() followed by BeamSession._select step 1 and the cache reorder
  *                           src/owsm_trt/runtime.py:1399-1413
  *   owsm_dec_get_error   <- MegaDecoder.check           src/owsm_trt/megakernel.py:616-622
@@ -102,6 +103,21 @@ int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t t
                   int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
                   const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
                   int first_time, int last_time);
+
+/* A verify call of the speculative greedy session (_Bound.body, src/owsm_trt/runtime.py:1292-1316) in one launch:
+ * the decoder call on the rows of `inp` -- int64 [R][inp_stride >= S + 4] = [S tokens | offset | timestamps so far |
+ * last timestamp | first generated position] (runtime.py:1240-1241) -- then, in the vocabulary epilogue, the argmax
+ * after every window position into pred int64 [R, S], under ESPnet's timestamp rules when rules != 0
+ * (TimestampRules.forbidden + _Verify.predict, runtime.py:471-492, :1251-1267; replaces kernels.choose,
+ * src/owsm_trt/kernels.py:26-66, 115-123), with notime (uint8 [R] or NULL) the rows whose primer holds
+ * <notimestamps> and first_time .. last_time the timestamp ids; and, when res != NULL, per row the drafted tokens
+ * accepted and the argmax after them into res int64 [R, 2] (_Verify.accept, runtime.py:1269-1278; replaces
+ * kernels.accept, kernels.py:89-101, 133-136). Other arguments as owsm_dec_step; the plan is a greedy plan of
+ * (R, S). */
+int owsm_dec_step_verify(OwsmDecPlan* p, void* stream, const int64_t* inp, int64_t inp_stride, void* self_k,
+                         void* self_v, const void* cross_k, const void* cross_v, const int32_t* enc_len,
+                         float* logits, void* new_kv, int64_t* pred, const uint8_t* notime, int rules,
+                         int first_time, int last_time, int eos, int64_t* res);
 
 /* owsm_dec_step (S = 1) followed by the beam selection of BeamSession._select step 1 over the plan's
  * batch x beam rows: logp = log_softmax(logits) (fp32), cand = score[r] + logp, inactive rows LOG_ZERO,

@@ -184,3 +184,50 @@ class TimestampRules:
         timed = torch.where((count % 2 == 1)[:, None], open_pair, closed)
         timed = torch.where(first[:, None], ~time, timed)
         return torch.where(notime[:, None], time, timed)
+
+
+def verify_predict(logits: torch.Tensor, inp: torch.Tensor, notime: torch.Tensor | None, rules) -> torch.Tensor:
+    """``_Verify.predict`` (src/owsm_trt/runtime.py:1251-1267): the argmax after each window position of
+    logits [R, W, V] under the timestamp rules (``rules`` None: plain argmax). ``inp`` [R, W + 4] int64 =
+    W tokens, offset, timestamps so far, last timestamp, first generated position; ``notime`` [R] the rows
+    whose primer holds <notimestamps>. Restated position by position: the rule state of position i takes the
+    row's count / last timestamp and the timestamps the window's own tokens 1 .. i add."""
+    if rules is None:
+        return argmax_first(logits)
+    R, W, V = logits.shape
+    flags = torch.zeros(R, dtype=torch.bool) if notime is None else notime.bool()
+    st_notime, st_first, st_count, st_last, st_prev = [], [], [], [], []
+    for r in range(R):
+        row = [int(t) for t in inp[r]]
+        count, last = row[W + 1], max(row[W + 2], -1)
+        for i in range(W):
+            if i > 0 and rules.first_time <= row[i] <= rules.last_time:
+                count += 1
+                last = max(last, row[i])
+            st_notime.append(bool(flags[r]))
+            st_first.append(row[W + 3] == i)
+            st_count.append(count)
+            st_last.append(last)
+            st_prev.append(row[i])
+    bad = rules.forbidden(
+        torch.tensor(st_notime), torch.tensor(st_first), torch.tensor(st_count), torch.tensor(st_last),
+        torch.tensor(st_prev),
+    )
+    return argmax_first(logits.reshape(R * W, V).masked_fill(bad, float("-inf"))).view(R, W)
+
+
+def verify_accept(pred: torch.Tensor, inp: torch.Tensor, eos: int) -> torch.Tensor:
+    """``_Verify.accept`` (src/owsm_trt/runtime.py:1269-1278) per row: positions before the head's end s
+    (inp's first-position column, at least 0) count as accepted; then drafted token i + 1 is accepted while it
+    equals the argmax after position i and is not <eos>. Returns [R, 2] = (drafted tokens accepted, the argmax
+    after the last accepted position)."""
+    R, W = pred.shape
+    out = torch.zeros(R, 2, dtype=torch.long)
+    for r in range(R):
+        s = max(int(inp[r, W + 3]), 0)
+        end = 0
+        while end < W - 1 and (end < s or (int(pred[r, end]) == int(inp[r, end + 1]) and int(inp[r, end + 1]) != eos)):
+            end += 1
+        out[r, 0] = end - s
+        out[r, 1] = pred[r, end]
+    return out

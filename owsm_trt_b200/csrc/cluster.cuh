@@ -937,6 +937,8 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
   const int M = pd.M, V = pd.V;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   __half* bbuf = reinterpret_cast<__half*>(work);
+  if (a.rules)  // the timestamp-rule state of every token (read by the argmax after the next barrier)
+    for (int m = threadIdx.x; m < M; m += NTHR) rule_state(pd, a, m, os.topi + m * KTOP);
   cl_ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx, (int)(blockIdx.x % CS), xb, ph, ring);
   event(cx, 70);
   float best[NT][2];
@@ -955,7 +957,7 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
                          if (m >= M || n >= V) continue;
                          const float y = acc[nt][e] + bia[e >> 1];
                          a.logits[(long long)m * V + n] = y;
-                         const float ya = (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ? -INFINITY : y;
+                         const float ya = argmax_bad(pd, a, os.topi + m * KTOP, m, n) ? -INFINITY : y;
                          merge_best(best[nt][e & 1], besti[nt][e & 1], ya, n);
                        }
                    });

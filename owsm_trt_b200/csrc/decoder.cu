@@ -135,6 +135,12 @@ struct CallArgs {
   int64_t* pred;
   const uint8_t* notime;
   int ft, lt;
+  // verify calls: the input rows, timestamp rules (ESPnet's ScoreFilter) on the argmax, the drafted tokens accepted
+  const int64_t* inp;  // [R] rows of [S tokens | offset | timestamps so far | last timestamp | first position]
+  int64_t inp_stride;
+  int rules;           // 1: the argmax under the timestamp rules (ft, lt, eos; notime = the rows' flags)
+  int eos;
+  int64_t* res;        // [R][2]: drafted tokens accepted, the argmax after them (NULL: not wanted)
   float* score;
   const uint8_t* active;
   int64_t* parent;
@@ -539,6 +545,46 @@ struct OutState {
   float* wtile;  // [NWARP][16][M]
 };
 
+// Timestamp rules of the argmax (runtime.py:457-492 TimestampRules.forbidden, applied per window position as
+// _Verify.predict, runtime.py:1251-1267): the state of token m = (row r, position i) from its input row --
+// timestamps so far (count, last) plus those the window adds at positions 1 .. i, the token at i, whether i is
+// the first generated position, the row's <notimestamps> flag -- packed into st[0] (bits: no-time, first, odd
+// count, previous token a timestamp) and st[1] (last timestamp).
+__device__ __forceinline__ void rule_state(const PlanDev& pd, const CallArgs& a, int m, int* st) {
+  const int W = pd.S, r = m / W, i = m - r * W;
+  const int64_t* row = a.inp + (long long)r * a.inp_stride;
+  long long count = row[W + 1], last = row[W + 2];
+  for (int j = 1; j <= i; ++j) {
+    const long long t = row[j];
+    if (t >= a.ft && t <= a.lt) {
+      ++count;
+      last = t > last ? t : last;
+    }
+  }
+  const long long prev = row[i];
+  const int flags = (a.notime && a.notime[r] ? 1 : 0) | (row[W + 3] == i ? 2 : 0) | ((count & 1) ? 4 : 0) |
+                    ((prev >= a.ft && prev <= a.lt) ? 8 : 0);
+  st[0] = flags;
+  st[1] = (int)(last < -1 ? -1 : (last > 0x7fffffff ? 0x7fffffff : last));
+}
+
+// Whether id v is forbidden for a token in state st (rule_state).
+__device__ __forceinline__ bool rule_bad(const int* st, int v, const CallArgs& a) {
+  const int f = st[0], last = st[1];
+  const bool time = v >= a.ft && v <= a.lt;
+  if (f & 1) return time;
+  if (f & 2) return !time;
+  if (f & 4) return v == a.eos || (time && v <= last);
+  if (f & 8) return (v < last || v > a.lt) && v != a.eos;
+  return true;
+}
+
+// Forbidden for the argmax of token m: the full rules when the call has them, else the <notimestamps> mask.
+__device__ __forceinline__ bool argmax_bad(const PlanDev& pd, const CallArgs& a, const int* st, int m, int n) {
+  if (a.rules) return rule_bad(st, n, a);
+  return a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S];
+}
+
 __device__ __forceinline__ void merge_best(float& bv, int& bi, float v, int i) {
   if (v > bv || (v == bv && i < bi)) {
     bv = v;
@@ -624,7 +670,7 @@ __device__ __forceinline__ void block_epilogue(const PlanDev& pd, const CallArgs
         case K_OUT: {
           a.logits[(long long)m * V + n] = y;
           float ya = y;
-          if (a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S]) ya = -INFINITY;
+          if (argmax_bad(pd, a, os.topi + m * KTOP, m, n)) ya = -INFINITY;
           merge_best(best[nt][e & 1], besti[nt][e & 1], ya, n);
           break;
         }
@@ -698,6 +744,8 @@ __device__ void gemm_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, con
     for (int i = threadIdx.x; i < n16; i += NTHR) dst[i] = __ldcg(src + i);
   }
   event(cx, 10 + kind);
+  if (kind == K_OUT && a.rules && !a.beam_mode)  // the timestamp-rule state of every token (greedy calls)
+    for (int m = threadIdx.x; m < M; m += NTHR) rule_state(pd, a, m, os.topi + m * KTOP);
   if (kind == K_OUT) {  // this warp's running output state
     for (int m = lane; m < M; m += 32) {
       os.wamax[warp * M + m] = -INFINITY;
@@ -1410,7 +1458,24 @@ __device__ void argmax_finish(const PlanDev& pd, const CallArgs& a, int c, OutSt
       const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
       if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
     }
-    if (lane == 0) a.pred[m] = bi == 0x7fffffff ? 0 : bi;
+    if (lane == 0) {
+      a.pred[m] = bi == 0x7fffffff ? 0 : bi;
+      si[m] = bi == 0x7fffffff ? 0 : bi;  // (this CTA's copy of the argmax, for the accepted-draft count)
+    }
+  }
+  if (a.res) {
+    // drafted tokens accepted per row (_Verify.accept, runtime.py:1269-1278): positions up to the head's end s
+    // count as accepted, then each drafted token that equals the argmax before it and is not <eos>
+    csync();
+    const int W = pd.S;
+    for (int r = threadIdx.x; r < pd.R; r += NTHR) {
+      const int64_t* row = a.inp + (long long)r * a.inp_stride;
+      const long long s = row[W + 3] < 0 ? 0 : row[W + 3];
+      int end = 0;
+      while (end < W - 1 && ((si[r * W + end] == row[1 + end] && row[1 + end] != a.eos) || end < s)) ++end;
+      a.res[2 * r] = end - s;
+      a.res[2 * r + 1] = si[r * W + end];
+    }
   }
   if (threadIdx.x == 0) atomicExch(&pd.ctr[2], 0u);
 }
@@ -2602,23 +2667,26 @@ static int check_common(OwsmDecPlan* p, const int64_t* tokens, const int64_t* of
   return OWSM_DEC_OK;
 }
 
-int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride, const int64_t* offset,
-                  int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
-                  const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
-                  int first_time, int last_time) {
-  int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
-  if (rc) return rc;
-  if (!p->subs.empty()) {  // row slices: the same buffers, offset to each slice's first row
+// A greedy call, with (inp != NULL) a verify call's extras: the argmax under the timestamp rules (rules != 0) and
+// the drafted tokens accepted (res != NULL). Row slices: the same buffers, offset to each slice's first row.
+static int step_impl(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride, const int64_t* offset,
+                     int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
+                     const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
+                     int first_time, int last_time, const int64_t* inp, int64_t inp_stride, int rules, int eos,
+                     int64_t* res) {
+  if (!p->subs.empty()) {
     const PlanDev& d0 = p->subs[0]->pd;
     const long long H = d0.H, C = d0.C, T = d0.T, S = d0.S, V = d0.V, G = d0.G;
     for (size_t i = 0; i < p->subs.size(); ++i) {
       const long long r0 = p->sub_r0[i], u0 = r0 / G;
-      rc = owsm_dec_step(p->subs[i], stream, tokens + r0 * tok_stride, tok_stride, offset + r0 * off_stride, off_stride,
-                         reinterpret_cast<__half*>(self_k) + r0 * H * C * DK, reinterpret_cast<__half*>(self_v) + r0 * H * C * DK,
-                         reinterpret_cast<const __half*>(cross_k) + u0 * H * T * DK,
-                         reinterpret_cast<const __half*>(cross_v) + u0 * H * T * DK, enc_len ? enc_len + u0 : nullptr,
-                         logits + r0 * S * V, reinterpret_cast<__half*>(new_kv) + r0 * H * S * DK, pred ? pred + r0 * S : nullptr,
-                         notime ? notime + r0 : nullptr, first_time, last_time);
+      const int rc = step_impl(
+          p->subs[i], stream, tokens + r0 * tok_stride, tok_stride, offset + r0 * off_stride, off_stride,
+          reinterpret_cast<__half*>(self_k) + r0 * H * C * DK, reinterpret_cast<__half*>(self_v) + r0 * H * C * DK,
+          reinterpret_cast<const __half*>(cross_k) + u0 * H * T * DK,
+          reinterpret_cast<const __half*>(cross_v) + u0 * H * T * DK, enc_len ? enc_len + u0 : nullptr,
+          logits + r0 * S * V, reinterpret_cast<__half*>(new_kv) + r0 * H * S * DK, pred ? pred + r0 * S : nullptr,
+          notime ? notime + r0 : nullptr, first_time, last_time, inp ? inp + r0 * inp_stride : nullptr, inp_stride,
+          rules, eos, res ? res + 2 * r0 : nullptr);
       if (rc) return rc;
     }
     return OWSM_DEC_OK;
@@ -2631,8 +2699,34 @@ int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t t
   a.enc_len = enc_len;
   a.logits = logits; a.new_kv = reinterpret_cast<__half*>(new_kv);
   a.pred = pred; a.notime = notime; a.ft = first_time; a.lt = last_time;
+  a.inp = inp; a.inp_stride = inp_stride; a.rules = rules; a.eos = eos; a.res = res;
   a.beam_mode = 0;
   return launch(p, stream, a);
+}
+
+int owsm_dec_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride, const int64_t* offset,
+                  int64_t off_stride, void* self_k, void* self_v, const void* cross_k, const void* cross_v,
+                  const int32_t* enc_len, float* logits, void* new_kv, int64_t* pred, const uint8_t* notime,
+                  int first_time, int last_time) {
+  const int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
+  if (rc) return rc;
+  return step_impl(p, stream, tokens, tok_stride, offset, off_stride, self_k, self_v, cross_k, cross_v, enc_len,
+                   logits, new_kv, pred, notime, first_time, last_time, nullptr, 0, 0, -1, nullptr);
+}
+
+int owsm_dec_step_verify(OwsmDecPlan* p, void* stream, const int64_t* inp, int64_t inp_stride, void* self_k,
+                         void* self_v, const void* cross_k, const void* cross_v, const int32_t* enc_len,
+                         float* logits, void* new_kv, int64_t* pred, const uint8_t* notime, int rules,
+                         int first_time, int last_time, int eos, int64_t* res) {
+  if (!p || !inp || !pred) return fail(OWSM_DEC_ERR_ARG, "owsm_dec_step_verify needs the input rows and pred");
+  if (p->beam) return fail(OWSM_DEC_ERR_ARG, "a verify call needs a greedy plan");
+  const int S = p->subs.empty() ? p->pd.S : p->subs[0]->pd.S;
+  if (inp_stride < S + 4) return fail(OWSM_DEC_ERR_ARG, "input rows are [S tokens, offset, count, last, first]");
+  if (rules && first_time > last_time) return fail(OWSM_DEC_ERR_ARG, "timestamp ids: first > last");
+  const int rc = check_common(p, inp, inp + S, self_k, self_v, cross_k, cross_v, logits, new_kv);
+  if (rc) return rc;
+  return step_impl(p, stream, inp, inp_stride, inp + S, inp_stride, self_k, self_v, cross_k, cross_v, enc_len, logits,
+                   new_kv, pred, notime, first_time, last_time, inp, inp_stride, rules ? 1 : 0, eos, res);
 }
 
 int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride,

@@ -638,7 +638,6 @@ __device__ __noinline__ void dn_epi_out(const PlanDev& pd, const CallArgs& a, co
     const float4 v = dn_norm(reinterpret_cast<const float4*>(y)[m * (DN_TILE / 4) + g], st, cs, m, tile * DN_TILE + 4 * g);
     const float vv[4] = {v.x, v.y, v.z, v.w};
     const int n0 = tile * DN_TILE + 4 * g;
-    const bool masked = a.notime && a.notime[m / pd.S];
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
@@ -647,7 +646,7 @@ __device__ __noinline__ void dn_epi_out(const PlanDev& pd, const CallArgs& a, co
       if (n < V) {
         const float yv = vv[e] + bias[n];
         a.logits[(size_t)m * V + n] = yv;
-        if (!(masked && n >= a.ft && n <= a.lt)) merge_best(bv, bi, yv, n);
+        if (!argmax_bad(pd, a, os.topi + m * KTOP, m, n)) merge_best(bv, bi, yv, n);
       }
     }
 #pragma unroll
@@ -822,6 +821,8 @@ __global__ void __launch_bounds__(BLOCK, 1)
         os.wamax[warp * M + m] = -INFINITY;
         os.waidx[warp * M + m] = 0x7fffffff;
       }
+      if (a.rules)  // the timestamp-rule state of every token (dn_gemm's operand staging syncs before its epilogues)
+        for (int m = threadIdx.x; m < M; m += NTHR) rule_state(pd, a, m, os.topi + m * KTOP);
       __syncwarp();
       dn_gemm(pd, ring, cx, G_OUT, tmem, acc, opb, bbuf, tflag, ln_stage,
               [&](int tile, const float* y) { dn_epi_out(pd, a, y, bias, st, cs, tile, os); });

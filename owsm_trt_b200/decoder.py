@@ -8,8 +8,10 @@ graph-capturable ``run()`` that fills ``logits`` and ``new_kv``, writes the new 
 sessions and ``OWSM.from_pretrained(..., decoder_kernel=...)`` can use it unchanged.
 
 Additions (keyword-only, optional): ``enc_len`` (int32 [U] frames per utterance: a key-padding mask),
-``rows_per_utt`` (rows sharing one utterance's cross K/V, e.g. the beam), and :meth:`B200Decoder.beam_fn`
-(the call + BeamSession._select's top-K + the cache reorder in one launch).
+``rows_per_utt`` (rows sharing one utterance's cross K/V, e.g. the beam), :meth:`B200Decoder.verify_fn` (a
+verify call of the speculative greedy session: the call on its input rows + the argmax under the timestamp rules
++ the drafted tokens accepted, in one launch) and :meth:`B200Decoder.beam_fn` (the call + BeamSession._select's
+top-K + the cache reorder in one launch).
 
 All compute runs in ``libowsmdec.so`` (CUDA, sm_100a), called through ctypes with raw device pointers.
 """
@@ -312,6 +314,67 @@ class B200Decoder:
         run.plan = plan
         run.beam = False
         run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, ntm, enc_len)
+        run.programs = self._plan_info(plan)[0]
+        run.kernel = self
+        return run
+
+    def verify_fn(self, inp, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, *, rules=None, notime=None,
+                  res=None, eos=None, enc_len=None, rows_per_utt: int = 1):  # fmt: skip
+        """A verify call of the speculative greedy session in one launch (_Bound.body, runtime.py:1292-1316):
+        the decoder call on the tokens and offsets of ``inp`` (int64 [R, W + 4] = W tokens, offset, timestamps
+        so far, last timestamp, first generated position), the argmax after every position into ``pred``
+        [R, W] -- under ``rules`` (the session's TimestampRules, or (first_time, last_time, eos)) with
+        ``notime`` [R] bool the rows whose primer holds <notimestamps> (_Verify.predict, runtime.py:1251-1267)
+        -- and, with ``res`` int64 [R, 2], the drafted tokens accepted and the argmax after them
+        (_Verify.accept, runtime.py:1269-1278; ``eos`` defaults to the rules'). ``run.writes_res``: the
+        session's kernels.choose and kernels.accept have nothing left to do."""
+        if inp.dtype != torch.int64 or inp.dim() != 2 or inp.stride(1) != 1:
+            raise TypeError("inp must be int64 [R, W + 4], contiguous along a row")
+        R, W = inp.shape[0], inp.shape[1] - 4
+        if W < 1:
+            raise ValueError("inp rows are [W tokens, offset, #timestamps, last timestamp, first position]")
+        G = int(rows_per_utt)
+        tokens, offset = inp[:, :W], inp[:, W]
+        R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G)
+        if pred.dtype != torch.int64 or pred.shape != (R, S) or not pred.is_contiguous():
+            raise ValueError("pred must be contiguous int64 [R, W]")
+        if res is not None and (res.dtype != torch.int64 or res.shape != (R, 2) or not res.is_contiguous()):
+            raise ValueError("res must be contiguous int64 [R, 2]")
+        ft, lt, on = 0, -1, 0
+        if rules is not None:
+            ft, lt, r_eos = (rules.first_time, rules.last_time, rules.eos) if hasattr(rules, "eos") else rules
+            eos = r_eos if eos is None else eos
+            on = 1
+        if res is not None and eos is None:
+            raise ValueError("res needs the <eos> id: pass eos= or the session's TimestampRules")
+        eos = -1 if eos is None else eos
+        ntm = None
+        if notime is not None:
+            if notime.dtype not in (torch.bool, torch.uint8) or not notime.is_contiguous() or notime.shape != (R,):
+                raise TypeError("notime must be a contiguous bool or uint8 tensor [R]")
+            ntm = notime
+        for t in (pred, res, ntm, enc_len):
+            if t is not None and t.device != self.device:
+                raise ValueError(f"all buffers must be on {self.device}")
+        if enc_len is not None and (enc_len.dtype != torch.int32 or enc_len.numel() != R // G):
+            raise ValueError("enc_len must be int32 [R / rows_per_utt]")
+        plan = self._plan(R, S, Cc, T, G, 0)
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        args = (ptr(inp), inp.stride(0), ptr(self_k), ptr(self_v), ptr(cross_k), ptr(cross_v), ptr(enc_len),
+                ptr(logits), ptr(new_kv), ptr(pred), ptr(ntm), on, int(ft), int(lt), int(eos), ptr(res))  # fmt: skip
+        fn = _lib.lib().owsm_dec_step_verify
+        dev = self.device
+
+        def run() -> None:
+            _lib.check(fn(plan, torch.cuda.current_stream(dev).cuda_stream, *args), "owsm_dec_step_verify")
+
+        run.writes_cache = True
+        run.writes_pred = True
+        run.writes_res = res is not None
+        run.reads_inp = True
+        run.plan = plan
+        run.beam = False
+        run.buffers = (inp, self_k, self_v, cross_k, cross_v, logits, new_kv, pred, ntm, res, enc_len)
         run.programs = self._plan_info(plan)[0]
         run.kernel = self
         return run

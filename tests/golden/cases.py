@@ -76,3 +76,61 @@ def medium_inputs(d: DecoderDims):
     v = torch.randn(d.L, 1, d.H, C, d.dk, generator=g).half()
     enc = torch.randn(1, T, d.D, generator=g)
     return tokens, offset, k, v, enc
+
+
+# Verify calls of the speculative greedy session: timestamp ids 500..900, <eos> 1, <notimestamps> 3 in a
+# vocabulary of 1000; name -> (rows, window, seed).
+VERIFY_RULES = {"notime": 3, "first_time": 500, "last_time": 900, "eos": 1, "vocab": 1000}
+VERIFY_CASES = {"r5w4": (5, 4, 31), "r8w1": (8, 1, 32), "r6w8": (6, 8, 33), "r16w3": (16, 3, 34)}
+
+
+def verify_inputs(R: int, W: int, seed: int):
+    """logits [R, W, V] fp32, inp [R, W + 4] int64 (W tokens, offset, timestamps so far, last timestamp, first
+    generated position), notime [R] bool. The drafted tokens mostly follow the timestamp grammar (a start time
+    first, text, an end time at or after it, then a start time or <eos>), sometimes not; the logits favour the
+    next drafted token at most positions (so drafts get accepted), timestamps and <eos> elsewhere (so every
+    branch of the rules decides some argmax)."""
+    rl = VERIFY_RULES
+    V, ft, lt, eos = rl["vocab"], rl["first_time"], rl["last_time"], rl["eos"]
+    g = torch.Generator().manual_seed(seed)
+
+    def rnd(lo, hi):  # uniform integer in [lo, hi]
+        return int(torch.randint(lo, hi + 1, (1,), generator=g))
+
+    def u():
+        return float(torch.rand(1, generator=g))
+
+    inp = torch.zeros(R, W + 4, dtype=torch.long)
+    notime = torch.rand(R, generator=g) < 0.25
+    for r in range(R):
+        first = rnd(-1, W - 1)
+        count, last = rnd(0, 6), (rnd(ft, lt - 100) if u() < 0.8 else -1)
+        inp[r, W:] = torch.tensor([rnd(0, 40), count, last, first])
+        toks = [rnd(10, ft - 1) if u() < 0.5 else rnd(ft, lt)]
+        for i in range(W - 1):  # token i + 1, chosen in the state after position i
+            is_t = lambda t: ft <= t <= lt  # noqa: E731
+            if i > 0 and is_t(toks[i]):
+                count, last = count + 1, max(last, toks[i])
+            x = u()
+            if x < 0.15:
+                t = rnd(0, V - 1)
+            elif notime[r]:
+                t = rnd(10, ft - 1) if x < 0.9 else eos
+            elif i == first:
+                t = rnd(ft, lt)
+            elif count % 2 == 1:
+                t = rnd(10, ft - 1) if x < 0.6 else rnd(min(max(last + 1, ft), lt), lt)
+            elif is_t(toks[i]):
+                t = eos if x < 0.3 else rnd(min(max(last, ft), lt), lt)
+            else:
+                t = rnd(ft, lt)
+            toks.append(t)
+        inp[r, :W] = torch.tensor(toks)
+    logits = torch.randn(R, W, V, generator=g) * 2.0
+    logits[:, :, ft : lt + 1] += 1.5 * torch.rand(R, W, 1, generator=g)
+    logits[:, :, eos] += 3.0 * torch.rand(R, W, generator=g)
+    tok = inp[:, :W]
+    nxt = torch.cat([tok[:, 1:], tok[:, -1:]], 1)
+    boost = (torch.rand(R, W, generator=g) < 0.8).float() * 12.0
+    logits.scatter_add_(2, nxt[:, :, None], boost[:, :, None])
+    return logits, inp, notime

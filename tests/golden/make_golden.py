@@ -16,6 +16,8 @@ reference's inputs and outputs:
 * ``beam.npz`` -- ``BeamSession._select`` (src/owsm_trt/runtime.py:1399-1446) on given logits / scores /
   active slots / caches: new scores, tokens, and the reordered caches.
 * ``greedy.npz`` -- ``GreedySession.decode`` (runtime.py:804-828) with ``TorchBackend`` (fp32, CPU).
+* ``verify.npz`` -- ``_Verify.predict`` / ``_Verify.accept`` (runtime.py:1251-1278): the argmax of every window
+  position under the timestamp rules and the drafted tokens accepted, on given logits and input rows.
 * ``medium_step.npz`` -- one ``Decoder.step`` of the 18-layer d=1024 model (plain weights), b1: the
   top-32 logits, their ids and checksums.
 """
@@ -157,6 +159,31 @@ def medium_case() -> None:
     print("medium", top.values[:4], top.indices[:4])
 
 
+def verify_case() -> None:
+    """_Verify.predict / _Verify.accept (runtime.py:1251-1278) on given logits and input rows, CPU buffers."""
+    from owsm_trt.runtime import TimestampRules, _Verify
+
+    rl = cases.VERIFY_RULES
+    out = {}
+    for name, (R, W, seed) in cases.VERIFY_CASES.items():
+        logits, inp, notime = cases.verify_inputs(R, W, seed)
+        cfg = dataclasses.replace(TINY, vocab_size=rl["vocab"])
+        rules = TimestampRules(rl["notime"], rl["first_time"], rl["last_time"], rl["eos"], rl["vocab"],
+                               torch.device("cpu"))  # fmt: skip
+        bufs = _Verify(cfg, R, W, {"device": torch.device("cpu"), "dtype": torch.float32}, rules, notime, rl["eos"])
+        bufs.inp.copy_(inp)
+        bufs.tok.copy_(inp[:, :W])
+        bufs.logits.copy_(logits)
+        bufs.pred.copy_(bufs.predict())
+        out[f"{name}_pred"] = bufs.pred.numpy().copy()
+        out[f"{name}_res"] = bufs.accept().numpy().copy()
+        plain = _Verify(cfg, R, W, {"device": torch.device("cpu"), "dtype": torch.float32}, None, notime, rl["eos"])
+        plain.logits.copy_(logits)
+        out[f"{name}_plain"] = plain.predict().numpy().copy()
+        print("verify", name, out[f"{name}_res"].tolist())
+    np.savez_compressed(HERE / "verify.npz", **out)
+
+
 def main() -> None:
     torch.set_num_threads(os.cpu_count() or 1)
     d = TEST_CFG
@@ -166,6 +193,7 @@ def main() -> None:
     beam_case(d)
     greedy_case(d)
     medium_case()
+    verify_case()
 
 
 if __name__ == "__main__":

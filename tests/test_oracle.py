@@ -108,3 +108,51 @@ def test_medium_step_matches_reference():
     torch.testing.assert_close(top.values, torch.from_numpy(gold["top_val"]), rtol=1e-4, atol=1e-4)
     assert abs(float(lg.double().sum()) - float(gold["sum"])) < 1e-2
     assert abs(float((lg.double() ** 2).sum()) - float(gold["sumsq"])) < 1e-3 * float(gold["sumsq"])
+
+
+def _verify_rules():
+    rl = cases.VERIFY_RULES
+    return ref.TimestampRules(rl["notime"], rl["first_time"], rl["last_time"], rl["eos"], rl["vocab"])
+
+
+@pytest.mark.parametrize("name", list(cases.VERIFY_CASES))
+def test_verify_predict_accept_match_reference(name):
+    """_Verify.predict (timestamp rules per window position) and _Verify.accept, bit-exact."""
+    R, W, seed = cases.VERIFY_CASES[name]
+    logits, inp, notime = cases.verify_inputs(R, W, seed)
+    gold = np.load(f"{GOLD}/verify.npz")
+    rules = _verify_rules()
+    pred = ref.verify_predict(logits, inp, notime, rules)
+    assert torch.equal(pred, torch.from_numpy(gold[f"{name}_pred"]))
+    assert torch.equal(ref.verify_accept(pred, inp, rules.eos), torch.from_numpy(gold[f"{name}_res"]))
+    assert torch.equal(ref.verify_predict(logits, inp, notime, None), torch.from_numpy(gold[f"{name}_plain"]))
+
+
+def test_verify_cases_cover_every_rule_branch():
+    """The verify fixtures reach every branch of TimestampRules.forbidden that decides an argmax (no-time row,
+    first position, open pair, after an end time, neither) and accepted counts of 0 and more."""
+    rl = cases.VERIFY_RULES
+    seen, accepted = set(), set()
+    for R, W, seed in cases.VERIFY_CASES.values():
+        logits, inp, notime = cases.verify_inputs(R, W, seed)
+        for r in range(R):
+            count, last = int(inp[r, W + 1]), int(inp[r, W + 2])
+            for i in range(W):
+                t = int(inp[r, i])
+                if i > 0 and rl["first_time"] <= t <= rl["last_time"]:
+                    count += 1
+                prev_time = rl["first_time"] <= t <= rl["last_time"]
+                if notime[r]:
+                    seen.add("notime")
+                elif int(inp[r, W + 3]) == i:
+                    seen.add("first")
+                elif count % 2 == 1:
+                    seen.add("open")
+                elif prev_time:
+                    seen.add("after_end")
+                else:
+                    seen.add("closed")
+        pred = ref.verify_predict(logits, inp, notime, _verify_rules())
+        accepted |= set(ref.verify_accept(pred, inp, rl["eos"])[:, 0].tolist())
+    assert seen == {"notime", "first", "open", "after_end", "closed"}
+    assert 0 in accepted and max(accepted) >= 2

@@ -145,6 +145,9 @@ int owsm_dec_plan_info(const OwsmDecPlan* p, int* programs, int* ring_slots, int
  * stop. The stage count of a call is owsm_dec_plan_stages(p, beam_call). Mirrors the megakernels' TS option
  * (src/owsm_trt/megakernel.py:421-422, :612-614). */
 int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps);
+/* Profiling: the event log of traced calls (128 words per CTA after the stage stamps) starts at stage
+ * `first_stage` instead of the call's start. */
+int owsm_dec_plan_trace_from(OwsmDecPlan* p, int first_stage);
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call);
 
 /* Which kernel later plans of this handle use (no counterpart in owsm-trt, which picks its kernel by GPU):

@@ -48,6 +48,7 @@ SIGNATURES = {
     "owsm_dec_plan_reset": (i32, [vp]),
     "owsm_dec_plan_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i64)]),
     "owsm_dec_plan_trace": (i32, [vp, vp]),
+    "owsm_dec_plan_trace_from": (i32, [vp, i32]),
     "owsm_dec_plan_stages": (i32, [vp, i32]),
     "owsm_dec_set_max_spin": (i32, [vp, u32]),
     "owsm_dec_set_path": (i32, [vp, i32]),

@@ -1076,7 +1076,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   uint8_t* work = smem + pd.off_work;
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int L = pd.L, n_out = 3 * L + 1, n_stages = n_out + 1 + (BEAM ? 3 : 0);
+  const int L = pd.L, n_out = 3 * L + 1, n_stages = n_out + 1 + (BEAM ? 2 : 0);
   int* so = reinterpret_cast<int*>(smem + pd.off_sched);
   int* sb = so + NGEMM + 1;
   int* offs = reinterpret_cast<int*>(smem + pd.off_rows);
@@ -1104,7 +1104,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   cluster_sync_all();
   unsigned long long* evlog = pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
   int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
-  if (threadIdx.x == 0) *nev = 0;
+  if (threadIdx.x == 0) *nev = pd.ev_from > 0 ? NEV : 0;  // (recording starts at stage ev_from)
   __syncthreads();
   const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
 
@@ -1172,6 +1172,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   bool dead = false;
   for (int g = 0; g < n_stages; ++g) {
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (cx.ev && threadIdx.x == 0 && g == pd.ev_from && g > 0) *cx.nev = 0;
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     Ring ring{full, empty, ringdata, pd.nslot, pd.sstride, ring_i, pd.max_spin, pd.err, dead, 0ull, pd.ts != nullptr};
     // A failed call (this CTA's or another's timed-out wait, known to every thread of the CTA from the last grid
@@ -1216,7 +1217,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       }
     } else if (BEAM) {
       if (g == n_out + 1) select_stage(pd, a, c, work);
-      else reorder_stage(pd, a, cx, c, g == n_out + 2);
+      else reorder_stage(pd, a, cx, c);
     }
     ring_i = ring.i;
     dead = ring.dead;

@@ -88,10 +88,9 @@ struct PlanDev {
   int* topi;      // [P][M][KTOP]
   uint32_t* ctr;  // [0] grid barrier, [1] exits, [2] argmax arrivals
   int* err;
-  __half* tmpk;   // reorder staging [L][R][H][C][DK]
-  __half* tmpv;
   int Qmax;           // queries of the largest attention unit
   unsigned long long* ts;  // optional stamps [stage][P][4] (profiling), NULL = off
+  int ev_from;              // profiling: the stage from which CTAs log events (0: from the start)
   int off_pre, off_out, off_ring, off_work;  // shared-memory layout (bytes)
   int off_sched, off_rows;  // this CTA's block lists and the rows' cache offsets (shared memory)
   int inflight;             // bulk copies in flight per CTA (ring slots may hold more, finished)
@@ -246,7 +245,7 @@ __device__ __forceinline__ bool next_piece(const Frames& fr, long long& f, long 
 // ------------------------------------------------------------------------------------------------ stages
 // Stage index g: 0 embed; 1 + 8 l + i for i in (QKV, SATT, WO, CQ, XATT, WCO, F1, F2); 8 L + 1 output;
 // beam calls: 8 L + 2 select, 8 L + 3 reorder A, 8 L + 4 reorder B.
-enum Kind { K_EMBED, K_QKV, K_SATT, K_WO, K_CQ, K_XATT, K_WCO, K_F1, K_F2, K_OUT, K_SELECT, K_REORD_A, K_REORD_B };
+enum Kind { K_EMBED, K_QKV, K_SATT, K_WO, K_CQ, K_XATT, K_WCO, K_F1, K_F2, K_OUT, K_SELECT, K_REORDER };
 
 __device__ __forceinline__ Kind stage_kind(const PlanDev& pd, int g, int& layer) {
   layer = 0;
@@ -1603,27 +1602,50 @@ __host__ __device__ constexpr size_t select_smem(int K, int P) {
   return sizeof(float) * (3 * KTOP + 2 * NTHR + KTOP) + (size_t)K * (P * K + K) * 8;
 }
 
-// Cache reorder (BeamSession._select: buf.index_select(1, parent)), in two stages through a staging copy.
-__device__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, bool to_tmp) {
+// Cache reorder (BeamSession._select: buf.index_select(1, parent), runtime.py:1412-1413) in one stage, in place:
+// row r's slots 0 .. offset + S - 1 become its parent's, for the rows whose parent is another row. A copy at
+// (layer, head, position) reads and writes only that triple of the rows, so each CTA owns a contiguous range of
+// triples and moves them in rounds: every row's K and V of a round's triples into registers (16 uint4 per
+// thread, consecutive threads on consecutive bytes of a row), a CTA barrier, then the stores.
+__device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
   const int N = pd.R, H = pd.H;
-  const long long units = (long long)pd.L * N * H;
-  for (long long uidx = c; uidx < units; uidx += pd.P) {
-    int h = (int)(uidx % H);
-    int r = (int)((uidx / H) % N);
-    int l = (int)(uidx / ((long long)H * N));
-    int par = (int)__ldcg(reinterpret_cast<const long long*>(a.parent) + r);
-    if (par == r || par < 0 || par >= N) continue;
-    int len = cx.offs[par] + pd.S;
-    long long src = ((((long long)l * N + par) * H + h) * pd.C) * DK;
-    long long dst = ((((long long)l * N + r) * H + h) * pd.C) * DK;
-    long long n16 = (long long)len * DK * 2 / 16;
-    for (int kv = 0; kv < 2; ++kv) {
-      __half* cache = kv ? a.vc : a.kc;
-      __half* tmp = kv ? pd.tmpv : pd.tmpk;
-      const uint4* s = reinterpret_cast<const uint4*>(to_tmp ? cache + src : tmp + dst);
-      uint4* d = reinterpret_cast<uint4*>(to_tmp ? tmp + dst : cache + dst);
-#pragma unroll 4
-      for (long long i = threadIdx.x; i < n16; i += NTHR) d[i] = __ldcg(s + i);
+  int maxlen = 0;
+  for (int r = 0; r < N; ++r) maxlen = max(maxlen, cx.offs[r] + pd.S);
+  const long long total = (long long)pd.L * H * maxlen;
+  const long long t0 = total * c / pd.P, t1 = total * (c + 1) / pd.P;
+  constexpr int PER = 16;
+  const int T = max(1, NTHR * PER / (N * 16));  // triples per round
+  const long long* parent = reinterpret_cast<const long long*>(a.parent);
+  for (long long tb = t0; tb < t1; tb += T) {
+    const int nt = (int)min((long long)T, t1 - tb);
+    const int nslot = N * 2 * nt * 8;  // [row][K | V][triple][16-byte piece]
+    uint4 v[PER];
+    long long dst[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      dst[i] = -1;
+      const int s = threadIdx.x + i * NTHR;
+      if (s >= nslot) continue;
+      const int q = s & 7, tri = (s >> 3) % nt, rkv = (s >> 3) / nt, kv = rkv & 1, r = rkv >> 1;
+      const long long par = __ldcg(parent + r);
+      if (par == r || par < 0 || par >= N) continue;
+      const long long t = tb + tri;
+      const int pos = (int)(t % maxlen);
+      const long long lh = t / maxlen;  // layer * H + head
+      const int l = (int)(lh / H), h = (int)(lh % H);
+      if (pos >= cx.offs[par] + pd.S) continue;
+      const __half* cache = kv ? a.vc : a.kc;
+      const long long src = ((((long long)l * N + par) * H + h) * pd.C + pos) * DK;
+      v[i] = __ldcg(reinterpret_cast<const uint4*>(cache + src) + q);
+      dst[i] = (((((long long)l * N + r) * H + h) * pd.C + pos) * DK) / 8 + q;
+      dst[i] = kv ? -2 - dst[i] : dst[i];  // (the V cache: encoded negative)
+    }
+    csync();  // every read of these triples is done before any of them is overwritten
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      if (dst[i] == -1) continue;
+      if (dst[i] >= 0) reinterpret_cast<uint4*>(a.kc)[dst[i]] = v[i];
+      else reinterpret_cast<uint4*>(a.vc)[-2 - dst[i]] = v[i];
     }
   }
 }
@@ -1670,7 +1692,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   uint8_t* work = smem + pd.off_work;
   const int c = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_stages = 8 * pd.L + 2 + (a.beam_mode ? 3 : 0);
+  const int n_stages = 8 * pd.L + 2 + (a.beam_mode ? 2 : 0);
 
   int* so = reinterpret_cast<int*>(smem + pd.off_sched);
   int* sb = so + NGEMM + 1;
@@ -1696,7 +1718,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   unsigned long long* evlog =
       pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
   int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
-  if (threadIdx.x == 0) *nev = 0;
+  if (threadIdx.x == 0) *nev = pd.ev_from > 0 ? NEV : 0;  // (recording starts at stage ev_from)
   const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
   Frames fr;
   fr.total = (long long)pd.H * pre[pd.U];
@@ -1761,6 +1783,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
     int layer;
     const Kind k = stage_kind(pd, g, layer);
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (cx.ev && threadIdx.x == 0 && g == pd.ev_from && g > 0) *cx.nev = 0;
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     switch (k) {
       case K_EMBED: embed_stage(pd, a, cx, c); break;
@@ -1773,8 +1796,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
         else cross_attn_stage<MAXQ>(pd, a, ring, layer, c, work, fr);
         break;
       case K_SELECT: select_stage(pd, a, c, work); break;
-      case K_REORD_A: reorder_stage(pd, a, cx, c, true); break;
-      case K_REORD_B: reorder_stage(pd, a, cx, c, false); break;
+      case K_REORDER: reorder_stage(pd, a, cx, c); break;
       default: gemm_stage<NT>(pd, a, ring, cx, fr, k, layer, c, work, os); break;
     }
     if (k == K_OUT) {
@@ -2307,8 +2329,6 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
     if ((rc = dev_alloc(p->allocs, &pd.lsum, (size_t)P * M, tot))) return bail(rc);
     if ((rc = dev_alloc(p->allocs, &pd.topv, (size_t)P * M * KTOP, tot))) return bail(rc);
     if ((rc = dev_alloc(p->allocs, &pd.topi, (size_t)P * M * KTOP, tot))) return bail(rc);
-    if ((rc = dev_alloc(p->allocs, &pd.tmpk, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
-    if ((rc = dev_alloc(p->allocs, &pd.tmpv, (size_t)d.L * R * d.H * C * DK, tot))) return bail(rc);
   }
   // shared memory: barriers | utterance prefix sums + flag | block lists | row offsets | output-stage state |
   // ring | work area
@@ -2793,9 +2813,16 @@ int owsm_dec_plan_trace(OwsmDecPlan* p, void* stamps) {
   return OWSM_DEC_OK;
 }
 
+int owsm_dec_plan_trace_from(OwsmDecPlan* p, int first_stage) {
+  if (!p || first_stage < 0) return fail(OWSM_DEC_ERR_ARG, "null plan or negative stage");
+  if (!p->subs.empty()) return owsm_dec_plan_trace_from(p->subs[0], first_stage);
+  p->pd.ev_from = first_stage;
+  return OWSM_DEC_OK;
+}
+
 int owsm_dec_plan_stages(const OwsmDecPlan* p, int beam_call) {
   if (!p) return fail(OWSM_DEC_ERR_ARG, "null plan");
-  return (p->pd.cl ? 3 * p->pd.L + 2 : 8 * p->pd.L + 2) + (beam_call ? 3 : 0);
+  return (p->pd.cl ? 3 * p->pd.L + 2 : 8 * p->pd.L + 2) + (beam_call ? 2 : 0);
 }
 
 int owsm_dec_set_path(OwsmDec* h, int path) {

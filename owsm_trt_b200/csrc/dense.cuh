@@ -431,7 +431,12 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 __device__ __noinline__ void dn_attn_q1(const PlanDev& pd, const CallArgs& a, const Ctx& cx, const int* pre, int layer,
                                         int c, bool self) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, H = pd.H, D = pd.D;
+  // lane = 8 grp + e: lane group grp takes keys p0 + 4 i + grp (i = 0 .. 7) of each 32-key chunk, lane e of the
+  // group holds dims 8 e .. 8 e + 7 of q, of those keys and of the group's output; a key's score is summed over
+  // its 8 lanes. Each group keeps its own online-softmax state (max, sum, output), merged over the 4 groups at
+  // the end. Loads are uint4 per lane, 512 contiguous bytes per warp instruction; the next chunk's keys and values
+  // are loaded while the current chunk is scored.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = lane >> 3, e = lane & 7, H = pd.H, D = pd.D;
   const int nunits = (self ? pd.R : pd.U) * H;
   const float qs = 0.125f * kLog2e;  // 1 / sqrt(64), scores in the log2 domain
   for (int u = c * NWARP + warp; u < nunits; u += pd.P * NWARP) {
@@ -451,91 +456,131 @@ __device__ __noinline__ void dn_attn_q1(const PlanDev& pd, const CallArgs& a, co
       K = a.ck + base;
       V = a.cv + base;
     }
-    float q[DK];
-#pragma unroll
-    for (int i = 0; i < DK / 8; ++i) {
-      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(qrow) + i);
+    float q[8];
+    {
+      const uint4 w = __ldcg(reinterpret_cast<const uint4*>(qrow) + e);
       const __half2* h2 = reinterpret_cast<const __half2*>(&w);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h2[e]);
-        q[i * 8 + 2 * e] = f.x * qs;
-        q[i * 8 + 2 * e + 1] = f.y * qs;
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(h2[t]);
+        q[2 * t] = f.x * qs;
+        q[2 * t + 1] = f.y * qs;
       }
     }
-    float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+    const uint4* K4 = reinterpret_cast<const uint4*>(K) + e;  // key j, this lane's dims: K4[j * 8]
+    const uint4* V4 = reinterpret_cast<const uint4*>(V) + e;
+    float m = -INFINITY, l = 0.f, o[8];
+#pragma unroll
+    for (int t = 0; t < 8; ++t) o[t] = 0.f;
+    uint4 kc[8], vc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int j = 4 * i + grp;
+      kc[i] = j < n ? __ldg(K4 + (size_t)j * 8) : make_uint4(0u, 0u, 0u, 0u);
+      vc[i] = j < n ? __ldg(V4 + (size_t)j * 8) : make_uint4(0u, 0u, 0u, 0u);
+    }
     for (int p0 = 0; p0 < n; p0 += 32) {
-      const int j = p0 + lane, cnt = n - p0 < 32 ? n - p0 : 32;
-      float sc = -INFINITY;
-      if (j < n) {
-        const uint4* kr = reinterpret_cast<const uint4*>(K + (size_t)j * DK);
+      uint4 kn[8], vn[8];
+      const int p1 = p0 + 32;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {  // the next chunk, in flight while this one is scored
+        const int j = p1 + 4 * i + grp;
+        kn[i] = j < n ? __ldg(K4 + (size_t)j * 8) : make_uint4(0u, 0u, 0u, 0u);
+        vn[i] = j < n ? __ldg(V4 + (size_t)j * 8) : make_uint4(0u, 0u, 0u, 0u);
+      }
+      float sc[8], cmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&kc[i]);
         float acc = 0.f;
 #pragma unroll
-        for (int i = 0; i < DK / 8; ++i) {
-          const uint4 w = __ldg(kr + i);
-          const __half2* h2 = reinterpret_cast<const __half2*>(&w);
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = __half22float2(h2[t]);
+          acc = fmaf(f.x, q[2 * t], fmaf(f.y, q[2 * t + 1], acc));
+        }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+        sc[i] = p0 + 4 * i + grp < n ? acc : -INFINITY;
+        cmax = fmaxf(cmax, sc[i]);
+      }
+      if (cmax != -INFINITY) {  // (a group with no key left in this chunk keeps its state)
+        const float mn = fmaxf(m, cmax);
+        const float alpha = exp2f(m - mn);  // 0 while m = -inf
+        l *= alpha;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(h2[e]);
-            acc = fmaf(f.x, q[i * 8 + 2 * e], fmaf(f.y, q[i * 8 + 2 * e + 1], acc));
+        for (int t = 0; t < 8; ++t) o[t] *= alpha;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float pi = exp2f(sc[i] - mn);
+          l += pi;
+          const __half2* h2 = reinterpret_cast<const __half2*>(&vc[i]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float2 f = __half22float2(h2[t]);
+            o[2 * t] = fmaf(pi, f.x, o[2 * t]);
+            o[2 * t + 1] = fmaf(pi, f.y, o[2 * t + 1]);
           }
         }
-        sc = acc;
+        m = mn;
       }
-      const float mn = fmaxf(m, warp_max(sc));
-      const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
-      const float p = j < n ? exp2f(sc - mn) : 0.f;
-      l = l * alpha + p;
-      o0 *= alpha;
-      o1 *= alpha;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        kc[i] = kn[i];
+        vc[i] = vn[i];
+      }
+    }
+    if (self) {  // the new key / value (causal: the query sees its own position), in group 0's state
+      const uint4 kw = __ldcg(reinterpret_cast<const uint4*>(qrow + D) + e);
+      const uint4 vw = __ldcg(reinterpret_cast<const uint4*>(qrow + 2 * D) + e);
+      const __half2* k2 = reinterpret_cast<const __half2*>(&kw);
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(k2[t]);
+        acc = fmaf(f.x, q[2 * t], fmaf(f.y, q[2 * t + 1], acc));
+      }
+      acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+      acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+      if (grp == 0) {
+        const float mn = fmaxf(m, acc);
+        const float alpha = exp2f(m - mn), pi = exp2f(acc - mn);
+        const __half2* v2 = reinterpret_cast<const __half2*>(&vw);
+        l = l * alpha + pi;
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = __half22float2(v2[t]);
+          o[2 * t] = fmaf(pi, f.x, o[2 * t] * alpha);
+          o[2 * t + 1] = fmaf(pi, f.y, o[2 * t + 1] * alpha);
+        }
+        m = mn;
+        const size_t cs = ((((size_t)layer * pd.Rs + r) * H + h) * pd.C + n) * DK;
+        reinterpret_cast<uint4*>(a.kc + cs)[e] = kw;
+        reinterpret_cast<uint4*>(a.vc + cs)[e] = vw;
+        reinterpret_cast<uint4*>(a.new_kv + ((((size_t)(layer * 2) * pd.Rs + r) * H + h)) * DK)[e] = kw;
+        reinterpret_cast<uint4*>(a.new_kv + ((((size_t)(layer * 2 + 1) * pd.Rs + r) * H + h)) * DK)[e] = vw;
+      }
+    }
+#pragma unroll
+    for (int off = 8; off <= 16; off <<= 1) {  // merge the groups' states
+      const float mo = __shfl_xor_sync(0xffffffffu, m, off), lo = __shfl_xor_sync(0xffffffffu, l, off);
+      const float mn = fmaxf(m, mo);
+      const float a1 = m == -INFINITY ? 0.f : exp2f(m - mn), a2 = mo == -INFINITY ? 0.f : exp2f(mo - mn);
+      l = l * a1 + lo * a2;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) o[t] = o[t] * a1 + __shfl_xor_sync(0xffffffffu, o[t], off) * a2;
       m = mn;
-      const uint32_t* vr = reinterpret_cast<const uint32_t*>(V + (size_t)p0 * DK) + lane;
-      uint32_t vv[32];
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) vv[jj] = jj < cnt ? __ldg(vr + jj * (DK / 2)) : 0u;
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const float pj = __shfl_sync(0xffffffffu, p, jj);
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vv[jj]));
-        o0 = fmaf(pj, f.x, o0);
-        o1 = fmaf(pj, f.y, o1);
-      }
     }
-    if (self) {  // the new key / value: the query sees it (causal: its own position); lane 0 scores it
-      const __half* kn = qrow + D;
-      const __half* vn = qrow + 2 * D;
-      float sc = -INFINITY;
-      if (lane == 0) {
-        float acc = 0.f;
-#pragma unroll
-        for (int i = 0; i < DK / 8; ++i) {
-          const uint4 w = __ldcg(reinterpret_cast<const uint4*>(kn) + i);
-          const __half2* h2 = reinterpret_cast<const __half2*>(&w);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(h2[e]);
-            acc = fmaf(f.x, q[i * 8 + 2 * e], fmaf(f.y, q[i * 8 + 2 * e + 1], acc));
-          }
-        }
-        sc = acc;
-      }
-      const float mn = fmaxf(m, warp_max(sc));
-      const float alpha = m == -INFINITY ? 0.f : exp2f(m - mn);
-      const float p = __shfl_sync(0xffffffffu, lane == 0 ? exp2f(sc - mn) : 0.f, 0);
-      const float2 vf = __half22float2(reinterpret_cast<const __half2*>(vn)[lane]);
-      l = l * alpha + (lane == 0 ? p : 0.f);
-      o0 = o0 * alpha + p * vf.x;
-      o1 = o1 * alpha + p * vf.y;
-      const uint32_t kw = reinterpret_cast<const uint32_t*>(kn)[lane], vw = reinterpret_cast<const uint32_t*>(vn)[lane];
-      const size_t cs = ((((size_t)layer * pd.Rs + r) * H + h) * pd.C + n) * DK;
-      reinterpret_cast<uint32_t*>(a.kc + cs)[lane] = kw;
-      reinterpret_cast<uint32_t*>(a.vc + cs)[lane] = vw;
-      reinterpret_cast<uint32_t*>(a.new_kv + ((((size_t)(layer * 2) * pd.Rs + r) * H + h)) * DK)[lane] = kw;
-      reinterpret_cast<uint32_t*>(a.new_kv + ((((size_t)(layer * 2 + 1) * pd.Rs + r) * H + h)) * DK)[lane] = vw;
+    if (grp == 0) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      uint4 w;
+      w.x = pack_half2(o[0] * inv, o[1] * inv);
+      w.y = pack_half2(o[2] * inv, o[3] * inv);
+      w.z = pack_half2(o[4] * inv, o[5] * inv);
+      w.w = pack_half2(o[6] * inv, o[7] * inv);
+      *reinterpret_cast<uint4*>(pd.obuf + dn_bidx(r, h * DK + 8 * e)) = w;
     }
-    const float lt = warp_sum(l);
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    *reinterpret_cast<uint32_t*>(pd.obuf + dn_bidx(r, h * DK + 2 * lane)) = pack_half2(o0 * inv, o1 * inv);
   }
 }
 
@@ -709,7 +754,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
   __syncthreads();
   unsigned long long* evlog = pd.ts ? pd.ts + (size_t)n_stages * pd.P * 4 + (size_t)c * NEV : nullptr;
   int* nev = reinterpret_cast<int*>(smem + pd.off_pre) + 1033;
-  if (threadIdx.x == 0) *nev = 0;
+  if (threadIdx.x == 0) *nev = pd.ev_from > 0 ? NEV : 0;  // (recording starts at stage ev_from)
   __syncthreads();
   const Ctx cx{so, sb, offs, evlog, nev, reinterpret_cast<float*>(smem + pd.off_pre) + 1040};
 
@@ -768,6 +813,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
     int layer;
     const Kind k = stage_kind(pd, g, layer);
     unsigned long long* ts = pd.ts ? pd.ts + ((size_t)g * pd.P + c) * 4 : nullptr;
+    if (cx.ev && threadIdx.x == 0 && g == pd.ev_from && g > 0) *cx.nev = 0;
     if (ts && threadIdx.x == 0) ts[0] = globaltimer();
     ring.dead = dead;
     const int gi = gemm_of(k);

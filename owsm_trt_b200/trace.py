@@ -1,7 +1,7 @@
 """Per-stage timing of one decoder call from the kernel's %globaltimer stamps (opt-in, profiling only).
 
 The stages are those of the persistent kernel: embedding; per layer QKV, self-attention, out-projection,
-cross-Q, cross-attention, cross-out, FFN1, FFN2; output layer; for beam calls select and two reorder stages.
+cross-Q, cross-attention, cross-out, FFN1, FFN2; output layer; for beam calls select and the cache reorder.
 ``profile(kernel, run)`` runs ``run`` once with stamps on and returns them; ``summary`` averages them per
 stage kind: the stage's span between consecutive grid-barrier releases, the slowest CTA's work, and the
 mean time CTAs spend in the barrier."""
@@ -21,7 +21,7 @@ def stage_names(L: int, beam: bool, cluster: bool = False) -> list[str]:
         names = ["EMBED"] + [("S1", "S2", "S3")[i % 3] for i in range(3 * L)] + ["OUT"]
     else:
         names = ["EMBED"] + [KINDS[i % 8] for i in range(8 * L)] + ["OUT"]
-    return names + (["SELECT", "REORD_A", "REORD_B"] if beam else [])
+    return names + (["SELECT", "REORDER"] if beam else [])
 
 
 def profile(kernel, run) -> torch.Tensor:
@@ -47,7 +47,7 @@ def profile(kernel, run) -> torch.Tensor:
 def summary(ts: torch.Tensor, L: int, beam: bool = False) -> dict[str, dict[str, float]]:
     """Per stage kind, in microseconds: span (barrier release to barrier release), work (slowest CTA's stage
     time), wait (mean barrier time), ring (the most a CTA waited for its data in the stage), count."""
-    names = stage_names(L, beam, cluster=ts.shape[0] == 3 * L + 2 + (3 if beam else 0))
+    names = stage_names(L, beam, cluster=ts.shape[0] == 3 * L + 2 + (2 if beam else 0))
     t = ts.double()
     start, end, exit_ = t[..., 0], t[..., 1], t[..., 2]
     t0 = start.min()
@@ -83,20 +83,31 @@ def main() -> None:
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--path", type=int, default=0, help="0: cluster kernel where it applies, 1: grid-stage kernel")
     ap.add_argument("--events", type=int, nargs="*", default=[], help="CTAs whose event log to print")
+    ap.add_argument("--beam", type=int, default=0, help="beam width: a beam call of --batch utterances x beam rows")
+    ap.add_argument("--from-stage", type=int, default=0, help="the stage at which the event logs start")
     args = ap.parse_args()
     from .decoder import B200Decoder
     from .synthetic import MEDIUM_1B, decoder_state_dict, make_workload
 
-    d, dev, B = MEDIUM_1B, torch.device("cuda", 0), args.batch
+    d, dev, K = MEDIUM_1B, torch.device("cuda", 0), max(args.beam, 1)
+    B = args.batch * K
     sd = decoder_state_dict(d, 0, False)
     k = B200Decoder.from_state_dict(sd, d.H, dev)
     k.set_path(args.path)
-    ck, cv, enc_len, prefix, kc, vc = make_workload(d, sd, dev, B, 5)
+    ck, cv, enc_len, prefix, kc, vc = make_workload(d, sd, dev, B, 5, rows_per_utt=K)
     tok = prefix[:, -1:].to(dev).contiguous()
     off = torch.full((B,), 100, dtype=torch.long, device=dev)
     logits = torch.zeros(B, 1, d.V, device=dev)
     new_kv = torch.zeros(d.L, 2, B, d.H, 1, d.dk, device=dev, dtype=torch.float16)
-    run = k.step_fn(tok, off, kc, vc, ck, cv, logits, new_kv, pred=tok, enc_len=enc_len.to(dev))
+    if args.beam:  # (every utterance at the full 750 frames, as the benchmark's beam line)
+        el = torch.full((args.batch,), ck.shape[3], dtype=torch.int32, device=dev)
+        score = torch.zeros(B, device=dev)
+        active = torch.ones(B, dtype=torch.uint8, device=dev)
+        parent = torch.zeros(B, dtype=torch.long, device=dev)
+        run = k.beam_fn(tok, off, kc, vc, ck, cv, logits, new_kv, score, active, parent, tok[:, 0].clone(),
+                        beam=K, enc_len=el)  # fmt: skip
+    else:
+        run = k.step_fn(tok, off, kc, vc, ck, cv, logits, new_kv, pred=tok, enc_len=enc_len.to(dev))
     for _ in range(3):
         run()
     torch.cuda.synchronize(dev)
@@ -106,9 +117,10 @@ def main() -> None:
         run()
     e1.record()
     torch.cuda.synchronize(dev)
+    _lib.check(_lib.lib().owsm_dec_plan_trace_from(run.plan, args.from_stage), "owsm_dec_plan_trace_from")
     ts = profile(k, run)
-    s = summary(ts, d.L)
-    print(json.dumps({"kernel": k.plan_kernel(run), "batch": B, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
+    s = summary(ts, d.L, beam=bool(args.beam))
+    print(json.dumps({"kernel": k.plan_kernel(run), "batch": B, "beam": args.beam, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
                       "stages": s}, indent=1))  # fmt: skip
     for c in args.events:
         print(json.dumps({"cta": c, "events": event_log(ts, c)}))

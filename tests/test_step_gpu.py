@@ -252,9 +252,19 @@ def test_greedy_decode_matches_reference_session(kern, sd):
         assert outs[b] == want
 
 
-def test_beam_step_matches_oracle(kern):
+@pytest.mark.parametrize("path", [0, 1])
+def test_beam_step_matches_oracle(kern, path):
     """Fused beam step: parents/tokens bit-exact vs BeamSession._select step 1 (oracle) on the kernel's own
-    logits, scores within 1e-2, the cache rows replaced by their parents' (bit-exact)."""
+    logits, scores within 1e-2, the cache rows replaced by their parents' (bit-exact); on the cluster kernel
+    (path 0) and the grid-stage kernel (path 1)."""
+    kern.set_path(path)
+    try:
+        _beam_step_case(kern, "cluster" if path == 0 else "grid")
+    finally:
+        kern.set_path(0)
+
+
+def _beam_step_case(kern, kernel):
     d = TEST_CFG
     B, K, C, T = 3, 5, 32, 37
     N = B * K
@@ -278,6 +288,7 @@ def test_beam_step_matches_oracle(kern):
     token = torch.zeros(N, dtype=torch.long, device=DEV)
     run = kern.beam_fn(tokens.to(DEV), offset.to(DEV), kcd, vcd, ck.to(DEV), cv.to(DEV), logits, new_kv, sc, act,
                        parent, token, beam=K)  # fmt: skip
+    assert kern.plan_kernel(run) == kernel
     run()
     torch.cuda.synchronize()
     kern.check()

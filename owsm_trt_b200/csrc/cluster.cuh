@@ -999,6 +999,7 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   __half* bbuf = reinterpret_cast<__half*>(work);
   cl_ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx, (int)(blockIdx.x % CS), xb, ph, ring);
+  event(cx, 70);
   for (int m = lane; m < M; m += 32) {
     os.wrmax[warp * M + m] = -INFINITY;
     os.wrsum[warp * M + m] = 0.f;
@@ -1027,6 +1028,7 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
                      beam_merge_block(os, warp, lane, M, rb);
                      __syncwarp();
                    });
+  event(cx, 71);
   csync();
   for (int m = threadIdx.x; m < M; m += NTHR) {
     float mx = os.rmax[m];
@@ -1217,7 +1219,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
       }
     } else if (BEAM) {
       if (g == n_out + 1) select_stage(pd, a, c, work);
-      else reorder_stage(pd, a, cx, c);
+      else reorder_stage(pd, a, cx, c, work);
     }
     ring_i = ring.i;
     dead = ring.dead;

@@ -1604,49 +1604,61 @@ __host__ __device__ constexpr size_t select_smem(int K, int P) {
 
 // Cache reorder (BeamSession._select: buf.index_select(1, parent), runtime.py:1412-1413) in one stage, in place:
 // row r's slots 0 .. offset + S - 1 become its parent's, for the rows whose parent is another row. A copy at
-// (layer, head, position) reads and writes only that triple of the rows, so each CTA owns a contiguous range of
-// triples and moves them in rounds: every row's K and V of a round's triples into registers (16 uint4 per
-// thread, consecutive threads on consecutive bytes of a row), a CTA barrier, then the stores.
-__device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c) {
-  const int N = pd.R, H = pd.H;
+// (layer, head, position, 16-byte piece) reads and writes only that piece of the rows, so the work is cut into
+// items of E consecutive pieces of one (layer, head) -- E the largest power of two with 2 N E <= 512 -- and a
+// warp moves an item alone: every row's K and V pieces into registers (at most 16 per lane), __syncwarp, then
+// the changed rows' stores. No CTA barrier, no staging copy.
+__device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, uint8_t* work) {
+  const int N = pd.R, H = pd.H, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* spar = reinterpret_cast<int*>(work);  // [N] the row's parent, -1 where the row keeps its own slots
+  for (int r = threadIdx.x; r < N; r += NTHR) {
+    const long long p = __ldcg(reinterpret_cast<const long long*>(a.parent) + r);
+    spar[r] = (p == r || p < 0 || p >= N) ? -1 : (int)p;
+  }
   int maxlen = 0;
   for (int r = 0; r < N; ++r) maxlen = max(maxlen, cx.offs[r] + pd.S);
-  const long long total = (long long)pd.L * H * maxlen;
-  const long long t0 = total * c / pd.P, t1 = total * (c + 1) / pd.P;
-  constexpr int PER = 16;
-  const int T = max(1, NTHR * PER / (N * 16));  // triples per round
-  const long long* parent = reinterpret_cast<const long long*>(a.parent);
-  for (long long tb = t0; tb < t1; tb += T) {
-    const int nt = (int)min((long long)T, t1 - tb);
-    const int nslot = N * 2 * nt * 8;  // [row][K | V][triple][16-byte piece]
-    uint4 v[PER];
-    long long dst[PER];
+  csync();
+  int lg = 0;  // E = 1 << lg pieces per item
+  while ((2 * N) << (lg + 1) <= 512) ++lg;
+  const int E = 1 << lg;
+  const int per_lh = (maxlen * (DK / 8) + E - 1) >> lg;  // items per (layer, head)
+  const int nitems = pd.L * H * per_lh;
+  const long long row = (long long)pd.C * DK / 8;  // 16-byte pieces of one (layer, row, head) cache row
+  const int nslot = (2 * N) << lg;                   // [row][K | V][piece]
+  const uint4* k4 = reinterpret_cast<const uint4*>(a.kc);
+  const uint4* v4 = reinterpret_cast<const uint4*>(a.vc);
+  constexpr int J = 16;
+  for (int it = c * NWARP + warp; it < nitems; it += pd.P * NWARP) {
+    const int lh = it / per_lh, e0 = (it - lh * per_lh) << lg, l = lh / H, h = lh - l * H;
+    const long long lbase = (long long)l * N * H + h;  // (layer l, row 0, head h) in rows of `row` pieces
+    long long src[J], dst[J];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      dst[i] = -1;
-      const int s = threadIdx.x + i * NTHR;
+    for (int j = 0; j < J; ++j) {
+      src[j] = -1;
+      const int s = lane + 32 * j;
       if (s >= nslot) continue;
-      const int q = s & 7, tri = (s >> 3) % nt, rkv = (s >> 3) / nt, kv = rkv & 1, r = rkv >> 1;
-      const long long par = __ldcg(parent + r);
-      if (par == r || par < 0 || par >= N) continue;
-      const long long t = tb + tri;
-      const int pos = (int)(t % maxlen);
-      const long long lh = t / maxlen;  // layer * H + head
-      const int l = (int)(lh / H), h = (int)(lh % H);
-      if (pos >= cx.offs[par] + pd.S) continue;
-      const __half* cache = kv ? a.vc : a.kc;
-      const long long src = ((((long long)l * N + par) * H + h) * pd.C + pos) * DK;
-      v[i] = __ldcg(reinterpret_cast<const uint4*>(cache + src) + q);
-      dst[i] = (((((long long)l * N + r) * H + h) * pd.C + pos) * DK) / 8 + q;
-      dst[i] = kv ? -2 - dst[i] : dst[i];  // (the V cache: encoded negative)
+      const int rkv = s >> lg, r = rkv >> 1, piece = e0 + (s & (E - 1));
+      const int par = spar[r];
+      if (par < 0 || (piece >> 3) >= cx.offs[par] + pd.S) continue;
+      src[j] = (lbase + (long long)par * H) * row + piece;
+      dst[j] = (lbase + (long long)r * H) * row + piece;
+      if (rkv & 1) {  // (V: encoded negative)
+        src[j] = -2 - src[j];
+        dst[j] = -2 - dst[j];
+      }
     }
-    csync();  // every read of these triples is done before any of them is overwritten
+    uint4 v[J];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      if (dst[i] == -1) continue;
-      if (dst[i] >= 0) reinterpret_cast<uint4*>(a.kc)[dst[i]] = v[i];
-      else reinterpret_cast<uint4*>(a.vc)[-2 - dst[i]] = v[i];
+    for (int j = 0; j < J; ++j)
+      if (src[j] != -1) v[j] = src[j] >= 0 ? __ldcg(k4 + src[j]) : __ldcg(v4 + (-2 - src[j]));
+    __syncwarp();  // every read of the item's pieces is done before any of them is overwritten
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      if (src[j] == -1) continue;
+      if (dst[j] >= 0) reinterpret_cast<uint4*>(a.kc)[dst[j]] = v[j];
+      else reinterpret_cast<uint4*>(a.vc)[-2 - dst[j]] = v[j];
     }
+    __syncwarp();
   }
 }
 
@@ -1796,7 +1808,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
         else cross_attn_stage<MAXQ>(pd, a, ring, layer, c, work, fr);
         break;
       case K_SELECT: select_stage(pd, a, c, work); break;
-      case K_REORDER: reorder_stage(pd, a, cx, c); break;
+      case K_REORDER: reorder_stage(pd, a, cx, c, work); break;
       default: gemm_stage<NT>(pd, a, ring, cx, fr, k, layer, c, work, os); break;
     }
     if (k == K_OUT) {

@@ -120,7 +120,8 @@ def main() -> None:
     _lib.check(_lib.lib().owsm_dec_plan_trace_from(run.plan, args.from_stage), "owsm_dec_plan_trace_from")
     ts = profile(k, run)
     s = summary(ts, d.L, beam=bool(args.beam))
-    print(json.dumps({"kernel": k.plan_kernel(run), "batch": B, "beam": args.beam, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
+    programs, slots, scratch = k._plan_info(run.plan)
+    print(json.dumps({"kernel": k.plan_kernel(run), "programs": programs, "ring_slots": slots, "batch": B, "beam": args.beam, "us_per_call": round(e0.elapsed_time(e1) / 20 * 1e3, 1),
                       "stages": s}, indent=1))  # fmt: skip
     for c in args.events:
         print(json.dumps({"cta": c, "events": event_log(ts, c)}))

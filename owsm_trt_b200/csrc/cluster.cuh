@@ -94,24 +94,29 @@ __device__ __forceinline__ ClSmem carve_cl(uint8_t* work, int NT, int D) {
 
 // ------------------------------------------------------------------------------------------------ schedule
 // Keys then values of positions p0 .. p1 - 1 (rows of 128 bytes), a chunk of at most apos positions each.
+// keep: the rows are read by several clusters (an utterance's cross K/V in a beam call), so the copies do not
+// mark them evict-first.
 template <class Fn>
-__device__ __forceinline__ void kv_chunks(const PlanDev& pd, const __half* kb, const __half* vb, int p0, int p1, Fn& fn) {
+__device__ __forceinline__ void kv_chunks(const PlanDev& pd, const __half* kb, const __half* vb, int p0, int p1, Fn& fn,
+                                          bool keep = false) {
   for (int j0 = p0; j0 < p1; j0 += pd.apos) {
     const int n = p1 - j0 < pd.apos ? p1 - j0 : pd.apos;
-    fn((const void*)(kb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u);
-    fn((const void*)(vb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u);
+    fn((const void*)(kb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u, keep);
+    fn((const void*)(vb + (long long)j0 * DK), (uint32_t)n * DK * 2, 1, 0u, keep);
   }
 }
 
 // The byte ranges the producer copies for cluster stage `kind` of layer `l`, in the order the consumers use
-// them: fn(src, piece_bytes, pieces, piece_stride_bytes) per ring chunk (the pieces land back to back).
+// them: fn(src, piece_bytes, pieces, piece_stride_bytes, keep) per ring chunk (the pieces land back to back;
+// keep: data other clusters read too, not evict-first).
 template <class Fn>
 __device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, const int* pre, const int* offs,
                           int kind, int l, Fn&& fn) {
   const int D = pd.D, H = pd.H, S = pd.S, r = cl.r;
   auto blocks = [&](int gi, int blk) {  // one whole 16-row block (K = D) with its bias tail
     const GemmW& gw = pd.g[gi];
-    fn((const void*)(gw.w + (long long)l * gw.lstride + (long long)blk * gw.bstride), (uint32_t)gw.bstride * 16, 1, 0u);
+    fn((const void*)(gw.w + (long long)l * gw.lstride + (long long)blk * gw.bstride), (uint32_t)gw.bstride * 16, 1, 0u,
+       false);
   };
   // 16-row blocks rb0 .. rb0 + nb - 1 of GEMM gi, k-blocks kb0 .. kb0 + nkb - 1 of each, packed per chunk
   auto kslices = [&](int gi, int rb0, int nb, int kb0, int nkb) {
@@ -121,7 +126,7 @@ __device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, co
     for (int b = 0; b < nb; b += per) {
       const int n = nb - b < per ? nb - b : per;
       fn((const void*)(gw.w + (long long)l * gw.lstride + (long long)(rb0 + b) * gw.bstride + (long long)kb0 * 32), piece,
-         n, (uint32_t)gw.bstride * 16);
+         n, (uint32_t)gw.bstride * 16, false);
     }
   };
   if (kind == 1 || kind == 2) {
@@ -144,8 +149,8 @@ __device__ void cl_chunks(const PlanDev& pd, const CallArgs& a, const Cl& cl, co
       const int ng = cl.u1 - cl.u0, parts = unit_parts(ng);
       for (int k = r; k < ng * parts; k += CS) {
         const int u = cl.u0 + k / parts, p = k % parts, len = pre[u + 1] - pre[u];
-        const long long base = (((long long)l * pd.Us + u) * H + h) * (long long)pd.T * DK;
-        kv_chunks(pd, a.ck + base, a.cv + base, len * p / parts, len * (p + 1) / parts, fn);
+        const long long base = (((long long)l * pd.Us + kv_utt(pd, u)) * H + h) * (long long)pd.T * DK;
+        kv_chunks(pd, a.ck + base, a.cv + base, len * p / parts, len * (p + 1) / parts, fn, pd.kvg > 1);
       }
       kslices(G_WCO, r * (D / 64), D / 64, 4 * h, 4);
     }
@@ -995,39 +1000,103 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
 template <int NT>
 __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ring, const Ctx& cx, uint8_t* work,
                                   OutState& os, uint64_t* xb, uint32_t& ph) {
-  const int M = pd.M, V = pd.V;
+  const int M = pd.M, V = pd.V, K = pd.beam;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   __half* bbuf = reinterpret_cast<__half*>(work);
   cl_ln_rows(pd, pd.xfix, 0, M, NT, bbuf, cx, (int)(blockIdx.x % CS), xb, ph, ring);
   event(cx, 70);
-  for (int m = lane; m < M; m += 32) {
-    os.wrmax[warp * M + m] = -INFINITY;
-    os.wrsum[warp * M + m] = 0.f;
-    for (int j = 0; j < KTOP; ++j) {
-      os.wtopv[((size_t)warp * M + m) * KTOP + j] = -INFINITY;
-      os.wtopi[((size_t)warp * M + m) * KTOP + j] = 0x7fffffff;
-    }
-  }
-  csync();
+  // Per lane and token (nt, s2) -- token nt * 8 + 2 t + s2, whose values in a block are vocabulary rows g and
+  // g + 8, held by the 8 lanes g = 0 .. 7 of that t: the running max and sum of exp of the lane's values
+  // (log-softmax partials), and entry g of the warp's sorted list of the token's KTOP best (value, id) so far
+  // (one entry per lane; empty entries carry distinct ids, so every element of a merge has its own rank).
+  float rmx[NT][2], rsm[NT][2], lv[NT][2];
+  int li[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2)
+      rmx[nt][s2] = lv[nt][s2] = -INFINITY, rsm[nt][s2] = 0.f, li[nt][s2] = 0x7fffffff - g;
   const int b0 = cx.so[G_OUT];
   block_chunks<NT>(ring, cx.so[G_OUT + 1] - b0, pd.D / 16, smem_u32(bbuf),
                    [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
                      const int rb = cx.sb[b0 + j];
-                     float* tile = os.wtile + (size_t)warp * 16 * M;
 #pragma unroll
                      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                       for (int e = 0; e < 4; ++e) {
-                         const int row = g + (e >> 1) * 8, m = nt * 8 + 2 * t + (e & 1), n = rb * 16 + row;
-                         if (m >= M) continue;
-                         const float y = acc[nt][e] + bia[e >> 1];
-                         if (n < V) a.logits[(long long)m * V + n] = y;
-                         tile[row * M + m] = (n < V) ? y : -INFINITY;
+                       for (int s2 = 0; s2 < 2; ++s2) {
+                         const int m = nt * 8 + 2 * t + s2, n0 = rb * 16 + g, n1 = n0 + 8;
+                         float y0 = acc[nt][s2] + bia[0], y1 = acc[nt][2 + s2] + bia[1];
+                         if (m < M) {
+                           if (n0 < V) a.logits[(long long)m * V + n0] = y0;
+                           if (n1 < V) a.logits[(long long)m * V + n1] = y1;
+                         }
+                         if (m >= M || n0 >= V) y0 = -INFINITY;
+                         if (m >= M || n1 >= V) y1 = -INFINITY;
+                         const float mx = fmaxf(rmx[nt][s2], fmaxf(y0, y1));
+                         if (mx > -INFINITY) {
+                           float sm = rmx[nt][s2] > -INFINITY ? rsm[nt][s2] * expf(rmx[nt][s2] - mx) : 0.f;
+                           if (y0 > -INFINITY) sm += expf(y0 - mx);
+                           if (y1 > -INFINITY) sm += expf(y1 - mx);
+                           rmx[nt][s2] = mx;
+                           rsm[nt][s2] = sm;
+                         }
+                         // the token's K-th best so far (lane g = K - 1 of this t) bars the block's values
+                         const float bv = __shfl_sync(0xffffffffu, lv[nt][s2], (K - 1) * 4 + t);
+                         const int bi = __shfl_sync(0xffffffffu, li[nt][s2], (K - 1) * 4 + t);
+                         const bool cand = m < M && (beats(y0, n0, bv, bi) || beats(y1, n1, bv, bi));
+                         if (!__any_sync(0xffffffffu, cand)) continue;
+                         // merge: the rank of each of the lane's 3 elements among the token's 24 (8 lanes x
+                         // {list entry, y0, y1}); the element of rank q < KTOP becomes entry q (lane q)
+                         const float ev[3] = {lv[nt][s2], y0, y1};
+                         const int ei[3] = {li[nt][s2], n0, n1};
+                         int rk[3] = {0, 0, 0};
+#pragma unroll
+                         for (int o = 0; o < 8; ++o) {
+                           const int src = o * 4 + t;
+#pragma unroll
+                           for (int q = 0; q < 3; ++q) {
+                             const float ov = __shfl_sync(0xffffffffu, ev[q], src);
+                             const int oi = __shfl_sync(0xffffffffu, ei[q], src);
+#pragma unroll
+                             for (int e = 0; e < 3; ++e) rk[e] += beats(ov, oi, ev[e], ei[e]) ? 1 : 0;
+                           }
+                         }
+                         float* tv = os.wtopv + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
+                         int* ti = os.wtopi + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
+#pragma unroll
+                         for (int e = 0; e < 3; ++e)
+                           if (m < M && rk[e] < KTOP) tv[rk[e]] = ev[e], ti[rk[e]] = ei[e];
+                         __syncwarp();
+                         if (m < M) lv[nt][s2] = tv[g], li[nt][s2] = ti[g];
+                         __syncwarp();
                        }
-                     __syncwarp();
-                     beam_merge_block(os, warp, lane, M, rb);
-                     __syncwarp();
                    });
+  // the 8 lanes of a token (g = 0 .. 7) combine their partials; the warp's partial per token -> os.wrmax / wrsum;
+  // its list -> os.wtopv / wtopi (entry g from lane g)
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int s2 = 0; s2 < 2; ++s2) {
+      float mx = rmx[nt][s2], sm = rsm[nt][s2];
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        const float om = __shfl_xor_sync(0xffffffffu, mx, o), osm = __shfl_xor_sync(0xffffffffu, sm, o);
+        const float nm = fmaxf(mx, om);
+        if (nm > -INFINITY) {
+          sm = (mx > -INFINITY ? sm * expf(mx - nm) : 0.f) + (om > -INFINITY ? osm * expf(om - nm) : 0.f);
+          mx = nm;
+        }
+      }
+      const int m = nt * 8 + 2 * t + s2;
+      if (m < M) {
+        if (g == 0) {
+          os.wrmax[warp * M + m] = mx;
+          os.wrsum[warp * M + m] = sm;
+        }
+        os.wtopv[((size_t)warp * M + m) * KTOP + g] = lv[nt][s2];
+        os.wtopi[((size_t)warp * M + m) * KTOP + g] = li[nt][s2];
+      }
+    }
   event(cx, 71);
   csync();
   for (int m = threadIdx.x; m < M; m += NTHR) {
@@ -1061,7 +1130,7 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
 }
 
 // The cluster kernel. Stages: 0 embedding; 1 + 3 l + (0, 1, 2) = S1, S2, S3 of layer l; 3 L + 1 output;
-// beam calls (BEAM): 3 L + 2 select, 3 L + 3 and 3 L + 4 the two halves of the cache reorder. WIDE:
+// beam calls (BEAM): 3 L + 2 select, 3 L + 3 the cache reorder. WIDE:
 // one-query attention units of at least 256 positions take steps of 32 positions.
 // Only the ring position, the exchange parities and the error flag live in registers across stages; the
 // rest of the per-CTA state is rebuilt inside each stage from shared memory and the launch parameters, which
@@ -1143,14 +1212,15 @@ __global__ void __launch_bounds__(BLOCK, 1)
                    reinterpret_cast<const uint8_t*>(src) + (size_t)q * stride, piece, &full[s], pol);
         ++i;
       };
-      const uint64_t first = policy_evict_first();
+      const uint64_t first = policy_evict_first(), normal = policy_evict_normal();
       for (int g = 1; g <= n_out && !dead; ++g) {
         if (g == n_out) {  // output stage: the grid kernel's block schedule
           for_chunks(pd, a, fr, cx, 8 * L + 1, c, [&](const void* src, uint32_t bytes) { put(src, bytes, 1, 0u, first); });
         } else {
           const int kind = (g - 1) % 3 + 1, l = (g - 1) / 3;
-          cl_chunks(pd, a, cl, pre, offs, kind, l,
-                    [&](const void* src, uint32_t piece, int pieces, uint32_t stride) { put(src, piece, pieces, stride, first); });
+          cl_chunks(pd, a, cl, pre, offs, kind, l, [&](const void* src, uint32_t piece, int pieces, uint32_t stride, bool keep) {
+            put(src, piece, pieces, stride, keep ? normal : first);
+          });
         }
       }
       const uint32_t from = i > (uint32_t)pd.nslot ? i - pd.nslot : 0;
@@ -1218,7 +1288,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
         if (a.pred) argmax_finish(pd, a, c, os, flag, work);
       }
     } else if (BEAM) {
-      if (g == n_out + 1) select_stage(pd, a, c, work);
+      if (g == n_out + 1) select_stage(pd, a, cx, c, work);
       else reorder_stage(pd, a, cx, c, work);
     }
     ring_i = ring.i;

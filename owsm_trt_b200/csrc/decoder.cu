@@ -102,6 +102,8 @@ struct PlanDev {
   int wide;                 // cluster kernel: one-query attention units of >= 256 positions take steps of 32
   int Rs, Us;               // cluster kernel: rows / utterances of the caller's buffers (layer strides of the
                             // caches, new_kv and cross K/V), more than R / U when the call is a row slice
+  int kvg;                  // cluster kernel, beam calls: attention groups (one row each) per copy of cross K/V
+                            // and per enc_len entry (the utterance's hypotheses); 0 or 1 = one each
   long long* xf[3];         // cluster kernel: rotating fixed-point residual buffers [M][D]
   // dense kernel (calls of 33 to 64 tokens; tcgen05 GEMMs)
   int dense;
@@ -187,8 +189,11 @@ __device__ __forceinline__ void event(const Ctx& cx, int tag) {
   }
 }
 
+// The copy of cross K/V (and its enc_len entry) that attention group u reads.
+__device__ __forceinline__ int kv_utt(const PlanDev& pd, int u) { return pd.kvg > 1 ? u / pd.kvg : u; }
+
 __device__ __forceinline__ int utt_len(const PlanDev& pd, const CallArgs& a, int u) {
-  int t = a.enc_len ? a.enc_len[u] : pd.T;
+  int t = a.enc_len ? a.enc_len[kv_utt(pd, u)] : pd.T;
   return t < 1 ? 1 : (t > pd.T ? pd.T : t);
 }
 
@@ -583,6 +588,9 @@ __device__ __forceinline__ bool argmax_bad(const PlanDev& pd, const CallArgs& a,
   if (a.rules) return rule_bad(st, n, a);
   return a.notime && n >= a.ft && n <= a.lt && a.notime[m / pd.S];
 }
+
+// Candidate order of the beam select: value descending, then flat index ascending.
+__device__ __forceinline__ bool beats(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
 __device__ __forceinline__ void merge_best(float& bv, int& bi, float v, int i) {
   if (v > bv || (v == bv && i < bi)) {
@@ -1492,35 +1500,96 @@ __device__ void beam_partials(const PlanDev& pd, int c, OutState& os) {
 
 constexpr float LOG_ZERO = -1.0e10f;
 
-// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials (a warp per
-// row), candidates score + (logit - lse) from every CTA's per-row top-K staged in shared memory
-// (LOG_ZERO for inactive rows), top-`beam` by (value desc, flat index asc).
-__device__ void select_stage(const PlanDev& pd, const CallArgs& a, int c, uint8_t* work) {
+// A sorted list of the KTOP best candidates in registers (a beam of K <= KTOP uses its first K): insert (v, i)
+// where it belongs. (Every index is static: a register array indexed by a run-time value would live in local
+// memory.)
+__device__ __forceinline__ void list_insert(float (&lv)[KTOP], int (&li)[KTOP], float v, int i) {
+  if (!beats(v, i, lv[KTOP - 1], li[KTOP - 1])) return;
+#pragma unroll
+  for (int j = KTOP - 1; j > 0; --j) {  // shift down the entries v beats, from the end of the list
+    if (beats(v, i, lv[j - 1], li[j - 1])) {
+      lv[j] = lv[j - 1];
+      li[j] = li[j - 1];
+    } else if (beats(v, i, lv[j], li[j])) {
+      lv[j] = v;
+      li[j] = i;
+    }
+  }
+  if (beats(v, i, lv[0], li[0])) {
+    lv[0] = v;
+    li[0] = i;
+  }
+}
+
+// The warp's K best of its lanes' sorted lists (K rounds: the warp's best head, popped from its lane's list),
+// written by lane 0 to out_v / out_i [K].
+__device__ __forceinline__ void warp_merge_lists(float (&lv)[KTOP], int (&li)[KTOP], int K, float* out_v, int* out_i) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int sel = 0; sel < K; ++sel) {
+    float bv = lv[0];
+    int bi = li[0];
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (beats(ov, oi, bv, bi)) bv = ov, bi = oi;
+    }
+    if (lane == 0) out_v[sel] = bv, out_i[sel] = bi;
+    if (li[0] == bi && lv[0] == bv && bi != 0x7fffffff) {  // (flat indices are unique: one lane pops)
+#pragma unroll
+      for (int j = 0; j < KTOP - 1; ++j) lv[j] = lv[j + 1], li[j] = li[j + 1];
+      lv[KTOP - 1] = -INFINITY;
+      li[KTOP - 1] = 0x7fffffff;
+    }
+  }
+}
+
+// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials; candidates
+// score + (logit - lse) from every CTA's per-row top-K (LOG_ZERO for inactive rows), each thread keeping the K
+// best of its candidates in registers; the warps' lists merged by shuffles, then the warps' results by warp 0:
+// top-`beam` by (value desc, flat index asc). The stage runs once per call, so its code is kept short (loops
+// rolled up: a call finds it cold in the instruction cache); loads go first into shared memory.
+// (Out of line: its register lists would otherwise compete with the rest of the kernel's allocation.)
+__device__ __noinline__ void select_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, uint8_t* work) {
   const int K = pd.beam, V = pd.V, P = pd.P;
   const int B = pd.R / K;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* lmx = reinterpret_cast<float*>(work);  // [KTOP] row max of the logits
   float* lse = lmx + KTOP;                      // [KTOP] log of the row's sum of exp(logit - max)
-  float* pickv = lse + KTOP;                    // [KTOP]
-  float* rv = pickv + KTOP;                     // [NTHR]
-  int* ri = reinterpret_cast<int*>(rv + NTHR);  // [NTHR]
-  int* picked = ri + NTHR;                      // [KTOP]
-  float* cv = reinterpret_cast<float*>(picked + KTOP);  // [K][P*K + K] candidate values
-  const int per_row = P * K + K;
-  const int ncand = K * per_row;
-  int* ci = reinterpret_cast<int*>(cv + ncand);  // flat indices
+  float* rsc = lse + KTOP;                      // [KTOP] the rows' scores (before this step)
+  int* ract = reinterpret_cast<int*>(rsc + KTOP);           // [KTOP] the rows' active flags
+  float* wv = reinterpret_cast<float*>(ract + KTOP);        // [NWARP][KTOP] the warps' best
+  int* wi = reinterpret_cast<int*>(wv + NWARP * KTOP);
+  float* pm = reinterpret_cast<float*>(wi + NWARP * KTOP);  // [K][P] the CTAs' row max, then sum
+  float* ps = pm + K * P;
+  float* cvv = ps + K * P;                                  // [K][P * K] the CTAs' top-K values, then ids
+  int* cvi = reinterpret_cast<int*>(cvv + K * P * K);
+  const int nc = P * K;  // candidates of an active row
   for (int u = c; u < B; u += P) {
+    if (threadIdx.x < K) {
+      rsc[threadIdx.x] = a.score[u * K + threadIdx.x];
+      ract[threadIdx.x] = a.active[u * K + threadIdx.x] != 0;
+    }
+    for (int i = threadIdx.x; i < K * P; i += NTHR) {
+      const int k = i / P, q = i - k * P, r = u * K + k;
+      pm[i] = __ldcg(pd.lmax + (long long)q * pd.M + r);
+      ps[i] = __ldcg(pd.lsum + (long long)q * pd.M + r);
+    }
+    for (int i = threadIdx.x; i < K * nc; i += NTHR) {
+      const int k = i / nc, j = i - k * nc, q = j / K, e = j - q * K, r = u * K + k;
+      cvv[i] = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
+      cvi[i] = __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
+    }
+    csync();
     for (int k = warp; k < K; k += NWARP) {
-      const int r = u * K + k;
       float mx = -INFINITY;
-      for (int q = lane; q < P; q += 32) mx = fmaxf(mx, __ldcg(pd.lmax + (long long)q * pd.M + r));
+      for (int q = lane; q < P; q += 32) mx = fmaxf(mx, pm[k * P + q]);
 #pragma unroll
       for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
       float sm = 0.f;
-      for (int q = lane; q < P; q += 32) {
-        const float mq = __ldcg(pd.lmax + (long long)q * pd.M + r);
-        if (mq > -INFINITY) sm += __ldcg(pd.lsum + (long long)q * pd.M + r) * expf(mq - mx);
-      }
+      for (int q = lane; q < P; q += 32)
+        if (pm[k * P + q] > -INFINITY) sm += ps[k * P + q] * expf(pm[k * P + q] - mx);
 #pragma unroll
       for (int o = 16; o; o >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, o);
       if (lane == 0) {
@@ -1529,137 +1598,152 @@ __device__ void select_stage(const PlanDev& pd, const CallArgs& a, int c, uint8_
       }
     }
     csync();
-#pragma unroll 4
-    for (int idx = threadIdx.x; idx < ncand; idx += NTHR) {
-      const int k = idx / per_row, j = idx % per_row;
-      const int r = u * K + k;
-      const bool act = a.active[r] != 0;
-      float v = -INFINITY;
-      int fi = 0x7fffffff;
-      if (j < P * K) {
-        if (act) {
-          const int q = j / K, e = j % K;
-          const float lv = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
-          if (lv > -INFINITY) {
-            v = a.score[r] + ((lv - lmx[k]) - lse[k]);  // log_softmax = (x - max) - log(sum)
-            fi = k * V + __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
-          }
-        }
-      } else if (!act) {
-        v = LOG_ZERO;
-        fi = k * V + (j - P * K);
-      }
-      cv[idx] = v;
-      ci[idx] = fi;
-    }
-    csync();
-    for (int sel = 0; sel < K; ++sel) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff, bp = -1;
-      for (int idx = threadIdx.x; idx < ncand; idx += NTHR) {
-        const float v = cv[idx];
-        const int fi = ci[idx];
-        if (fi != 0x7fffffff && (v > bv || (v == bv && fi < bi))) { bv = v; bi = fi; bp = idx; }
-      }
+    event(cx, 74);
+    float lv[KTOP];
+    int li[KTOP];
 #pragma unroll
-      for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        const int op = __shfl_xor_sync(0xffffffffu, bp, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; bp = op; }
+    for (int j = 0; j < KTOP; ++j) lv[j] = -INFINITY, li[j] = 0x7fffffff;
+#pragma unroll 1
+    for (int i = threadIdx.x; i < K * (nc + K); i += NTHR) {
+      const int k = i / (nc + K), j = i - k * (nc + K);
+      if (ract[k]) {
+        if (j < nc && cvv[k * nc + j] > -INFINITY)  // log_softmax = (x - max) - log(sum)
+          list_insert(lv, li, rsc[k] + ((cvv[k * nc + j] - lmx[k]) - lse[k]), k * V + cvi[k * nc + j]);
+      } else if (j >= nc) {  // an inactive row: LOG_ZERO candidates (its first K ids stand for all of them)
+        list_insert(lv, li, LOG_ZERO, k * V + (j - nc));
       }
-      if (lane == 0) {
-        rv[warp] = bv;
-        ri[warp] = bi;
-        ri[NWARP + warp] = bp;
-      }
-      csync();
-      if (threadIdx.x == 0) {
-        float v0 = rv[0];
-        int i0 = ri[0], p0 = ri[NWARP];
-        for (int w = 1; w < NWARP; ++w)
-          if (rv[w] > v0 || (rv[w] == v0 && ri[w] < i0)) { v0 = rv[w]; i0 = ri[w]; p0 = ri[NWARP + w]; }
-        picked[sel] = i0;
-        pickv[sel] = v0;
-        if (p0 >= 0) ci[p0] = 0x7fffffff;  // taken
-      }
-      csync();
     }
-    // the scores of the (old) rows are read above: write the new ones only after all rounds
-    if (threadIdx.x < K) {
-      const int sel = threadIdx.x;
-      const int fi = picked[sel] == 0x7fffffff ? 0 : picked[sel];
-      a.score[u * K + sel] = pickv[sel];
-      a.parent[u * K + sel] = (long long)u * K + fi / V;
-      a.token[u * K + sel] = fi % V;
+    event(cx, 75);
+    warp_merge_lists(lv, li, K, wv + warp * KTOP, wi + warp * KTOP);
+    event(cx, 76);
+    csync();
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < KTOP; ++j) {
+        lv[j] = (lane < NWARP && j < K) ? wv[lane * KTOP + j] : -INFINITY;
+        li[j] = (lane < NWARP && j < K) ? wi[lane * KTOP + j] : 0x7fffffff;
+      }
+      __syncwarp();
+      warp_merge_lists(lv, li, K, wv, wi);  // (lane 0 overwrites warp 0's entries: every lane has read them)
+      __syncwarp();
+      // (the old rows' scores were staged above, before the CTA barriers)
+      if (lane < K) {
+        const int fi = wi[lane] == 0x7fffffff ? 0 : wi[lane];
+        a.score[u * K + lane] = wv[lane];
+        a.parent[u * K + lane] = (long long)u * K + fi / V;
+        a.token[u * K + lane] = fi % V;
+      }
     }
     csync();
+    event(cx, 77);
   }
 }
 
 // Bytes of the select stage's shared memory.
 __host__ __device__ constexpr size_t select_smem(int K, int P) {
-  return sizeof(float) * (3 * KTOP + 2 * NTHR + KTOP) + (size_t)K * (P * K + K) * 8;
+  return sizeof(float) * (4 * KTOP + 2 * NWARP * KTOP + 2 * (size_t)K * P + 2 * (size_t)K * P * K);
 }
 
-// Cache reorder (BeamSession._select: buf.index_select(1, parent), runtime.py:1412-1413) in one stage, in place:
-// row r's slots 0 .. offset + S - 1 become its parent's, for the rows whose parent is another row. A copy at
-// (layer, head, position, 16-byte piece) reads and writes only that piece of the rows, so the work is cut into
-// items of E consecutive pieces of one (layer, head) -- E the largest power of two with 2 N E <= 512 -- and a
-// warp moves an item alone: every row's K and V pieces into registers (at most 16 per lane), __syncwarp, then
-// the changed rows' stores. No CTA barrier, no staging copy.
+// Cache reorder (BeamSession._select: buf.index_select(1, parent), runtime.py:1412-1413) in one stage, in place,
+// by bulk copies: row r's slots 0 .. offset(parent) + S - 1 become its parent's, for the rows whose parent is
+// another row (the slots past that are written by later calls before any call reads them). An item is (layer,
+// head, block of PB positions); a run is a changed row's keys or values in it. Thread i < 2 x (changed rows) owns
+// run i of every item: it copies the parent's run into its part of a shared-memory buffer and arrives on the
+// buffer's barrier (expecting its bytes); once the barrier completes -- every run of the item has landed -- it
+// copies its part into the row's slots. So an item's reads all land before any of its writes, and items are
+// disjoint: the copy is in place. Two buffers: an item's loads overlap the previous item's stores (a thread
+// reuses its part of a buffer after its own stores from there have read it). The stage's free shared memory --
+// the ring, idle after the output stage, and the work area -- holds the buffers; PB is as large as they allow.
 __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, uint8_t* work) {
-  const int N = pd.R, H = pd.H, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* spar = reinterpret_cast<int*>(work);  // [N] the row's parent, -1 where the row keeps its own slots
+  const int N = pd.R, H = pd.H, S = pd.S;
+  uint8_t* area = work - (pd.off_work - pd.off_ring);
+  const size_t avail = (size_t)(pd.off_work - pd.off_ring) + (size_t)pd.work_bytes;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(area);  // [2] one per buffer
+  int* info = reinterpret_cast<int*>(area + 16);      // [3] changed rows, longest parent length, PB
+  int* spar = info + 4;                               // [N] the row's parent, -1 where it keeps its slots
+  int* chg = spar + N;                                // [N] the changed rows
+  const size_t hdr = (32 + (size_t)8 * N + 127) & ~(size_t)127;
   for (int r = threadIdx.x; r < N; r += NTHR) {
     const long long p = __ldcg(reinterpret_cast<const long long*>(a.parent) + r);
     spar[r] = (p == r || p < 0 || p >= N) ? -1 : (int)p;
   }
-  int maxlen = 0;
-  for (int r = 0; r < N; ++r) maxlen = max(maxlen, cx.offs[r] + pd.S);
   csync();
-  int lg = 0;  // E = 1 << lg pieces per item
-  while ((2 * N) << (lg + 1) <= 512) ++lg;
-  const int E = 1 << lg;
-  const int per_lh = (maxlen * (DK / 8) + E - 1) >> lg;  // items per (layer, head)
-  const int nitems = pd.L * H * per_lh;
-  const long long row = (long long)pd.C * DK / 8;  // 16-byte pieces of one (layer, row, head) cache row
-  const int nslot = (2 * N) << lg;                   // [row][K | V][piece]
-  const uint4* k4 = reinterpret_cast<const uint4*>(a.kc);
-  const uint4* v4 = reinterpret_cast<const uint4*>(a.vc);
-  constexpr int J = 16;
-  for (int it = c * NWARP + warp; it < nitems; it += pd.P * NWARP) {
-    const int lh = it / per_lh, e0 = (it - lh * per_lh) << lg, l = lh / H, h = lh - l * H;
-    const long long lbase = (long long)l * N * H + h;  // (layer l, row 0, head h) in rows of `row` pieces
-    long long src[J], dst[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      src[j] = -1;
-      const int s = lane + 32 * j;
-      if (s >= nslot) continue;
-      const int rkv = s >> lg, r = rkv >> 1, piece = e0 + (s & (E - 1));
-      const int par = spar[r];
-      if (par < 0 || (piece >> 3) >= cx.offs[par] + pd.S) continue;
-      src[j] = (lbase + (long long)par * H) * row + piece;
-      dst[j] = (lbase + (long long)r * H) * row + piece;
-      if (rkv & 1) {  // (V: encoded negative)
-        src[j] = -2 - src[j];
-        dst[j] = -2 - dst[j];
+  const size_t bufsz = ((avail - hdr) / 2) & ~(size_t)127;
+  if (threadIdx.x == 0) {
+    int nch = 0, maxlen = 0;
+    for (int r = 0; r < N; ++r)
+      if (spar[r] >= 0) {
+        chg[nch++] = r;
+        maxlen = max(maxlen, cx.offs[spar[r]] + S);
+      }
+    info[0] = nch;
+    info[1] = maxlen;
+    info[2] = nch ? (int)min((size_t)maxlen, bufsz / ((size_t)nch * 2 * DK * 2)) : 0;
+    if (nch > 0) {
+      mbar_init(&bar[0], 2 * nch);
+      mbar_init(&bar[1], 2 * nch);
+      fence_barrier_init();
+    }
+    event(cx, 78);
+  }
+  csync();
+  const int nch = info[0], maxlen = info[1], PB = info[2];
+  const int i = threadIdx.x;
+  if (nch > 0 && PB > 0 && i < 2 * nch) {
+    const int r = chg[i >> 1], par = spar[r], lp = cx.offs[par] + S;
+    __half* cache = (i & 1) ? a.vc : a.kc;
+    const uint64_t pol = policy_evict_first();
+    const int nblk = (maxlen + PB - 1) / PB, nitems = pd.L * H * nblk;
+    const size_t part = (size_t)i * PB * DK * 2;  // this thread's part of a buffer
+    uint8_t* const buf0 = area + hdr + part;
+    uint8_t* const buf1 = area + hdr + bufsz + part;
+    const long long rowh = (long long)pd.C * DK;  // halves of one (layer, row, head) cache row
+    // item it: its run's bytes (0: nothing of this row in the block) and its source / destination offsets
+    auto run_of = [&](int it, long long& src, long long& dst) -> uint32_t {
+      const int lh = it / nblk, p0 = (it - lh * nblk) * PB, l = lh / H, h = lh - l * H;
+      const int n = min(p0 + PB, lp) - p0;
+      src = (((long long)l * N + par) * H + h) * rowh + (long long)p0 * DK;
+      dst = (((long long)l * N + r) * H + h) * rowh + (long long)p0 * DK;
+      return n > 0 ? (uint32_t)n * DK * 2 : 0u;
+    };
+    auto load = [&](int it, uint8_t* buf, uint64_t* b) {
+      long long src, dst;
+      const uint32_t bytes = run_of(it, src, dst);
+      if (bytes) {
+        mbar_arrive_expect_tx(b, bytes);
+        bulk_g2s(buf, cache + src, bytes, b, pol);
+      } else {
+        mbar_arrive(b);
+      }
+    };
+    uint32_t ph0 = 0u, ph1 = 0u;
+    if (c < nitems) load(c, buf0, &bar[0]);
+    int k = 0;
+    for (int it = c; it < nitems; it += pd.P, ++k) {
+      const bool odd = k & 1;
+      const int nit = it + pd.P;
+      if (nit < nitems) {
+        bulk_wait_read_all();  // this thread's stores from the other buffer (the item before) have read it
+        load(nit, odd ? buf0 : buf1, odd ? &bar[0] : &bar[1]);
+      }
+      if (!mbar_wait(odd ? &bar[1] : &bar[0], odd ? ph1 : ph0, pd.max_spin)) {
+        atomicExch(pd.err, E_ERR_TIMEOUT);
+        break;
+      }
+      if (odd) ph1 ^= 1u;
+      else ph0 ^= 1u;
+      long long src, dst;
+      const uint32_t bytes = run_of(it, src, dst);
+      if (bytes) {
+        fence_proxy_async_cta();
+        bulk_s2g(cache + dst, odd ? buf1 : buf0, bytes);
+        bulk_commit();
       }
     }
-    uint4 v[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j)
-      if (src[j] != -1) v[j] = src[j] >= 0 ? __ldcg(k4 + src[j]) : __ldcg(v4 + (-2 - src[j]));
-    __syncwarp();  // every read of the item's pieces is done before any of them is overwritten
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      if (src[j] == -1) continue;
-      if (dst[j] >= 0) reinterpret_cast<uint4*>(a.kc)[dst[j]] = v[j];
-      else reinterpret_cast<uint4*>(a.vc)[-2 - dst[j]] = v[j];
-    }
-    __syncwarp();
+    bulk_wait_all();
   }
+  event(cx, 79);
+  csync();
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
@@ -1807,7 +1891,7 @@ __global__ void __launch_bounds__(BLOCK, 1)
         if (pd.G * pd.S == 1) cross_attn_stage<1>(pd, a, ring, layer, c, work, fr);
         else cross_attn_stage<MAXQ>(pd, a, ring, layer, c, work, fr);
         break;
-      case K_SELECT: select_stage(pd, a, c, work); break;
+      case K_SELECT: select_stage(pd, a, cx, c, work); break;
       case K_REORDER: reorder_stage(pd, a, cx, c, work); break;
       default: gemm_stage<NT>(pd, a, ring, cx, fr, k, layer, c, work, os); break;
     }
@@ -2096,7 +2180,8 @@ KernelFn kernel_for(int NT) {
 // One instantiation per (token tiles, bound on the queries of an attention unit, beam): the per-query state
 // of the attention code lives in registers, so a tighter bound leaves more registers to the rest.
 KernelFn cl_kernel_for(int NT, int Qmax, bool beam, bool wide) {
-  if (beam) return NT == 1 ? decoder_cl_kernel<1, 8, true, false> : decoder_cl_kernel<2, 8, true, false>;  // beam <= 8
+  if (beam && wide) return NT == 1 ? decoder_cl_kernel<1, 1, true, true> : decoder_cl_kernel<2, 1, true, true>;
+  if (beam) return NT == 1 ? decoder_cl_kernel<1, 1, true, false> : decoder_cl_kernel<2, 1, true, false>;
   if (Qmax == 1 && wide) return NT == 1 ? decoder_cl_kernel<1, 1, false, true> : decoder_cl_kernel<2, 1, false, true>;
   if (Qmax == 1) return NT == 1 ? decoder_cl_kernel<1, 1, false, false> : decoder_cl_kernel<2, 1, false, false>;
   if (Qmax <= 8) return NT == 1 ? decoder_cl_kernel<1, 8, false, false> : decoder_cl_kernel<2, 8, false, false>;
@@ -2273,7 +2358,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   // row groups so that heads x row groups <= clusters; the FFN split over the largest count of clusters that
   // divides F / 64 and keeps a cluster's hidden fragments within the exchange buffer.
   if (allow_cl && (!beam || pd.Qmax > 1) && M <= 16 && pd.Qmax <= CLQ && d.D % 64 == 0 && d.F % 64 == 0) {
-    KernelFn kf = cl_kernel_for(pd.NT, pd.Qmax, beam > 0, false);
+    KernelFn kf = cl_kernel_for(pd.NT, beam ? 1 : pd.Qmax, beam > 0, false);
     CUDA_TRY(cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)prop0.sharedMemPerBlockOptin));
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[1];
@@ -2298,8 +2383,18 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
       pd.RG = std::max(1, std::min(ncl / d.H, U));
       pd.NCL3 = ncl3;
       pd.F3 = d.F / ncl3;
+      if (beam) {
+        // a beam call's hypotheses attend as one-query groups of one row each (the one-query attention code,
+        // lighter on registers than the kernel for units of several queries); the `beam` groups of an
+        // utterance read its one copy of cross K/V (pd.Us copies in the caller's buffers, as before)
+        pd.G = 1;
+        pd.U = R;
+        pd.kvg = beam;
+        pd.Qmax = 1;
+        pd.RG = std::max(1, std::min(ncl / d.H, R));
+      }
       // one-query calls whose cross-attention units reach 256 frames: the kernel with wide attention steps
-      const int ngm = (U + pd.RG - 1) / pd.RG, parts = ngm >= CS ? 1 : CS / ngm;
+      const int ngm = (pd.U + pd.RG - 1) / pd.RG, parts = ngm >= CS ? 1 : CS / ngm;
       pd.wide = pd.Qmax == 1 && T / parts >= 256;
     }
   }
@@ -2332,7 +2427,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   } else if ((rc = dev_alloc(p->allocs, &pd.xpart, (size_t)U * d.H * P * Q * XPS, tot))) {
     return bail(rc);
   }
-  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)pd.U * d.H, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);
@@ -2544,7 +2639,7 @@ static int plan_dense(OwsmDec* h, int R, int S, int C, int T, int G, OwsmDecPlan
   if ((rc = dev_alloc(p->allocs, &pd.part, (size_t)std::max(max_tiles_split, 1) * DN_TOK * DN_TILE, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.tcnt, (size_t)max_tiles, tot))) return bail(rc);
   p->tcnt_bytes = (size_t)max_tiles * sizeof(uint32_t);
-  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)U * d.H, tot))) return bail(rc);
+  if ((rc = dev_alloc(p->allocs, &pd.xcnt, (size_t)pd.U * d.H, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.amax, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.aidx, (size_t)P * M, tot))) return bail(rc);
   if ((rc = dev_alloc(p->allocs, &pd.ctr, 8, tot))) return bail(rc);

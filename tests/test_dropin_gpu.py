@@ -119,3 +119,38 @@ def test_session_with_timestamp_rules(ref_model, primer):
         outs.append(out)
     assert not be.failed
     assert outs[0] == outs[1]
+
+
+def _beam_session(runtime, cls, cfg, backend, batch, beam, **kw):
+    return cls(backend, cfg, batch, beam, 64, eos=1, dtype=torch.float16, device=torch.device("cuda"),
+               buckets=[16, 32, 64], **kw)  # fmt: skip
+
+
+@pytest.mark.parametrize("batch,beam", [(1, 4), (3, 5)])
+def test_beam_session_with_fused_step(ref_model, batch, beam):
+    """owsm-trt's BeamSession with each search step as one fused beam_fn launch (decoder call, log-softmax, top-K,
+    parents / tokens, cache reorder; owsm_trt_b200.beam.fused_beam_session) gives the hypotheses of the same
+    session run unfused over MegaBackend (the kernel's step_fn for the decoder call, torch's selection and cache
+    reorder on its logits): the same logits, the same selection. (Against TorchBackend's fp32 search the fp16
+    logits may break near-ties between hypotheses' cumulative scores the other way, which beam search carries on
+    into different hypotheses; the teacher-forced beam test of the 1B decoder counts those near-ties instead.)"""
+    megakernel, runtime, _, _ = _reference()
+    from owsm_trt_b200.beam import fused_beam_session
+    from owsm_trt_b200.decoder import B200Decoder
+
+    cfg, model = ref_model
+    m16 = copy.deepcopy(model).half()
+    m16.frontend.float()
+    kern = B200Decoder(model.decoder, torch.device("cuda"))
+    be = megakernel.MegaBackend(runtime.TorchBackend(m16), kern, max_tokens=64, trial=True)
+    torch.manual_seed(100 + batch)
+    feats = m16.frontend(torch.randn(batch, cfg.num_samples, device="cuda"))
+    primer = torch.tensor([[2, 3, 4]] * batch, device="cuda")
+    fused = fused_beam_session(runtime)
+    outs = []
+    for cls, kw in ((runtime.BeamSession, {}), (fused, {"kernel": kern})):
+        sess = _beam_session(runtime, cls, cfg, be, batch, beam, **kw)
+        sess.encode(feats)
+        outs.append(sess.decode(primer, 24))
+    assert not be.failed
+    assert outs[1] == outs[0], "fused beam step differs from the same kernel's logits with torch's selection"

@@ -1500,86 +1500,59 @@ __device__ void beam_partials(const PlanDev& pd, int c, OutState& os) {
 
 constexpr float LOG_ZERO = -1.0e10f;
 
-// A sorted list of the KTOP best candidates in registers (a beam of K <= KTOP uses its first K): insert (v, i)
-// where it belongs. (Every index is static: a register array indexed by a run-time value would live in local
-// memory.)
-__device__ __forceinline__ void list_insert(float (&lv)[KTOP], int (&li)[KTOP], float v, int i) {
-  if (!beats(v, i, lv[KTOP - 1], li[KTOP - 1])) return;
-#pragma unroll
-  for (int j = KTOP - 1; j > 0; --j) {  // shift down the entries v beats, from the end of the list
-    if (beats(v, i, lv[j - 1], li[j - 1])) {
-      lv[j] = lv[j - 1];
-      li[j] = li[j - 1];
-    } else if (beats(v, i, lv[j], li[j])) {
-      lv[j] = v;
-      li[j] = i;
-    }
-  }
-  if (beats(v, i, lv[0], li[0])) {
-    lv[0] = v;
-    li[0] = i;
-  }
-}
-
-// The warp's K best of its lanes' sorted lists (K rounds: the warp's best head, popped from its lane's list),
-// written by lane 0 to out_v / out_i [K].
-__device__ __forceinline__ void warp_merge_lists(float (&lv)[KTOP], int (&li)[KTOP], int K, float* out_v, int* out_i) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll 1
-  for (int sel = 0; sel < K; ++sel) {
-    float bv = lv[0];
-    int bi = li[0];
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (beats(ov, oi, bv, bi)) bv = ov, bi = oi;
-    }
-    if (lane == 0) out_v[sel] = bv, out_i[sel] = bi;
-    if (li[0] == bi && lv[0] == bv && bi != 0x7fffffff) {  // (flat indices are unique: one lane pops)
-#pragma unroll
-      for (int j = 0; j < KTOP - 1; ++j) lv[j] = lv[j + 1], li[j] = li[j + 1];
-      lv[KTOP - 1] = -INFINITY;
-      li[KTOP - 1] = 0x7fffffff;
-    }
-  }
-}
-
-// BeamSession._select step 1 for utterance u (one CTA): lse per row from the CTAs' partials; candidates
-// score + (logit - lse) from every CTA's per-row top-K (LOG_ZERO for inactive rows), each thread keeping the K
-// best of its candidates in registers; the warps' lists merged by shuffles, then the warps' results by warp 0:
-// top-`beam` by (value desc, flat index asc). The stage runs once per call, so its code is kept short (loops
-// rolled up: a call finds it cold in the instruction cache); loads go first into shared memory.
-// (Out of line: its register lists would otherwise compete with the rest of the kernel's allocation.)
+// BeamSession._select step 1 for utterance u (one CTA). Each CTA of the output stage left, per row, its top-K
+// logits as a sorted list (topv / topi), the row's max and sum of exp (lmax / lsum). The rows' lse come from the
+// partials; a candidate's value is score + (logit - lse) (log_softmax), LOG_ZERO for every id of an inactive row
+// (represented by its first K ids, the ones the order picks among equals). The best K of all lists are the best
+// of their heads, K times: each warp takes lists round-robin (a lane holds the heads of up to SEL_LPL lists) and
+// pops its best head K times (a warp argmax per round), then warp 0 merges the warps' K best the same way:
+// top-`beam` by (value desc, flat index asc). The lists arrive in shared memory by bulk copies (one per CTA of
+// the output stage and array); the stage's code stays short (it runs once per call, from a cold instruction
+// cache).
+// (Out of line: its registers would otherwise compete with the rest of the kernel's allocation.)
+constexpr int SEL_LPL = 8;  // lists per lane: P x K + K <= NTHR x SEL_LPL
 __device__ __noinline__ void select_stage(const PlanDev& pd, const CallArgs& a, const Ctx& cx, int c, uint8_t* work) {
-  const int K = pd.beam, V = pd.V, P = pd.P;
+  const int K = pd.beam, V = pd.V, P = pd.P, M = pd.M;
   const int B = pd.R / K;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* lmx = reinterpret_cast<float*>(work);  // [KTOP] row max of the logits
-  float* lse = lmx + KTOP;                      // [KTOP] log of the row's sum of exp(logit - max)
-  float* rsc = lse + KTOP;                      // [KTOP] the rows' scores (before this step)
-  int* ract = reinterpret_cast<int*>(rsc + KTOP);           // [KTOP] the rows' active flags
-  float* wv = reinterpret_cast<float*>(ract + KTOP);        // [NWARP][KTOP] the warps' best
+  uint64_t* bar = reinterpret_cast<uint64_t*>(work);        // the lists' copies
+  float* lmx = reinterpret_cast<float*>(work + 16);          // [KTOP] row max of the logits
+  float* lse = lmx + KTOP;                                   // [KTOP] log of the row's sum of exp(logit - max)
+  float* rsc = lse + KTOP;                                   // [KTOP] the rows' scores (before this step)
+  int* ract = reinterpret_cast<int*>(rsc + KTOP);            // [KTOP] the rows' active flags
+  float* wv = reinterpret_cast<float*>(ract + KTOP);         // [NWARP][KTOP] the warps' best
   int* wi = reinterpret_cast<int*>(wv + NWARP * KTOP);
-  float* pm = reinterpret_cast<float*>(wi + NWARP * KTOP);  // [K][P] the CTAs' row max, then sum
+  float* pm = reinterpret_cast<float*>(wi + NWARP * KTOP);   // [K][P] the CTAs' row max, then sum
   float* ps = pm + K * P;
-  float* cvv = ps + K * P;                                  // [K][P * K] the CTAs' top-K values, then ids
-  int* cvi = reinterpret_cast<int*>(cvv + K * P * K);
-  const int nc = P * K;  // candidates of an active row
+  float* cvv = reinterpret_cast<float*>(work + ((16 + sizeof(float) * (4 * KTOP + 2 * NWARP * KTOP + 2 * (size_t)K * P) +
+                                                 15) & ~(size_t)15));  // [P][K][KTOP] the CTAs' lists: values
+  int* cvi = reinterpret_cast<int*>(cvv + (size_t)P * K * KTOP);                          // ... then ids
+  const uint32_t run = (uint32_t)K * KTOP * 4;  // bytes of one CTA's lists of the utterance's rows
+  const int nl = P * K + K;                     // lists: (CTA q, row k), then one per inactive row
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_barrier_init();
+  }
+  uint32_t ph = 0;
   for (int u = c; u < B; u += P) {
+    csync();  // (the barrier's initialisation; the previous utterance's reads of the staging areas)
+    if (threadIdx.x == 0) mbar_arrive_expect_tx(bar, 2 * run * (uint32_t)P);
+    csync();
+    for (int i = threadIdx.x; i < 2 * P; i += NTHR) {  // copy i: CTA i / 2's lists, values (even) or ids (odd)
+      const int q = i >> 1;
+      const size_t at = ((size_t)q * M + (size_t)u * K) * KTOP;
+      if (i & 1) bulk_g2s(cvi + (size_t)q * K * KTOP, pd.topi + at, run, bar, policy_evict_first());
+      else bulk_g2s(cvv + (size_t)q * K * KTOP, pd.topv + at, run, bar, policy_evict_first());
+    }
     if (threadIdx.x < K) {
       rsc[threadIdx.x] = a.score[u * K + threadIdx.x];
       ract[threadIdx.x] = a.active[u * K + threadIdx.x] != 0;
     }
+#pragma unroll 4
     for (int i = threadIdx.x; i < K * P; i += NTHR) {
       const int k = i / P, q = i - k * P, r = u * K + k;
-      pm[i] = __ldcg(pd.lmax + (long long)q * pd.M + r);
-      ps[i] = __ldcg(pd.lsum + (long long)q * pd.M + r);
-    }
-    for (int i = threadIdx.x; i < K * nc; i += NTHR) {
-      const int k = i / nc, j = i - k * nc, q = j / K, e = j - q * K, r = u * K + k;
-      cvv[i] = __ldcg(pd.topv + ((long long)q * pd.M + r) * KTOP + e);
-      cvi[i] = __ldcg(pd.topi + ((long long)q * pd.M + r) * KTOP + e);
+      pm[i] = __ldcg(pd.lmax + (long long)q * M + r);
+      ps[i] = __ldcg(pd.lsum + (long long)q * M + r);
     }
     csync();
     for (int k = warp; k < K; k += NWARP) {
@@ -1597,51 +1570,110 @@ __device__ __noinline__ void select_stage(const PlanDev& pd, const CallArgs& a, 
         lse[k] = logf(sm);
       }
     }
+    if (!mbar_wait(bar, ph, pd.max_spin)) atomicExch(pd.err, E_ERR_TIMEOUT);
+    ph ^= 1u;
     csync();
     event(cx, 74);
-    float lv[KTOP];
-    int li[KTOP];
+    // entry e of list l as a candidate (value, flat id); (-inf, INT_MAX) past its end
+    auto entry = [&](int l, int e, float& v, int& id) {
+      v = -INFINITY;
+      id = 0x7fffffff;
+      if (l < 0 || e >= K) return;
+      if (l < P * K) {
+        const int k = l % K;
+        const float x = cvv[(size_t)l * KTOP + e];
+        if (ract[k] && x > -INFINITY) {
+          v = rsc[k] + ((x - lmx[k]) - lse[k]);  // log_softmax = (x - max) - log(sum)
+          id = k * V + cvi[(size_t)l * KTOP + e];
+        }
+      } else {
+        const int k = l - P * K;
+        if (!ract[k]) {
+          v = LOG_ZERO;
+          id = k * V + e;
+        }
+      }
+    };
+    // this thread's lists: l = threadIdx.x + NTHR * j, and their heads
+    int hl[SEL_LPL], he[SEL_LPL];
+    float hv[SEL_LPL];
+    int hid[SEL_LPL];
 #pragma unroll
-    for (int j = 0; j < KTOP; ++j) lv[j] = -INFINITY, li[j] = 0x7fffffff;
+    for (int j = 0; j < SEL_LPL; ++j) {
+      const int l = threadIdx.x + NTHR * j;
+      hl[j] = l < nl ? l : -1;
+      he[j] = 0;
+      entry(hl[j], 0, hv[j], hid[j]);
+    }
 #pragma unroll 1
-    for (int i = threadIdx.x; i < K * (nc + K); i += NTHR) {
-      const int k = i / (nc + K), j = i - k * (nc + K);
-      if (ract[k]) {
-        if (j < nc && cvv[k * nc + j] > -INFINITY)  // log_softmax = (x - max) - log(sum)
-          list_insert(lv, li, rsc[k] + ((cvv[k * nc + j] - lmx[k]) - lse[k]), k * V + cvi[k * nc + j]);
-      } else if (j >= nc) {  // an inactive row: LOG_ZERO candidates (its first K ids stand for all of them)
-        list_insert(lv, li, LOG_ZERO, k * V + (j - nc));
+    for (int sel = 0; sel < K; ++sel) {
+      float bv = -INFINITY;
+      int bi = 0x7fffffff, bj = -1;
+#pragma unroll
+      for (int j = 0; j < SEL_LPL; ++j)
+        if (beats(hv[j], hid[j], bv, bi)) bv = hv[j], bi = hid[j], bj = j;
+      float wv0 = bv;
+      int wi0 = bi;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, wv0, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, wi0, o);
+        if (beats(ov, oi, wv0, wi0)) wv0 = ov, wi0 = oi;
+      }
+      if (lane == 0) wv[warp * KTOP + sel] = wv0, wi[warp * KTOP + sel] = wi0;
+      if (bj >= 0 && bi == wi0 && bi != 0x7fffffff) {  // (flat ids are unique: one lane pops its list)
+#pragma unroll
+        for (int j = 0; j < SEL_LPL; ++j)
+          if (j == bj) {
+            ++he[j];
+            entry(hl[j], he[j], hv[j], hid[j]);
+          }
       }
     }
     event(cx, 75);
-    warp_merge_lists(lv, li, K, wv + warp * KTOP, wi + warp * KTOP);
-    event(cx, 76);
     csync();
-    if (warp == 0) {
+    if (warp == 0) {  // the warps' K best, each sorted: lane w < NWARP walks warp w's list
+      int e = 0;
+      float v = -INFINITY;
+      int id = 0x7fffffff;
+      if (lane < NWARP) v = wv[lane * KTOP], id = wi[lane * KTOP];
+      float outv = -INFINITY;
+      int outi = 0x7fffffff;
+#pragma unroll 1
+      for (int sel = 0; sel < K; ++sel) {
+        float bv = v;
+        int bi = id;
 #pragma unroll
-      for (int j = 0; j < KTOP; ++j) {
-        lv[j] = (lane < NWARP && j < K) ? wv[lane * KTOP + j] : -INFINITY;
-        li[j] = (lane < NWARP && j < K) ? wi[lane * KTOP + j] : 0x7fffffff;
+        for (int o = 16; o; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (beats(ov, oi, bv, bi)) bv = ov, bi = oi;
+        }
+        if (lane == sel) outv = bv, outi = bi;
+        if (lane < NWARP && id == bi && bi != 0x7fffffff) {
+          ++e;
+          v = e < K ? wv[lane * KTOP + e] : -INFINITY;
+          id = e < K ? wi[lane * KTOP + e] : 0x7fffffff;
+        }
       }
-      __syncwarp();
-      warp_merge_lists(lv, li, K, wv, wi);  // (lane 0 overwrites warp 0's entries: every lane has read them)
-      __syncwarp();
       // (the old rows' scores were staged above, before the CTA barriers)
       if (lane < K) {
-        const int fi = wi[lane] == 0x7fffffff ? 0 : wi[lane];
-        a.score[u * K + lane] = wv[lane];
+        const int fi = outi == 0x7fffffff ? 0 : outi;
+        a.score[u * K + lane] = outv;
         a.parent[u * K + lane] = (long long)u * K + fi / V;
         a.token[u * K + lane] = fi % V;
       }
     }
-    csync();
     event(cx, 77);
   }
+  csync();
+  if (threadIdx.x == 0) mbar_inval(bar);  // (the next stage uses this memory for other data)
 }
 
 // Bytes of the select stage's shared memory.
 __host__ __device__ constexpr size_t select_smem(int K, int P) {
-  return sizeof(float) * (4 * KTOP + 2 * NWARP * KTOP + 2 * (size_t)K * P + 2 * (size_t)K * P * K);
+  return ((16 + sizeof(float) * (4 * KTOP + 2 * NWARP * KTOP + 2 * (size_t)K * P) + 15) & ~(size_t)15) +
+         2 * sizeof(float) * (size_t)P * K * KTOP;
 }
 
 // Cache reorder (BeamSession._select: buf.index_select(1, parent), runtime.py:1412-1413) in one stage, in place,
@@ -2326,6 +2358,8 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
   if (M > MAXNT * 8) return fail(OWSM_DEC_ERR_LIMIT, "at most 64 tokens (rows x window) per call");
   if (S > MAXQ || G * S > MAXQ) return fail(OWSM_DEC_ERR_LIMIT, "rows_per_utt x window must be <= 32");
   if (beam) {
+    if ((long long)h->programs * beam + beam > (long long)NTHR * SEL_LPL)
+      return fail(OWSM_DEC_ERR_LIMIT, "beam calls: too many programs for the select stage's lists");
     if (beam < 1 || beam > KTOP || S != 1 || R % beam || G != beam)
       return fail(OWSM_DEC_ERR_LIMIT, "beam calls: S = 1, beam <= 8, rows = batch x beam, rows_per_utt = beam");
   }

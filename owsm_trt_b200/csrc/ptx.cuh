@@ -26,6 +26,10 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 }
 
 // Make the initialised barriers visible to the bulk-copy (async) proxy.
+__device__ __forceinline__ void mbar_inval(uint64_t* bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

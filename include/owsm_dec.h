@@ -124,11 +124,16 @@ int owsm_dec_step_verify(OwsmDecPlan* p, void* stream, const int64_t* inp, int64
  * top-`beam` of beam x V per utterance (ties: lower flat index) ->
  *   score fp32 [R] (overwritten with the new scores), parent int64 [R] (row each slot came from),
  *   token int64 [R]; then self_k / self_v rows are replaced by their parent's rows (slots 0 .. offset+S-1).
- * active uint8 [R]. */
+ * active uint8 [R].
+ * shared int32 [R / beam][beam][beam] or NULL: the caller's record, per utterance, of how many leading cache
+ *   slots each pair of its rows holds in common (the same keys and values). With it only the slots past that
+ *   are copied from a row's parent, and the call updates the record for the next call; set every entry to the
+ *   prompt length when the rows start from the same prompt (and again whenever the caches are rewritten
+ *   otherwise). NULL: every slot 0 .. offset+S-1 is copied, as BeamSession's index_select does. */
 int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride,
                        const int64_t* offset, int64_t off_stride, void* self_k, void* self_v, const void* cross_k,
                        const void* cross_v, const int32_t* enc_len, float* logits, void* new_kv, float* score,
-                       const uint8_t* active, int64_t* parent, int64_t* token);
+                       const uint8_t* active, int64_t* parent, int64_t* token, int32_t* shared);
 
 /* Read and clear the device error word of the handle's calls (synchronises the device).
  * Returns OWSM_DEC_OK, OWSM_DEC_ERR_TIMEOUT (a bounded wait gave up) or OWSM_DEC_ERR_CUDA. */

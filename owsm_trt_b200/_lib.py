@@ -43,7 +43,7 @@ SIGNATURES = {
     "owsm_dec_plan_destroy": (None, [vp]),
     "owsm_dec_step": (i32, [vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32]),
     "owsm_dec_step_verify": (i32, [vp, vp, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]),
-    "owsm_dec_beam_step": (i32, [vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
+    "owsm_dec_beam_step": (i32, [vp, vp, vp, i64, vp, i64, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp]),
     "owsm_dec_get_error": (i32, [vp]),
     "owsm_dec_plan_reset": (i32, [vp]),
     "owsm_dec_plan_info": (i32, [vp, C.POINTER(i32), C.POINTER(i32), C.POINTER(i64)]),

@@ -9,6 +9,9 @@ reference needs no other change (``INTEGRATION.md`` shows where ``transcribe`` w
 the reference's session:
   * the decoder reads each utterance's cross K/V once for its ``beam`` hypotheses (``cross_kb`` / ``cross_vb``),
     so ``encode`` no longer copies them to every hypothesis row;
+  * the session keeps, per utterance, how many leading cache slots each pair of hypotheses holds in common
+    (``shared``: the prompt's after the first selection, then updated by every step), so a hypothesis copies only
+    its parent's slots past that instead of its whole cache;
   * the timestamp rules are not fused: a session with ``rules`` raises ``ValueError`` (use ``BeamSession``).
 The first selection after the prompt (from the prefill logits) is the reference's own eager ``_select``."""
 
@@ -37,12 +40,20 @@ def fused_beam_session(runtime):
             self.parent = torch.zeros(self.rows, dtype=torch.long, device=self.device)
             self.token = torch.zeros(self.rows, dtype=torch.long, device=self.device)
             active = self.active.view(torch.uint8)  # (bool and uint8 share the byte layout)
+            self.shared = torch.zeros(self.batch, self.beam, self.beam, dtype=torch.int32, device=self.device)
             self._fused = {
                 c: self.kernel.beam_fn(self.tok, self.offs, k, v, self.cross_kb, self.cross_vb, self.logits,
-                                       self.new_kv, self.score, active, self.parent, self.token, beam=self.beam)
+                                       self.new_kv, self.score, active, self.parent, self.token, beam=self.beam,
+                                       shared=self.shared)
                 for c, (k, v) in self.caches.items()
             }  # fmt: skip
             super()._capture_all()
+
+        def _select(self, c: int) -> None:
+            # (called eagerly once per decode, on the prompt's logits: BeamSession's own selection) every row of an
+            # utterance then holds the prompt's keys and values, slots 0 .. pos - 1
+            super()._select(c)
+            self.shared.copy_(self.pos.to(torch.int32).expand(self.batch, self.beam, self.beam))
 
         def encode(self, feats: torch.Tensor) -> torch.Tensor:
             return self._encoder(feats, self.cross_kb, self.cross_vb, self.ctc_ids)

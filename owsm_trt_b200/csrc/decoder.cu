@@ -84,6 +84,7 @@ struct PlanDev {
   int* aidx;      // [P][M]
   float* lmax;    // [P][M]
   float* lsum;    // [P][M]
+  int* cstart;    // [R] beam calls: the first cache slot a row takes from its parent (shared prefixes known)
   float* topv;    // [P][M][KTOP]
   int* topi;      // [P][M][KTOP]
   uint32_t* ctr;  // [0] grid barrier, [1] exits, [2] argmax arrivals
@@ -146,6 +147,7 @@ struct CallArgs {
   const uint8_t* active;
   int64_t* parent;
   int64_t* token;
+  int32_t* shared;  // beam calls, NULL or [R / beam][beam][beam]: cache slots each pair of rows holds in common
   int beam_mode;
 };
 
@@ -1657,11 +1659,38 @@ __device__ __noinline__ void select_stage(const PlanDev& pd, const CallArgs& a, 
         }
       }
       // (the old rows' scores were staged above, before the CTA barriers)
+      const int fi = outi == 0x7fffffff ? 0 : outi;
       if (lane < K) {
-        const int fi = outi == 0x7fffffff ? 0 : outi;
         a.score[u * K + lane] = outv;
         a.parent[u * K + lane] = (long long)u * K + fi / V;
         a.token[u * K + lane] = fi % V;
+      }
+      if (a.shared) {
+        // The caller's record of the slots each pair (i, j) of the utterance's rows holds in common (before this
+        // step's write): row i takes its parent's slots from D[i][parent] on (the ones before are the same), and
+        // afterwards two rows hold in common all of a parent's slots when they share it, else what their parents
+        // held in common. (K x K <= 64 entries: lane l holds entries l and l + 32.)
+        int32_t* Dm = a.shared + (size_t)u * K * K;
+        const int pl = lane < K ? fi / V : 0;  // row lane's parent (index in the utterance)
+        const int kk = K * K;
+        const int e0 = lane < kk ? Dm[lane] : 0, e1 = lane + 32 < kk ? Dm[lane + 32] : 0;
+        auto old_at = [&](int idx) {  // entry idx of the old matrix (every lane passes its own idx)
+          const int x0 = __shfl_sync(0xffffffffu, e0, idx & 31), x1 = __shfl_sync(0xffffffffu, e1, idx & 31);
+          return idx < 32 ? x0 : x1;
+        };
+        const int cs = old_at(lane < K ? lane * K + pl : 0);
+        if (lane < K) pd.cstart[u * K + lane] = cs;
+        int nv[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int idx = lane + 32 * h, i = idx < kk ? idx / K : 0, j = idx < kk ? idx % K : 0;
+          const int pi = __shfl_sync(0xffffffffu, pl, i), pj = __shfl_sync(0xffffffffu, pl, j);
+          const int o = old_at(pi * K + pj);
+          nv[h] = pi == pj ? cx.offs[u * K + pi] + pd.S : o;
+        }
+        __syncwarp();  // (every lane's reads of the old matrix are done)
+        if (lane < kk) Dm[lane] = nv[0];
+        if (lane + 32 < kk) Dm[lane + 32] = nv[1];
       }
     }
     event(cx, 77);
@@ -1691,7 +1720,7 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
   uint8_t* area = work - (pd.off_work - pd.off_ring);
   const size_t avail = (size_t)(pd.off_work - pd.off_ring) + (size_t)pd.work_bytes;
   uint64_t* bar = reinterpret_cast<uint64_t*>(area);  // [2] one per buffer
-  int* info = reinterpret_cast<int*>(area + 16);      // [3] changed rows, longest parent length, PB
+  int* info = reinterpret_cast<int*>(area + 16);      // [4] changed rows, longest parent length, PB, first slot
   int* spar = info + 4;                               // [N] the row's parent, -1 where it keeps its slots
   int* chg = spar + N;                                // [N] the changed rows
   const size_t hdr = (32 + (size_t)8 * N + 127) & ~(size_t)127;
@@ -1702,15 +1731,18 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
   csync();
   const size_t bufsz = ((avail - hdr) / 2) & ~(size_t)127;
   if (threadIdx.x == 0) {
-    int nch = 0, maxlen = 0;
+    int nch = 0, maxlen = 0, mincs = 0x7fffffff;
     for (int r = 0; r < N; ++r)
       if (spar[r] >= 0) {
         chg[nch++] = r;
-        maxlen = max(maxlen, cx.offs[spar[r]] + S);
+        const int lp = cx.offs[spar[r]] + S;
+        maxlen = max(maxlen, lp);
+        mincs = min(mincs, a.shared ? min(max(__ldcg(pd.cstart + r), 0), lp) : 0);
       }
     info[0] = nch;
     info[1] = maxlen;
-    info[2] = nch ? (int)min((size_t)maxlen, bufsz / ((size_t)nch * 2 * DK * 2)) : 0;
+    info[2] = nch ? (int)min((size_t)max(maxlen - mincs, 1), bufsz / ((size_t)nch * 2 * DK * 2)) : 0;
+    info[3] = nch ? mincs : 0;
     if (nch > 0) {
       mbar_init(&bar[0], 2 * nch);
       mbar_init(&bar[1], 2 * nch);
@@ -1719,21 +1751,23 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
     event(cx, 78);
   }
   csync();
-  const int nch = info[0], maxlen = info[1], PB = info[2];
+  const int nch = info[0], maxlen = info[1], PB = info[2], s0 = info[3];
   const int i = threadIdx.x;
   if (nch > 0 && PB > 0 && i < 2 * nch) {
     const int r = chg[i >> 1], par = spar[r], lp = cx.offs[par] + S;
+    // the slots before cs are the same in the row and its parent (with the caller's record, else none)
+    const int cs = a.shared ? min(max(__ldcg(pd.cstart + r), 0), lp) : 0;
     __half* cache = (i & 1) ? a.vc : a.kc;
     const uint64_t pol = policy_evict_first();
-    const int nblk = (maxlen + PB - 1) / PB, nitems = pd.L * H * nblk;
+    const int nblk = (maxlen - s0 + PB - 1) / PB, nitems = pd.L * H * nblk;  // blocks of slots from s0 on
     const size_t part = (size_t)i * PB * DK * 2;  // this thread's part of a buffer
     uint8_t* const buf0 = area + hdr + part;
     uint8_t* const buf1 = area + hdr + bufsz + part;
     const long long rowh = (long long)pd.C * DK;  // halves of one (layer, row, head) cache row
     // item it: its run's bytes (0: nothing of this row in the block) and its source / destination offsets
     auto run_of = [&](int it, long long& src, long long& dst) -> uint32_t {
-      const int lh = it / nblk, p0 = (it - lh * nblk) * PB, l = lh / H, h = lh - l * H;
-      const int n = min(p0 + PB, lp) - p0;
+      const int lh = it / nblk, b0 = s0 + (it - lh * nblk) * PB, l = lh / H, h = lh - l * H;
+      const int p0 = max(b0, cs), n = min(b0 + PB, lp) - p0;
       src = (((long long)l * N + par) * H + h) * rowh + (long long)p0 * DK;
       dst = (((long long)l * N + r) * H + h) * rowh + (long long)p0 * DK;
       return n > 0 ? (uint32_t)n * DK * 2 : 0u;
@@ -2470,6 +2504,7 @@ static int plan_impl(OwsmDec* h, int R, int S, int C, int T, int rows_per_utt, i
     if ((rc = dev_alloc(p->allocs, &pd.lsum, (size_t)P * M, tot))) return bail(rc);
     if ((rc = dev_alloc(p->allocs, &pd.topv, (size_t)P * M * KTOP, tot))) return bail(rc);
     if ((rc = dev_alloc(p->allocs, &pd.topi, (size_t)P * M * KTOP, tot))) return bail(rc);
+    if ((rc = dev_alloc(p->allocs, &pd.cstart, (size_t)R, tot))) return bail(rc);
   }
   // shared memory: barriers | utterance prefix sums + flag | block lists | row offsets | output-stage state |
   // ring | work area
@@ -2893,7 +2928,7 @@ int owsm_dec_step_verify(OwsmDecPlan* p, void* stream, const int64_t* inp, int64
 int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int64_t tok_stride,
                        const int64_t* offset, int64_t off_stride, void* self_k, void* self_v, const void* cross_k,
                        const void* cross_v, const int32_t* enc_len, float* logits, void* new_kv, float* score,
-                       const uint8_t* active, int64_t* parent, int64_t* token) {
+                       const uint8_t* active, int64_t* parent, int64_t* token, int32_t* shared) {
   int rc = check_common(p, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv);
   if (rc) return rc;
   if (!p->beam) return fail(OWSM_DEC_ERR_ARG, "the plan was not made for beam calls");
@@ -2906,6 +2941,7 @@ int owsm_dec_beam_step(OwsmDecPlan* p, void* stream, const int64_t* tokens, int6
   a.enc_len = enc_len;
   a.logits = logits; a.new_kv = reinterpret_cast<__half*>(new_kv);
   a.score = score; a.active = active; a.parent = parent; a.token = token;
+  a.shared = shared;
   a.beam_mode = 1;
   return launch(p, stream, a);
 }

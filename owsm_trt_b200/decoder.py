@@ -380,10 +380,13 @@ class B200Decoder:
         return run
 
     def beam_fn(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent,
-                token, *, beam: int, enc_len=None):  # fmt: skip
+                token, *, beam: int, enc_len=None, shared=None):  # fmt: skip
         """One beam step (S = 1, rows = batch x beam, utterance-major, cross K/V one per utterance): the decoder
         call, then BeamSession._select step 1 (runtime.py:1399-1411) -- ``score`` [R] fp32 is replaced by the new
-        scores, ``parent`` / ``token`` [R] int64 written -- and the cache rows replaced by their parents'."""
+        scores, ``parent`` / ``token`` [R] int64 written -- and the cache rows replaced by their parents'.
+        ``shared`` (int32 [R / beam, beam, beam], optional): per utterance, how many leading cache slots each pair
+        of its rows holds in common; with it a row copies only its parent's slots past that (the call keeps the
+        record up to date). Fill it with the prompt length when the rows start from the same prompt."""
         R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, beam)
         if S != 1:
             raise ValueError("beam steps feed one token per row")
@@ -391,11 +394,14 @@ class B200Decoder:
                             ("parent", parent, torch.int64), ("token", token, torch.int64)):  # fmt: skip
             if t.dtype != dt or t.shape != (R,) or not t.is_contiguous():
                 raise TypeError(f"{name} must be contiguous {dt} [R]")
+        if shared is not None and (shared.dtype != torch.int32 or shared.shape != (R // beam, beam, beam)
+                                   or not shared.is_contiguous() or shared.device != self.device):  # fmt: skip
+            raise TypeError("shared must be contiguous int32 [R / beam, beam, beam] on the kernel's device")
         plan = self._plan(R, S, Cc, T, beam, beam)
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         args = (ptr(tokens), tokens.stride(0), ptr(offset), offset.stride(0), ptr(self_k), ptr(self_v), ptr(cross_k),
                 ptr(cross_v), ptr(enc_len), ptr(logits), ptr(new_kv), ptr(score), ptr(active), ptr(parent),
-                ptr(token))  # fmt: skip
+                ptr(token), ptr(shared))  # fmt: skip
         fn = _lib.lib().owsm_dec_beam_step
         dev = self.device
 
@@ -405,5 +411,6 @@ class B200Decoder:
         run.writes_cache = True
         run.plan = plan
         run.beam = True
-        run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent, token)
+        run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent, token,
+                       shared)  # fmt: skip
         return run

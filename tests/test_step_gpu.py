@@ -436,3 +436,54 @@ def test_medium_row_counts_plan_and_run(R, S):
     assert bool(torch.isfinite(logits).all())
     assert torch.equal(pred.cpu(), ref.argmax_first(logits.cpu()))
     _check_cache(kc, vc, kc2, vc2, new_kv, offset)
+
+
+@pytest.mark.parametrize("path", [0, 1])
+def test_beam_shared_prefix_matches_full_reorder(kern, path):
+    """Eight consecutive fused beam steps with the record of common cache slots (`shared`: a row copies only its
+    parent's slots past what the two hold in common) against the same steps copying every slot: identical
+    selections and scores, and identical caches over the written slots, step after step; on the cluster kernel
+    (path 0) and the grid-stage kernel (path 1)."""
+    kern.set_path(path)
+    try:
+        _shared_prefix_case(kern)
+    finally:
+        kern.set_path(0)
+
+
+def _shared_prefix_case(kern):
+    d = TEST_CFG
+    B, K, C, T, P0 = 2, 4, 32, 37, 6
+    N = B * K
+    g = torch.Generator().manual_seed(33)
+    # the rows of an utterance start from the same prompt: equal keys / values in slots 0 .. P0 - 1
+    kc = torch.randn(d.L, B, d.H, C, d.dk, generator=g).half().repeat_interleave(K, dim=1)
+    vc = torch.randn(d.L, B, d.H, C, d.dk, generator=g).half().repeat_interleave(K, dim=1)
+    ck = torch.randn(d.L, B, d.H, T, d.dk, generator=g).half().to(DEV)
+    cv = torch.randn(d.L, B, d.H, T, d.dk, generator=g).half().to(DEV)
+    tok0 = torch.randint(0, d.V, (N, 1), generator=g)
+    states = []
+    for use_shared in (False, True):
+        st = {"kc": kc.clone().to(DEV), "vc": vc.clone().to(DEV), "tok": tok0.clone().to(DEV),
+              "off": torch.full((N,), P0, dtype=torch.long, device=DEV), "score": torch.zeros(N, device=DEV),
+              "active": torch.ones(N, dtype=torch.uint8, device=DEV), "parent": torch.zeros(N, dtype=torch.long, device=DEV),
+              "logits": torch.zeros(N, 1, d.V, device=DEV),
+              "new_kv": torch.zeros(d.L, 2, N, d.H, 1, d.dk, device=DEV, dtype=torch.float16),
+              "shared": torch.full((B, K, K), P0, dtype=torch.int32, device=DEV) if use_shared else None}  # fmt: skip
+        st["token"] = st["tok"][:, 0]
+        st["run"] = kern.beam_fn(st["tok"], st["off"], st["kc"], st["vc"], ck, cv, st["logits"], st["new_kv"],
+                                 st["score"], st["active"], st["parent"], st["token"], beam=K, shared=st["shared"])  # fmt: skip
+        states.append(st)
+    for step in range(8):
+        for st in states:
+            st["run"]()
+        torch.cuda.synchronize()
+        kern.check()
+        a, b = states
+        assert torch.equal(a["parent"], b["parent"]) and torch.equal(a["token"], b["token"]), step
+        assert torch.equal(a["score"], b["score"]), step
+        n = P0 + step + 1  # slots written so far
+        assert torch.equal(a["kc"][..., :n, :], b["kc"][..., :n, :]), step
+        assert torch.equal(a["vc"][..., :n, :], b["vc"][..., :n, :]), step
+        for st in states:
+            st["off"] += 1

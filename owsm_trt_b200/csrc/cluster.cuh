@@ -994,6 +994,22 @@ __device__ void cl_out_stage(const PlanDev& pd, const CallArgs& a, Ring& ring, c
   csync();
 }
 
+// (y, n) into a list of KTOP (value, id) in registers, sorted best first by beats(), if it beats the last
+// entry: it takes the place of the first entry it beats and the entries from there on move down one place
+// (the same list as inserting by shifting; the comparisons are independent of one another).
+__device__ __forceinline__ void list_push(float (&v)[KTOP], int (&id)[KTOP], float y, int n) {
+  bool b[KTOP];
+#pragma unroll
+  for (int e = 0; e < KTOP; ++e) b[e] = beats(y, n, v[e], id[e]);
+#pragma unroll
+  for (int e = KTOP - 1; e >= 0; --e)
+    if (b[e]) {
+      const bool sh = e > 0 && b[e - 1];
+      v[e] = sh ? v[e - 1] : y;
+      id[e] = sh ? id[e - 1] : n;
+    }
+}
+
 // The output stage of a beam call: final LayerNorm, this CTA's vocab blocks, logits out, and per token the
 // running max / sum of exp (log-softmax partials) and top-K over this CTA's ids, first per warp (a 16-row
 // tile at a time, as the grid kernel does), then merged over the warps into os.rmax / rsum / topv / topi.
@@ -1109,22 +1125,28 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
     }
     os.rmax[m] = mx;
     os.rsum[m] = sm;
+    // the token's list in registers: each warp's entries go in with independent comparisons, no chain of
+    // dependent shared-memory loads and stores per entry
     float* tv = os.topv + m * KTOP;
     int* ti = os.topi + m * KTOP;
-    for (int w = 0; w < NWARP; ++w)
+    float v[KTOP];
+    int id[KTOP];
+#pragma unroll
+    for (int e = 0; e < KTOP; ++e) v[e] = tv[e], id[e] = ti[e];
+#pragma unroll 1
+    for (int w = 0; w < NWARP; ++w) {
+      float wv[KTOP];
+      int wi[KTOP];
+#pragma unroll
       for (int e = 0; e < KTOP; ++e) {
-        const float y = os.wtopv[((size_t)w * M + m) * KTOP + e];
-        const int n = os.wtopi[((size_t)w * M + m) * KTOP + e];
-        if (!(y > tv[KTOP - 1] || (y == tv[KTOP - 1] && n < ti[KTOP - 1]))) continue;
-        int jj = KTOP - 1;
-        while (jj > 0 && (y > tv[jj - 1] || (y == tv[jj - 1] && n < ti[jj - 1]))) {
-          tv[jj] = tv[jj - 1];
-          ti[jj] = ti[jj - 1];
-          --jj;
-        }
-        tv[jj] = y;
-        ti[jj] = n;
+        wv[e] = os.wtopv[((size_t)w * M + m) * KTOP + e];
+        wi[e] = os.wtopi[((size_t)w * M + m) * KTOP + e];
       }
+#pragma unroll
+      for (int e = 0; e < KTOP; ++e) list_push(v, id, wv[e], wi[e]);
+    }
+#pragma unroll
+    for (int e = 0; e < KTOP; ++e) tv[e] = v[e], ti[e] = id[e];
   }
   csync();
 }

@@ -1035,12 +1035,14 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
   const int b0 = cx.so[G_OUT];
   block_chunks<NT>(ring, cx.so[G_OUT + 1] - b0, pd.D / 16, smem_u32(bbuf),
                    [&](int j, const float (&acc)[NT][4], const float (&bia)[2]) {
-                     const int rb = cx.sb[b0 + j];
+                     const int rb = cx.sb[b0 + j], n0 = rb * 16 + g, n1 = n0 + 8;
+                     float y0s[2 * NT], y1s[2 * NT];
+                     unsigned need = 0;  // bit k: token slot k = 2 nt + s2 has values for the list
 #pragma unroll
                      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                        for (int s2 = 0; s2 < 2; ++s2) {
-                         const int m = nt * 8 + 2 * t + s2, n0 = rb * 16 + g, n1 = n0 + 8;
+                         const int m = nt * 8 + 2 * t + s2;
                          float y0 = acc[nt][s2] + bia[0], y1 = acc[nt][2 + s2] + bia[1];
                          if (m < M) {
                            if (n0 < V) a.logits[(long long)m * V + n0] = y0;
@@ -1060,32 +1062,49 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
                          const float bv = __shfl_sync(0xffffffffu, lv[nt][s2], (K - 1) * 4 + t);
                          const int bi = __shfl_sync(0xffffffffu, li[nt][s2], (K - 1) * 4 + t);
                          const bool cand = m < M && (beats(y0, n0, bv, bi) || beats(y1, n1, bv, bi));
-                         if (!__any_sync(0xffffffffu, cand)) continue;
-                         // merge: the rank of each of the lane's 3 elements among the token's 24 (8 lanes x
-                         // {list entry, y0, y1}); the element of rank q < KTOP becomes entry q (lane q)
-                         const float ev[3] = {lv[nt][s2], y0, y1};
-                         const int ei[3] = {li[nt][s2], n0, n1};
-                         int rk[3] = {0, 0, 0};
-#pragma unroll
-                         for (int o = 0; o < 8; ++o) {
-                           const int src = o * 4 + t;
-#pragma unroll
-                           for (int q = 0; q < 3; ++q) {
-                             const float ov = __shfl_sync(0xffffffffu, ev[q], src);
-                             const int oi = __shfl_sync(0xffffffffu, ei[q], src);
-#pragma unroll
-                             for (int e = 0; e < 3; ++e) rk[e] += beats(ov, oi, ev[e], ei[e]) ? 1 : 0;
-                           }
-                         }
-                         float* tv = os.wtopv + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
-                         int* ti = os.wtopi + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
-#pragma unroll
-                         for (int e = 0; e < 3; ++e)
-                           if (m < M && rk[e] < KTOP) tv[rk[e]] = ev[e], ti[rk[e]] = ei[e];
-                         __syncwarp();
-                         if (m < M) lv[nt][s2] = tv[g], li[nt][s2] = ti[g];
-                         __syncwarp();
+                         if (__any_sync(0xffffffffu, cand)) need |= 1u << (2 * nt + s2);
+                         y0s[2 * nt + s2] = y0;
+                         y1s[2 * nt + s2] = y1;
                        }
+                     // the merges, one copy of the code for all slots (it runs once per call and SM, so its
+                     // size, not only its instruction count, sets its time): the slot's values are moved in and
+                     // out by predicated moves
+#pragma unroll 1
+                     for (int k = 0; k < 2 * NT; ++k) {
+                       if (!((need >> k) & 1u)) continue;
+                       const int m = (k >> 1) * 8 + 2 * t + (k & 1);
+                       float ev[3] = {0.f, 0.f, 0.f};
+                       int ei[3] = {0, n0, n1};
+#pragma unroll
+                       for (int kk = 0; kk < 2 * NT; ++kk)
+                         if (kk == k) ev[0] = lv[kk >> 1][kk & 1], ei[0] = li[kk >> 1][kk & 1], ev[1] = y0s[kk], ev[2] = y1s[kk];
+                       // merge: the rank of each of the lane's 3 elements among the token's 24 (8 lanes x
+                       // {list entry, y0, y1}); the element of rank q < KTOP becomes entry q (lane q)
+                       int rk[3] = {0, 0, 0};
+#pragma unroll
+                       for (int o = 0; o < 8; ++o) {
+                         const int src = o * 4 + t;
+#pragma unroll
+                         for (int q = 0; q < 3; ++q) {
+                           const float ov = __shfl_sync(0xffffffffu, ev[q], src);
+                           const int oi = __shfl_sync(0xffffffffu, ei[q], src);
+#pragma unroll
+                           for (int e = 0; e < 3; ++e) rk[e] += beats(ov, oi, ev[e], ei[e]) ? 1 : 0;
+                         }
+                       }
+                       float* tv = os.wtopv + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
+                       int* ti = os.wtopi + ((size_t)warp * M + (m < M ? m : 0)) * KTOP;
+#pragma unroll
+                       for (int e = 0; e < 3; ++e)
+                         if (m < M && rk[e] < KTOP) tv[rk[e]] = ev[e], ti[rk[e]] = ei[e];
+                       __syncwarp();
+                       const float nv = m < M ? tv[g] : 0.f;
+                       const int ni = m < M ? ti[g] : 0;
+                       __syncwarp();
+#pragma unroll
+                       for (int kk = 0; kk < 2 * NT; ++kk)
+                         if (kk == k && m < M) lv[kk >> 1][kk & 1] = nv, li[kk >> 1][kk & 1] = ni;
+                     }
                    });
   // the 8 lanes of a token (g = 0 .. 7) combine their partials; the warp's partial per token -> os.wrmax / wrsum;
   // its list -> os.wtopv / wtopi (entry g from lane g)
@@ -1134,16 +1153,9 @@ __device__ void cl_out_stage_beam(const PlanDev& pd, const CallArgs& a, Ring& ri
 #pragma unroll
     for (int e = 0; e < KTOP; ++e) v[e] = tv[e], id[e] = ti[e];
 #pragma unroll 1
-    for (int w = 0; w < NWARP; ++w) {
-      float wv[KTOP];
-      int wi[KTOP];
-#pragma unroll
-      for (int e = 0; e < KTOP; ++e) {
-        wv[e] = os.wtopv[((size_t)w * M + m) * KTOP + e];
-        wi[e] = os.wtopi[((size_t)w * M + m) * KTOP + e];
-      }
-#pragma unroll
-      for (int e = 0; e < KTOP; ++e) list_push(v, id, wv[e], wi[e]);
+    for (int i = 0; i < NWARP * KTOP; ++i) {  // entry i % KTOP of warp i / KTOP's list
+      const int w = i / KTOP, e = i - w * KTOP;
+      list_push(v, id, os.wtopv[((size_t)w * M + m) * KTOP + e], os.wtopi[((size_t)w * M + m) * KTOP + e]);
     }
 #pragma unroll
     for (int e = 0; e < KTOP; ++e) tv[e] = v[e], ti[e] = id[e];

@@ -1723,10 +1723,12 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
   int* info = reinterpret_cast<int*>(area + 16);      // [4] changed rows, longest parent length, PB, first slot
   int* spar = info + 4;                               // [N] the row's parent, -1 where it keeps its slots
   int* chg = spar + N;                                // [N] the changed rows
-  const size_t hdr = (32 + (size_t)8 * N + 127) & ~(size_t)127;
+  int* scs = chg + N;                                 // [N] the row's first slot to copy (with the record)
+  const size_t hdr = (32 + (size_t)12 * N + 127) & ~(size_t)127;
   for (int r = threadIdx.x; r < N; r += NTHR) {
     const long long p = __ldcg(reinterpret_cast<const long long*>(a.parent) + r);
     spar[r] = (p == r || p < 0 || p >= N) ? -1 : (int)p;
+    scs[r] = a.shared && spar[r] >= 0 ? min(max(__ldcg(pd.cstart + r), 0), cx.offs[spar[r]] + S) : 0;
   }
   csync();
   const size_t bufsz = ((avail - hdr) / 2) & ~(size_t)127;
@@ -1737,7 +1739,7 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
         chg[nch++] = r;
         const int lp = cx.offs[spar[r]] + S;
         maxlen = max(maxlen, lp);
-        mincs = min(mincs, a.shared ? min(max(__ldcg(pd.cstart + r), 0), lp) : 0);
+        mincs = min(mincs, scs[r]);
       }
     info[0] = nch;
     info[1] = maxlen;
@@ -1756,7 +1758,7 @@ __device__ __noinline__ void reorder_stage(const PlanDev& pd, const CallArgs& a,
   if (nch > 0 && PB > 0 && i < 2 * nch) {
     const int r = chg[i >> 1], par = spar[r], lp = cx.offs[par] + S;
     // the slots before cs are the same in the row and its parent (with the caller's record, else none)
-    const int cs = a.shared ? min(max(__ldcg(pd.cstart + r), 0), lp) : 0;
+    const int cs = scs[r];
     __half* cache = (i & 1) ? a.vc : a.kc;
     const uint64_t pol = policy_evict_first();
     const int nblk = (maxlen - s0 + PB - 1) / PB, nitems = pd.L * H * nblk;  // blocks of slots from s0 on

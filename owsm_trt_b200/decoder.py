@@ -275,14 +275,18 @@ class B200Decoder:
                 raise ValueError(f"all buffers must be on {self.device}")
         return R, S, Cc, T
 
+    def _check_enc_len(self, enc_len, n: int) -> None:
+        """The frames per utterance, if given: contiguous int32 [n] on the kernel's device (the kernel reads n)."""
+        if enc_len is not None and (enc_len.dtype != torch.int32 or enc_len.numel() != n
+                                    or not enc_len.is_contiguous() or enc_len.device != self.device):  # fmt: skip
+            raise ValueError(f"enc_len must be contiguous int32 [R / rows_per_utt] = [{n}] on {self.device}")
+
     def step_fn(self, tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, kind="decode", pred=None,
                 solo=False, notime=None, *, enc_len=None, rows_per_utt: int = 1):  # fmt: skip
         """The call on these buffers (see the module docstring). ``notime`` = (flags [R] bool, first timestamp
         token, last one): the argmax of flagged rows leaves those ids out."""
         G = int(rows_per_utt)
         R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G)
-        plan = self._plan(R, S, Cc, T, G, 0)
-        lib = _lib.lib()
         if pred is not None and (pred.dtype != torch.int64 or pred.shape != (R, S) or not pred.is_contiguous()):
             raise ValueError("pred must be contiguous int64 [R, S]")
         ntm, ft, lt = None, 0, -1
@@ -295,9 +299,9 @@ class B200Decoder:
             if flags.device != self.device:
                 raise ValueError(f"notime flags must be on {self.device}")
             ntm = flags
-        if enc_len is not None:
-            if enc_len.dtype != torch.int32 or enc_len.numel() != R // G:
-                raise ValueError("enc_len must be int32 [R / rows_per_utt]")
+        self._check_enc_len(enc_len, R // G)
+        plan = self._plan(R, S, Cc, T, G, 0)
+        lib = _lib.lib()
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         args = (plan, None, ptr(tokens), tokens.stride(0), ptr(offset), offset.stride(0), ptr(self_k), ptr(self_v),
                 ptr(cross_k), ptr(cross_v), ptr(enc_len), ptr(logits), ptr(new_kv), ptr(pred), ptr(ntm), int(ft),
@@ -356,8 +360,7 @@ class B200Decoder:
         for t in (pred, res, ntm, enc_len):
             if t is not None and t.device != self.device:
                 raise ValueError(f"all buffers must be on {self.device}")
-        if enc_len is not None and (enc_len.dtype != torch.int32 or enc_len.numel() != R // G):
-            raise ValueError("enc_len must be int32 [R / rows_per_utt]")
+        self._check_enc_len(enc_len, R // G)
         plan = self._plan(R, S, Cc, T, G, 0)
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         args = (ptr(inp), inp.stride(0), ptr(self_k), ptr(self_v), ptr(cross_k), ptr(cross_v), ptr(enc_len),
@@ -397,6 +400,7 @@ class B200Decoder:
         if shared is not None and (shared.dtype != torch.int32 or shared.shape != (R // beam, beam, beam)
                                    or not shared.is_contiguous() or shared.device != self.device):  # fmt: skip
             raise TypeError("shared must be contiguous int32 [R / beam, beam, beam] on the kernel's device")
+        self._check_enc_len(enc_len, R // beam)
         plan = self._plan(R, S, Cc, T, beam, beam)
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         args = (ptr(tokens), tokens.stride(0), ptr(offset), offset.stride(0), ptr(self_k), ptr(self_v), ptr(cross_k),
@@ -412,5 +416,5 @@ class B200Decoder:
         run.plan = plan
         run.beam = True
         run.buffers = (tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, score, active, parent, token,
-                       shared)  # fmt: skip
+                       shared, enc_len)  # fmt: skip
         return run

@@ -113,3 +113,38 @@ def test_beam_step_refuses_malformed_buffers(case):
     edit(buf)
     with pytest.raises(err):
         _beam_step(_kernel(), buf, **kw)
+
+
+def _verify(k, R=2, W=3, edit=None, **kw):
+    buf = _greedy(R=R, S=W)
+    buf.update(inp=torch.zeros(R, W + 4, dtype=torch.long), pred=torch.zeros(R, W, dtype=torch.long))
+    if edit is not None:
+        edit(buf)
+    return k.verify_fn(buf["inp"], buf["self_k"], buf["self_v"], buf["cross_k"], buf["cross_v"], buf["logits"],
+                       buf["new_kv"], buf["pred"], **kw)  # fmt: skip
+
+
+def test_well_formed_verify_calls_reach_the_plan():
+    k = _kernel()
+    with pytest.raises(_Reached):
+        _verify(k, res=torch.zeros(2, 2, dtype=torch.long), eos=1)
+    with pytest.raises(_Reached):  # the rules' <eos> serves the accepted-prefix output
+        _verify(k, res=torch.zeros(2, 2, dtype=torch.long), rules=(50, 90, 1), notime=torch.zeros(2, dtype=torch.bool))
+
+
+VERIFY_CASES = {
+    "inp int32": (TypeError, lambda b: b.update(inp=b["inp"].int()), {}),
+    "inp without tokens": (ValueError, lambda b: b.update(inp=b["inp"][:, :4].contiguous()), {}),
+    "pred window": (ValueError, lambda b: b.update(pred=b["pred"][:, :2].contiguous()), {}),
+    "res int32": (ValueError, None, {"res": torch.zeros(2, 2, dtype=torch.int32), "eos": 1}),
+    "res without eos": (ValueError, None, {"res": torch.zeros(2, 2, dtype=torch.long)}),
+    "notime float": (TypeError, None, {"notime": torch.zeros(2)}),
+    "enc_len count": (ValueError, None, {"enc_len": torch.full((1,), 8, dtype=torch.int32)}),
+}
+
+
+@pytest.mark.parametrize("case", sorted(VERIFY_CASES))
+def test_verify_refuses_malformed_buffers(case):
+    err, edit, kw = VERIFY_CASES[case]
+    with pytest.raises(err):
+        _verify(_kernel(), edit=edit, **kw)

@@ -226,6 +226,9 @@ class B200Decoder:
         t_cap = cross_k.shape[3]
         if t_cap < T or cross_v.shape != cross_k.shape:
             raise ValueError("cross_k / cross_v need at least T frames")
+        for t in (enc, cross_k, cross_v):
+            if t.device != self.device:
+                raise ValueError(f"enc, cross_k and cross_v must be on {self.device}")
         h = self._xkv_handle()
         fn, dev = _lib.lib().owsm_xkv_run, self.device
 

@@ -148,3 +148,45 @@ def test_verify_refuses_malformed_buffers(case):
     err, edit, kw = VERIFY_CASES[case]
     with pytest.raises(err):
         _verify(_kernel(), edit=edit, **kw)
+
+
+def _cross_kv(k, U=2, T=8, Tc=8, edit=None):
+    buf = dict(enc=torch.zeros(U, T, D, dtype=torch.float16),
+               cross_k=torch.zeros(L, U, H, Tc, DK, dtype=torch.float16),
+               cross_v=torch.zeros(L, U, H, Tc, DK, dtype=torch.float16))  # fmt: skip
+    if edit is not None:
+        edit(buf)
+
+    def handle():
+        raise _Reached()
+
+    k._xkv_handle = handle
+    return k.cross_kv_fn(buf["enc"], buf["cross_k"], buf["cross_v"])
+
+
+def test_cross_kv_checks():
+    with pytest.raises(_Reached):
+        _cross_kv(_kernel(), Tc=12)  # (cache frames past T are left alone)
+    with pytest.raises(TypeError):
+        _cross_kv(_kernel(), edit=lambda b: b.update(enc=b["enc"].float()))
+    with pytest.raises(TypeError):
+        _cross_kv(_kernel(), edit=lambda b: b.update(enc=b["enc"][..., :128].contiguous()))
+    with pytest.raises(TypeError):
+        _cross_kv(_kernel(), edit=lambda b: b.update(cross_v=b["cross_v"][:, :1].contiguous()))
+    with pytest.raises(ValueError):
+        _cross_kv(_kernel(), Tc=4)
+    k = _kernel()
+    k.device = torch.device("cuda", 0)  # buffers elsewhere than the kernel's device
+    with pytest.raises(ValueError):
+        _cross_kv(k)
+
+
+def test_buffers_elsewhere_than_the_kernels_device_are_refused():
+    k = _kernel()
+    k.device = torch.device("cuda", 0)
+    with pytest.raises(ValueError):
+        _step(k, _greedy())
+    with pytest.raises(ValueError):
+        _beam_step(k, _beam())
+    with pytest.raises(ValueError):
+        _verify(k)

@@ -292,6 +292,8 @@ class B200Decoder:
         R, S, Cc, T = self._validate(tokens, offset, self_k, self_v, cross_k, cross_v, logits, new_kv, G)
         if pred is not None and (pred.dtype != torch.int64 or pred.shape != (R, S) or not pred.is_contiguous()):
             raise ValueError("pred must be contiguous int64 [R, S]")
+        if pred is not None and pred.device != self.device:
+            raise ValueError(f"pred must be on {self.device}")
         ntm, ft, lt = None, 0, -1
         if notime is not None and pred is not None:
             flags, ft, lt = notime
@@ -400,6 +402,8 @@ class B200Decoder:
                             ("parent", parent, torch.int64), ("token", token, torch.int64)):  # fmt: skip
             if t.dtype != dt or t.shape != (R,) or not t.is_contiguous():
                 raise TypeError(f"{name} must be contiguous {dt} [R]")
+            if t.device != self.device:
+                raise ValueError(f"{name} must be on {self.device}")
         if shared is not None and (shared.dtype != torch.int32 or shared.shape != (R // beam, beam, beam)
                                    or not shared.is_contiguous() or shared.device != self.device):  # fmt: skip
             raise TypeError("shared must be contiguous int32 [R / beam, beam, beam] on the kernel's device")

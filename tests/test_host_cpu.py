@@ -190,3 +190,14 @@ def test_buffers_elsewhere_than_the_kernels_device_are_refused():
         _beam_step(k, _beam())
     with pytest.raises(ValueError):
         _verify(k)
+
+
+def test_outputs_on_the_host_are_refused():
+    # an output buffer (one the kernel writes) on another device than the kernel's: here a meta tensor
+    with pytest.raises(ValueError):
+        _step(_kernel(), _greedy(), pred=torch.zeros(2, 1, dtype=torch.long, device="meta"))
+    for name in ("score", "active", "parent", "token"):
+        buf = _beam()
+        buf[name] = buf[name].to("meta")
+        with pytest.raises(ValueError):
+            _beam_step(_kernel(), buf)

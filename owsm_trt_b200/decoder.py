@@ -405,8 +405,10 @@ class B200Decoder:
             if t.device != self.device:
                 raise ValueError(f"{name} must be on {self.device}")
         if shared is not None and (shared.dtype != torch.int32 or shared.shape != (R // beam, beam, beam)
-                                   or not shared.is_contiguous() or shared.device != self.device):  # fmt: skip
-            raise TypeError("shared must be contiguous int32 [R / beam, beam, beam] on the kernel's device")
+                                   or not shared.is_contiguous()):  # fmt: skip
+            raise TypeError("shared must be contiguous int32 [R / beam, beam, beam]")
+        if shared is not None and shared.device != self.device:
+            raise ValueError(f"shared must be on {self.device}")
         self._check_enc_len(enc_len, R // beam)
         plan = self._plan(R, S, Cc, T, beam, beam)
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731

@@ -201,3 +201,5 @@ def test_outputs_on_the_host_are_refused():
         buf[name] = buf[name].to("meta")
         with pytest.raises(ValueError):
             _beam_step(_kernel(), buf)
+    with pytest.raises(ValueError):
+        _beam_step(_kernel(), _beam(), shared=torch.zeros(2, 2, 2, dtype=torch.int32, device="meta"))
